@@ -1,0 +1,378 @@
+#!/usr/bin/env python
+"""Causal self-attention forward + backward throughput on B200.
+
+Workload (per GPU, weak scaling): the attention of kerr-engine's 768-dim model,
+n_embd 768 = 12 heads x head_dim 64, seq_len 256, batch 16 sequences, 4 blocks.
+One step = the 4 blocks' attention forwards followed by their backwards in
+reverse order, exactly the attention work of one training step
+(src/pipeline.rs:177-758).  Each block has its own q|k|v, o, lse, dout and
+dq|dk|dv buffers (~101 MB per block, ~404 MB per step > the 126 MB L2), so no
+L2 flush is needed between steps.  Inputs are seeded synthetic q, k, v ~
+N(0,1)/8 and dout ~ N(0,1) (no checkpoint or corpus is available).
+
+metric: tokens/s = (sequences x seq_len x ranks) / step time (CUDA events,
+max over ranks).  e2e: the same through the host-buffer C ABI calls
+(kattn_fwd_host / kattn_bwd_host), host<->device copies inside the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "kerr-engine_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "causal-attn fwd+bwd tokens/s per GPU at 768-dim T=256; % of roofline; 1/2/4/8 GPU"
+WORKLOAD = {"workload": "kerr-engine 768-dim attention fwd+bwd, 4 blocks per step",
+            "batch_per_gpu": 16, "seq_len": 256, "n_head": 12, "head_dim": 64, "n_embd": 768, "blocks": 4,
+            "causal": True, "layout": "q|k|v column blocks of one [B*T][3C] buffer (ld 3C)",
+            "l2": "no flush: 4 blocks x ~101 MB of distinct buffers per step exceed the 126 MB L2"}
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic(B, T, H, d):
+    """Per-block algorithmic work (causal, no recompute counted):
+    flops: 2 GEMM-like products forward (QK^T, PV) and 4 backward (dV, dP, dQ, dK),
+    each 2*d per (query, key<=query) pair; bytes: forward reads q,k,v and writes
+    o, lse; backward reads q,k,v,o,dout,lse and writes dq,dk,dv."""
+    pairs = T * (T + 1) / 2
+    slabs = B * H
+    return {
+        "fwd_flops": 2 * 2 * d * pairs * slabs,
+        "bwd_flops": 4 * 2 * d * pairs * slabs,
+        "fwd_bytes": 4 * (4 * T * d + T) * slabs,
+        "bwd_bytes": 4 * (8 * T * d + T) * slabs,
+    }
+
+
+class ClockSampler(threading.Thread):
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        super().__init__(daemon=True)
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self._stop = threading.Event()
+        self.max_mhz = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: clocks reported as unavailable
+            self.err = str(e)
+
+    def sample(self):
+        nv = self._nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        for bit, name in self.REASONS.items():
+            if mask & bit:
+                self.reasons.add(name)
+
+    def run(self):
+        if not self.ok:
+            return
+        while not self._stop.is_set():
+            try:
+                self.sample()
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def stop(self):
+        self._stop.set()
+        if self.ok:
+            self.join(timeout=2)
+            if not self.samples:
+                self.sample()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons - {"gpu_idle"}),
+                "samples": len(self.samples)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": FALLBACK_HBM_GBS}, "fallback"
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch of `name` from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == name:
+                return float(parts[1])
+    return None
+
+
+def cpu_sample(n_seq: int, T: int, H: int, d: int, seed: int = 7):
+    """One block's attention fwd+bwd through the oracle over n_seq sequences on
+    n_seq host threads (one thread per sequence, as src/train.rs:241-255)."""
+    import numpy as np
+
+    from oracle import oracle
+
+    C = H * d
+    rng = np.random.default_rng(seed)
+    qkv = (rng.standard_normal((n_seq, T, 3 * C)) / 8).astype(np.float32)
+    dout = rng.standard_normal((n_seq, T, C)).astype(np.float32)
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    t0 = time.perf_counter()
+    o, att, _ = oracle.forward(q, k, v, H, threads=n_seq)
+    oracle.backward(dout, q, k, v, att, H, threads=n_seq)
+    return time.perf_counter() - t0
+
+
+def run_reference(args):
+    """The reference's CPU path (oracle port) on this host's cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    W = WORKLOAD
+    cores = os.cpu_count() or 1
+    n_seq = min(cores, W["batch_per_gpu"])
+    from oracle import oracle
+
+    oracle.build()
+    for _ in range(args.warmup):
+        cpu_sample(n_seq, W["seq_len"], W["n_head"], W["head_dim"])
+    times = [cpu_sample(n_seq, W["seq_len"], W["n_head"], W["head_dim"]) for _ in range(args.steps)]
+    t = sum(times) / len(times)
+    tok_s = n_seq * W["seq_len"] / (W["blocks"] * t)
+    step_ms = 1e3 * t * W["blocks"] * math.ceil(W["batch_per_gpu"] / n_seq)
+    sample = (f"each step: 1 of 4 blocks, {n_seq} of {W['batch_per_gpu']} sequences in parallel "
+              f"(one host thread each); tokens/s scaled to the 4-block step")
+    line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": W, "impl": "reference",
+            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": n_seq, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import kerr_attn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    W = WORKLOAD
+    B, T, H, d, NB = W["batch_per_gpu"], W["seq_len"], W["n_head"], W["head_dim"], W["blocks"]
+    C = H * d
+    ctx = kerr_attn.Context(local)
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    blocks = []
+    for _ in range(NB):
+        qkv = torch.randn(B, T, 3 * C, device=dev, generator=g) / 8
+        blocks.append({
+            "qkv": qkv, "o": torch.empty(B, T, C, device=dev), "lse": torch.empty(B, H, T, device=dev),
+            "dout": torch.randn(B, T, C, device=dev, generator=g), "dqkv": torch.empty_like(qkv)})
+    for blk in blocks:
+        blk["q"], blk["k"], blk["v"] = kerr_attn.split_qkv(blk["qkv"], C)
+        blk["dq"], blk["dk"], blk["dv"] = kerr_attn.split_qkv(blk["dqkv"], C)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        n = 0
+        for i, blk in enumerate(blocks):
+            if ev is not None:
+                ev["f"][i][0].record(stream)
+            n += kerr_attn.fwd(ctx, blk["q"], blk["k"], blk["v"], blk["o"], blk["lse"], H, stream=stream)
+            if ev is not None:
+                ev["f"][i][1].record(stream)
+        for i in reversed(range(NB)):
+            blk = blocks[i]
+            if ev is not None:
+                ev["b"][i][0].record(stream)
+            n += kerr_attn.bwd(ctx, blk["q"], blk["k"], blk["v"], blk["o"], blk["dout"], blk["lse"],
+                               blk["dq"], blk["dk"], blk["dv"], H, stream=stream)
+            if ev is not None:
+                ev["b"][i][1].record(stream)
+        return n
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    sync_all()
+
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    evs = [{"f": [(mk(), mk()) for _ in range(NB)], "b": [(mk(), mk()) for _ in range(NB)]}
+           for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_start, t_end = mk(), mk()
+    sync_all()
+    t_start.record(stream)
+    launches = 0
+    for s in range(args.steps):
+        launches += step(evs[s])
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    sync_all()
+    ms_total = max_over_ranks(t_start.elapsed_time(t_end))
+    ms_step = ms_total / args.steps
+    fwd_ms = statistics.mean(e["f"][i][0].elapsed_time(e["f"][i][1]) for e in evs for i in range(NB))
+    bwd_ms = statistics.mean(e["b"][i][0].elapsed_time(e["b"][i][1]) for e in evs for i in range(NB))
+    fwd_ms, bwd_ms = max_over_ranks(fwd_ms), max_over_ranks(bwd_ms)
+    tokens_per_step = B * T * world
+    value = tokens_per_step / (ms_step / 1e3)
+
+    # End to end through the host-buffer ABI (pinned host inputs and outputs).
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    hb = []
+    for blk in blocks:
+        h = {k: blk[k].cpu().pin_memory() for k in ("qkv", "dout")}
+        h["o"] = torch.empty(B, T, C).pin_memory()
+        h["lse"] = torch.empty(B, H, T).pin_memory()
+        h["dqkv"] = torch.empty(B, T, 3 * C).pin_memory()
+        h["q"], h["k"], h["v"] = kerr_attn.split_qkv(h["qkv"], C)
+        h["dq"], h["dk"], h["dv"] = kerr_attn.split_qkv(h["dqkv"], C)
+        hb.append(h)
+
+    def step_host():
+        for h in hb:
+            kerr_attn.fwd_host(ctx, h["q"], h["k"], h["v"], h["o"], h["lse"], H)
+        for h in reversed(hb):
+            kerr_attn.bwd_host(ctx, h["q"], h["k"], h["v"], h["o"], h["dout"], h["lse"], h["dq"], h["dk"], h["dv"], H)
+
+    step_host()
+    sync_all()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        step_host()
+    sync_all()
+    e2e_s = max_over_ranks(time.perf_counter() - t0) / e2e_steps
+    f4 = 4
+    h2d = NB * (B * T * 3 * C * f4 + (B * T * 3 * C + 2 * B * T * C + B * H * T) * f4)
+    d2h = NB * ((B * T * C + B * H * T) * f4 + B * T * 3 * C * f4)
+
+    peaks, peak_src = measured_peaks()
+    work = algorithmic(B, T, H, d)
+    props = torch.cuda.get_device_properties(dev)
+    ck = clocks.summary()
+    sm_mhz = ck["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
+    ffma_peak_tflops = props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12
+    bwd_gbs = work["bwd_bytes"] / (bwd_ms / 1e3) / 1e9
+    bwd_tflops = work["bwd_flops"] / (bwd_ms / 1e3) / 1e12
+    fwd_tflops = work["fwd_flops"] / (fwd_ms / 1e3) / 1e12
+    traffic = profiled_traffic("attn_bwd_f32")
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded q,k,v ~ N(0,1)/8, dout ~ N(0,1))",
+        "config": dict(WORKLOAD, global_batch=B * world, parallelism=f"dp{world} (batch shards, no exchange)"),
+        "e2e": {"value": tokens_per_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "api": "kattn_fwd_host + kattn_bwd_host per block, pinned host buffers"},
+        "gpu_launches": launches,
+        "roofline": {
+            "kernel": "kattn_bwd call (attn_bwd_rowdot + attn_bwd_f32), 768-dim block",
+            "bound": "hbm", "achieved": bwd_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": bwd_gbs / peaks["hbm_gbs"], "traffic": traffic, "peak_source": peak_src,
+            "algorithmic_bytes_per_launch": work["bwd_bytes"], "launch_ms": bwd_ms,
+            "pipe": {"name": "fp32 FFMA (SIMT)", "achieved_tflops": bwd_tflops,
+                     "peak_tflops": ffma_peak_tflops, "frac": bwd_tflops / ffma_peak_tflops,
+                     "peak_source": "nominal: SMs x 128 FMA/clk x 2 x median sampled SM clock",
+                     "algorithmic_flops_per_launch": work["bwd_flops"]},
+            "fwd": {"launch_ms": fwd_ms, "achieved_tflops": fwd_tflops, "frac_ffma": fwd_tflops / ffma_peak_tflops,
+                    "achieved_gbs": work["fwd_bytes"] / (fwd_ms / 1e3) / 1e9},
+        },
+        "clocks": ck,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        n_seq = min(cores, B)
+        cpu_sample(n_seq, T, H, d)  # warm
+        t = cpu_sample(n_seq, T, H, d)
+        line["cpu_baseline"] = {
+            "value": n_seq * T / (NB * t), "unit": "tokens/s", "cores": n_seq, "kind": "port",
+            "sample": f"1 of 4 blocks, {n_seq} of {B} sequences on {n_seq} host threads; scaled to the step"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,114 @@
+/*
+ * kerr_attn.h — C ABI of the B200 (sm_100a) causal self-attention path of
+ * kerr-engine: forward (Q·Kᵀ scores, causal mask, softmax, P·V) and backward
+ * (dQ, dK, dV recomputed from the saved log-sum-exp).
+ *
+ * What each entry point replaces in the reference (paths inside kerr-engine):
+ *   kattn_fwd       the inline scalar head loop of attention_with_cache,
+ *                   src/pipeline.rs:305-347 (same math as
+ *                   src/model.rs:364-431).  It saves the row log-sum-exp
+ *                   [B][H][T] instead of AttnCache.att_weights [H][T][T]
+ *                   (src/pipeline.rs:157-164, :305, :337).
+ *   kattn_bwd       ComputeBackend::attention_backward, src/backend.rs:223-231,
+ *                   implemented today by CpuBackend (src/backend.rs:344-373 ->
+ *                   src/backward.rs:464-514) and by GpuBackend
+ *                   (src/gpu_dispatch.rs:921-1033 + shaders
+ *                   attn_backward_scores.wgsl / attn_backward_dkv.wgsl).
+ *   kattn_fwd_host, kattn_bwd_host
+ *                   the same two operations at the reference's call boundary:
+ *                   host buffers in, host buffers out, synchronous — the shape
+ *                   of the trait call made from src/pipeline.rs:707-714.
+ *
+ * Conventions
+ *   - All tensors are float32.  q, k, v (and dq, dk, dv) are [B][T][H][d]
+ *     row-major with a row stride (elements) ld >= H*d, so they may be the
+ *     q|k|v column blocks of one [B*T][3C] buffer (ld = 3C) exactly as
+ *     c_attn produces it (src/pipeline.rs:289-303).  o and dout use ld_o.
+ *     lse is [B][H][T], natural log: lse = log(sum_j exp(scale * q·k_j)).
+ *   - Device pointers (kattn_fwd / kattn_bwd) are caller-owned, 16-byte
+ *     aligned, with ld a multiple of 4 and d in {32, 64, 128}.  Outputs must
+ *     not alias inputs.
+ *   - No exception or exit crosses the ABI; every call returns a status.
+ *     kattn_last_error() gives the detail of the last failure on the calling
+ *     thread.
+ *   - kattn_fwd / kattn_bwd only enqueue work on `stream` (a cudaStream_t,
+ *     NULL = legacy default stream) and never synchronise the host.
+ *     kattn_bwd takes a [B][H][T] float workspace from the device's
+ *     stream-ordered memory pool on that stream and returns it there.
+ *   - A context may be shared by threads: the device-pointer calls keep no
+ *     per-call state in it; the host-buffer calls serialise on a lock inside
+ *     it (as the reference's GPU backend serialises on its buffer pool,
+ *     src/gpu_dispatch.rs:550).
+ */
+#ifndef KERR_ATTN_H
+#define KERR_ATTN_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kattn_ctx kattn_ctx;
+
+enum {
+    KATTN_OK = 0,
+    KATTN_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad stride */
+    KATTN_ERR_UNSUPPORTED = 2,      /* head_dim outside {32, 64, 128} */
+    KATTN_ERR_MISALIGNED = 3,       /* pointer not 16-byte aligned or ld % 4 != 0 */
+    KATTN_ERR_DEVICE = 4,           /* no CUDA device, or not an sm_100 part */
+    KATTN_ERR_CUDA = 5,             /* a CUDA runtime call failed */
+    KATTN_ERR_OUT_OF_MEMORY = 6     /* device or pinned allocation failed */
+};
+
+/* Library version, major*10000 + minor*100 + patch. */
+int kattn_version(void);
+
+/* Human-readable name of a status code (static storage). */
+const char* kattn_strerror(int status);
+
+/* Detail of the last non-OK status returned on this thread (static per thread). */
+const char* kattn_last_error(void);
+
+/* Open a context on CUDA device `device` (the Rust GpuBackend's adapter index,
+ * src/backend.rs:51-79).  Fails with KATTN_ERR_DEVICE when the device is absent
+ * or is not compute capability 10.0. */
+int kattn_create(int device, kattn_ctx** out);
+int kattn_destroy(kattn_ctx* ctx);
+
+/* Forward.  o[b,t,h,:] = sum_{j<=t} softmax_j(scale * q[b,t,h,:]·k[b,j,h,:]) v[b,j,h,:]
+ * (j < T instead of j <= t when causal == 0); lse[b,h,t] as above. */
+int kattn_fwd(kattn_ctx* ctx,
+              const float* q, const float* k, const float* v, long ld_qkv,
+              float* o, long ld_o, float* lse,
+              int B, int T, int H, int d, float scale, int causal, void* stream);
+
+/* Backward from the forward's o and lse.  dout is the gradient of o (the
+ * reference's d_pre_proj, same ld_o as o).  dq, dk, dv are fully overwritten. */
+int kattn_bwd(kattn_ctx* ctx,
+              const float* q, const float* k, const float* v, long ld_qkv,
+              const float* o, const float* dout, long ld_o, const float* lse,
+              float* dq, float* dk, float* dv, long ld_dqkv,
+              int B, int T, int H, int d, float scale, int causal, void* stream);
+
+/* Host-buffer forms: same arguments as above, but every pointer is host
+ * memory (pinned or pageable).  The call copies inputs to device buffers owned
+ * by the context, runs the kernels, copies the outputs back and returns when
+ * they are in host memory.  No alignment rule applies to host pointers. */
+int kattn_fwd_host(kattn_ctx* ctx,
+                   const float* q, const float* k, const float* v, long ld_qkv,
+                   float* o, long ld_o, float* lse,
+                   int B, int T, int H, int d, float scale, int causal);
+
+int kattn_bwd_host(kattn_ctx* ctx,
+                   const float* q, const float* k, const float* v, long ld_qkv,
+                   const float* o, const float* dout, long ld_o, const float* lse,
+                   float* dq, float* dk, float* dv, long ld_dqkv,
+                   int B, int T, int H, int d, float scale, int causal);
+
+/* Number of kernel launches the last kattn_fwd / kattn_bwd call on this
+ * thread enqueued (0 for an empty problem or an error). */
+int kattn_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KERR_ATTN_H */

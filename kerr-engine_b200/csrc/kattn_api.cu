@@ -1,0 +1,379 @@
+// C ABI of the attention path (include/kerr_attn.h): argument checking,
+// device contexts, workspace handling and the host-buffer entry points.
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdarg>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "kattn_launch.h"
+#include "kerr_attn.h"
+
+struct kattn_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;  // used by the host-buffer entry points
+    std::mutex host_mu;             // serialises the host-buffer entry points
+    char* arena = nullptr;          // device staging for the host-buffer entry points
+    size_t arena_bytes = 0;
+};
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+thread_local int g_last_launches = 0;
+
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof g_last_error, fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    const int status = (e == cudaErrorMemoryAllocation) ? KATTN_ERR_OUT_OF_MEMORY : KATTN_ERR_CUDA;
+    return fail(status, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Makes ctx->device current for the scope of one call and restores the
+// caller's device afterwards.
+struct DeviceScope {
+    int prev = -1;
+    int dev;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceScope(int d) : dev(d) {
+        err = cudaGetDevice(&prev);
+        if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    }
+};
+
+constexpr int kTile = 64;  // query / key tile rows of the kernels
+
+int check_shape(const kattn_ctx* ctx, int B, int T, int H, int d, float scale, int causal) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    if (B < 0 || T < 0) return fail(KATTN_ERR_INVALID_ARGUMENT, "negative size: B=%d T=%d", B, T);
+    if (H <= 0) return fail(KATTN_ERR_INVALID_ARGUMENT, "n_head must be positive (got %d)", H);
+    if (d != 32 && d != 64 && d != 128)
+        return fail(KATTN_ERR_UNSUPPORTED, "head_dim %d unsupported (32, 64 or 128)", d);
+    if (!std::isfinite(scale)) return fail(KATTN_ERR_INVALID_ARGUMENT, "scale is not finite");
+    if (causal != 0 && causal != 1) return fail(KATTN_ERR_INVALID_ARGUMENT, "causal must be 0 or 1");
+    const long tiles = (static_cast<long>(T) + kTile - 1) / kTile;
+    if (static_cast<long>(B) * H * tiles > INT_MAX)
+        return fail(KATTN_ERR_INVALID_ARGUMENT, "problem too large: B*H*ceil(T/64) exceeds 2^31-1");
+    if (static_cast<long>(H) * d > INT_MAX / 4) return fail(KATTN_ERR_INVALID_ARGUMENT, "H*d too large");
+    return KATTN_OK;
+}
+
+int check_tensor(const char* name, const void* p, long ld, int C, bool device) {
+    if (!p) return fail(KATTN_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+    if (ld < C) return fail(KATTN_ERR_INVALID_ARGUMENT, "%s row stride %ld < H*d = %d", name, ld, C);
+    if (device) {
+        if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+            return fail(KATTN_ERR_MISALIGNED, "%s is not 16-byte aligned", name);
+        if (ld % 4 != 0) return fail(KATTN_ERR_MISALIGNED, "%s row stride %ld is not a multiple of 4", name, ld);
+    }
+    return KATTN_OK;
+}
+
+int check_vec(const char* name, const void* p, bool device) {
+    if (!p) return fail(KATTN_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+    if (device && reinterpret_cast<uintptr_t>(p) % 4 != 0)
+        return fail(KATTN_ERR_MISALIGNED, "%s is not 4-byte aligned", name);
+    return KATTN_OK;
+}
+
+#define KATTN_TRY(expr)                  \
+    do {                                 \
+        const int _s = (expr);           \
+        if (_s != KATTN_OK) return _s;   \
+    } while (0)
+
+int fwd_checks(const kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv,
+               const float* o, long ld_o, const float* lse, int B, int T, int H, int d, float scale,
+               int causal, bool device) {
+    KATTN_TRY(check_shape(ctx, B, T, H, d, scale, causal));
+    if (B == 0 || T == 0) return KATTN_OK;
+    const int C = H * d;
+    KATTN_TRY(check_tensor("q", q, ld_qkv, C, device));
+    KATTN_TRY(check_tensor("k", k, ld_qkv, C, device));
+    KATTN_TRY(check_tensor("v", v, ld_qkv, C, device));
+    KATTN_TRY(check_tensor("o", o, ld_o, C, device));
+    KATTN_TRY(check_vec("lse", lse, device));
+    return KATTN_OK;
+}
+
+int bwd_checks(const kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv,
+               const float* o, const float* dout, long ld_o, const float* lse, const float* dq,
+               const float* dk, const float* dv, long ld_d, int B, int T, int H, int d, float scale,
+               int causal, bool device) {
+    KATTN_TRY(check_shape(ctx, B, T, H, d, scale, causal));
+    if (B == 0 || T == 0) return KATTN_OK;
+    const int C = H * d;
+    KATTN_TRY(check_tensor("q", q, ld_qkv, C, device));
+    KATTN_TRY(check_tensor("k", k, ld_qkv, C, device));
+    KATTN_TRY(check_tensor("v", v, ld_qkv, C, device));
+    KATTN_TRY(check_tensor("o", o, ld_o, C, device));
+    KATTN_TRY(check_tensor("dout", dout, ld_o, C, device));
+    KATTN_TRY(check_vec("lse", lse, device));
+    KATTN_TRY(check_tensor("dq", dq, ld_d, C, device));
+    KATTN_TRY(check_tensor("dk", dk, ld_d, C, device));
+    KATTN_TRY(check_tensor("dv", dv, ld_d, C, device));
+    return KATTN_OK;
+}
+
+int ok_with_launches(int n) {
+    g_last_launches = n;
+    return KATTN_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+int ensure_arena(kattn_ctx* ctx, size_t bytes) {
+    if (ctx->arena_bytes >= bytes) return KATTN_OK;
+    if (ctx->arena) {
+        cudaError_t e = cudaFree(ctx->arena);
+        ctx->arena = nullptr;
+        ctx->arena_bytes = 0;
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFree(staging)");
+    }
+    cudaError_t e = cudaMalloc(&ctx->arena, bytes);
+    if (e != cudaSuccess) {
+        ctx->arena = nullptr;
+        return cuda_fail(e, "cudaMalloc(staging)");
+    }
+    ctx->arena_bytes = bytes;
+    return KATTN_OK;
+}
+
+// Copies a [rows][C] block with row stride ld (elements) between host and a
+// packed device block with row stride ldd.
+cudaError_t copy_rows(float* dst, long ld_dst, const float* src, long ld_src, int C, long rows,
+                      cudaMemcpyKind kind, cudaStream_t s) {
+    if (ld_dst == C && ld_src == C)
+        return cudaMemcpyAsync(dst, src, sizeof(float) * C * rows, kind, s);
+    return cudaMemcpy2DAsync(dst, sizeof(float) * ld_dst, src, sizeof(float) * ld_src, sizeof(float) * C,
+                             static_cast<size_t>(rows), kind, s);
+}
+
+}  // namespace
+
+extern "C" {
+#pragma GCC visibility push(default)
+
+int kattn_version(void) { return 100; }
+
+const char* kattn_strerror(int status) {
+    switch (status) {
+        case KATTN_OK: return "ok";
+        case KATTN_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case KATTN_ERR_UNSUPPORTED: return "unsupported shape";
+        case KATTN_ERR_MISALIGNED: return "misaligned pointer or stride";
+        case KATTN_ERR_DEVICE: return "no usable sm_100 CUDA device";
+        case KATTN_ERR_CUDA: return "CUDA runtime error";
+        case KATTN_ERR_OUT_OF_MEMORY: return "out of memory";
+        default: return "unknown status";
+    }
+}
+
+const char* kattn_last_error(void) { return g_last_error; }
+
+int kattn_last_launch_count(void) { return g_last_launches; }
+
+int kattn_create(int device, kattn_ctx** out) {
+    if (!out) return fail(KATTN_ERR_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(KATTN_ERR_DEVICE, "no CUDA device (%s)", e == cudaSuccess ? "count 0" : cudaGetErrorString(e));
+    }
+    if (device < 0 || device >= n) return fail(KATTN_ERR_DEVICE, "device %d out of range [0, %d)", device, n);
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(KATTN_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", device,
+                    prop.major, prop.minor);
+    DeviceScope scope(device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    kattn_ctx* ctx = new (std::nothrow) kattn_ctx();
+    if (!ctx) return fail(KATTN_ERR_OUT_OF_MEMORY, "host allocation of the context failed");
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    // kattn_bwd takes its workspace from the stream-ordered pool: keep freed
+    // blocks cached in the pool instead of returning them at each sync.
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    cudaGetLastError();
+    *out = ctx;
+    return KATTN_OK;
+}
+
+int kattn_destroy(kattn_ctx* ctx) {
+    if (!ctx) return KATTN_OK;
+    int status = KATTN_OK;
+    {
+        DeviceScope scope(ctx->device);
+        if (ctx->stream) {
+            cudaError_t e = cudaStreamSynchronize(ctx->stream);
+            if (e != cudaSuccess) status = cuda_fail(e, "cudaStreamSynchronize");
+            cudaStreamDestroy(ctx->stream);
+        }
+        if (ctx->arena) cudaFree(ctx->arena);
+    }
+    delete ctx;
+    return status;
+}
+
+int kattn_fwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv, float* o, long ld_o,
+              float* lse, int B, int T, int H, int d, float scale, int causal, void* stream) {
+    g_last_launches = 0;
+    KATTN_TRY(fwd_checks(ctx, q, k, v, ld_qkv, o, ld_o, lse, B, T, H, d, scale, causal, true));
+    if (B == 0 || T == 0) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    kattn::FwdArgs a{q, k, v, ld_qkv, o, ld_o, lse, B, T, H, d, scale, causal};
+    int launches = 0;
+    cudaError_t e = kattn::launch_fwd(a, ctx->num_sms, static_cast<cudaStream_t>(stream), &launches);
+    if (e != cudaSuccess) return cuda_fail(e, "forward launch");
+    return ok_with_launches(launches);
+}
+
+int kattn_bwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv, const float* o,
+              const float* dout, long ld_o, const float* lse, float* dq, float* dk, float* dv, long ld_dqkv, int B,
+              int T, int H, int d, float scale, int causal, void* stream) {
+    g_last_launches = 0;
+    KATTN_TRY(bwd_checks(ctx, q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, B, T, H, d, scale, causal,
+                         true));
+    if (B == 0 || T == 0) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* dsum = nullptr;
+    const size_t ws = sizeof(float) * static_cast<size_t>(B) * H * T;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&dsum), ws, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(workspace)");
+    kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, dsum, B, T, H, d, scale, causal};
+    int launches = 0;
+    e = kattn::launch_bwd(a, ctx->num_sms, s, &launches);
+    cudaError_t ef = cudaFreeAsync(dsum, s);
+    if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+    if (ef != cudaSuccess) return cuda_fail(ef, "cudaFreeAsync(workspace)");
+    return ok_with_launches(launches);
+}
+
+int kattn_fwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv, float* o,
+                   long ld_o, float* lse, int B, int T, int H, int d, float scale, int causal) {
+    g_last_launches = 0;
+    KATTN_TRY(fwd_checks(ctx, q, k, v, ld_qkv, o, ld_o, lse, B, T, H, d, scale, causal, false));
+    if (B == 0 || T == 0) return ok_with_launches(0);
+    std::lock_guard<std::mutex> lock(ctx->host_mu);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    const int C = H * d;
+    const long rows = static_cast<long>(B) * T;
+    const size_t qkv_b = align256(sizeof(float) * rows * 3 * C);
+    const size_t o_b = align256(sizeof(float) * rows * C);
+    const size_t lse_b = align256(sizeof(float) * static_cast<size_t>(B) * H * T);
+    KATTN_TRY(ensure_arena(ctx, qkv_b + o_b + lse_b));
+    float* dqkv = reinterpret_cast<float*>(ctx->arena);
+    float* d_o = reinterpret_cast<float*>(ctx->arena + qkv_b);
+    float* d_lse = reinterpret_cast<float*>(ctx->arena + qkv_b + o_b);
+    cudaStream_t s = ctx->stream;
+    cudaError_t e;
+    if (k == q + C && v == q + 2 * C && ld_qkv == 3L * C) {
+        e = cudaMemcpyAsync(dqkv, q, sizeof(float) * rows * 3 * C, cudaMemcpyHostToDevice, s);
+    } else {
+        e = copy_rows(dqkv, 3L * C, q, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = copy_rows(dqkv + C, 3L * C, k, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = copy_rows(dqkv + 2 * C, 3L * C, v, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
+    kattn::FwdArgs a{dqkv, dqkv + C, dqkv + 2 * C, 3L * C, d_o, C, d_lse, B, T, H, d, scale, causal};
+    int launches = 0;
+    e = kattn::launch_fwd(a, ctx->num_sms, s, &launches);
+    if (e != cudaSuccess) return cuda_fail(e, "forward launch");
+    e = copy_rows(o, ld_o, d_o, C, C, rows, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(lse, d_lse, sizeof(float) * static_cast<size_t>(B) * H * T, cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) return cuda_fail(e, "device-to-host copy");
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    return ok_with_launches(launches);
+}
+
+int kattn_bwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv, const float* o,
+                   const float* dout, long ld_o, const float* lse, float* dq, float* dk, float* dv, long ld_dqkv,
+                   int B, int T, int H, int d, float scale, int causal) {
+    g_last_launches = 0;
+    KATTN_TRY(bwd_checks(ctx, q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, B, T, H, d, scale, causal,
+                         false));
+    if (B == 0 || T == 0) return ok_with_launches(0);
+    std::lock_guard<std::mutex> lock(ctx->host_mu);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    const int C = H * d;
+    const long rows = static_cast<long>(B) * T;
+    const size_t qkv_b = align256(sizeof(float) * rows * 3 * C);
+    const size_t row_b = align256(sizeof(float) * rows * C);
+    const size_t lse_b = align256(sizeof(float) * static_cast<size_t>(B) * H * T);
+    KATTN_TRY(ensure_arena(ctx, 2 * qkv_b + 2 * row_b + 2 * lse_b));
+    char* base = ctx->arena;
+    float* d_qkv = reinterpret_cast<float*>(base);
+    float* d_grad = reinterpret_cast<float*>(base + qkv_b);
+    float* d_o = reinterpret_cast<float*>(base + 2 * qkv_b);
+    float* d_do = reinterpret_cast<float*>(base + 2 * qkv_b + row_b);
+    float* d_lse = reinterpret_cast<float*>(base + 2 * qkv_b + 2 * row_b);
+    float* d_dsum = reinterpret_cast<float*>(base + 2 * qkv_b + 2 * row_b + lse_b);
+    cudaStream_t s = ctx->stream;
+    cudaError_t e;
+    if (k == q + C && v == q + 2 * C && ld_qkv == 3L * C) {
+        e = cudaMemcpyAsync(d_qkv, q, sizeof(float) * rows * 3 * C, cudaMemcpyHostToDevice, s);
+    } else {
+        e = copy_rows(d_qkv, 3L * C, q, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = copy_rows(d_qkv + C, 3L * C, k, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = copy_rows(d_qkv + 2 * C, 3L * C, v, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+    }
+    if (e == cudaSuccess) e = copy_rows(d_o, C, o, ld_o, C, rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = copy_rows(d_do, C, dout, ld_o, C, rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(d_lse, lse, sizeof(float) * static_cast<size_t>(B) * H * T, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
+    kattn::BwdArgs a{d_qkv, d_qkv + C, d_qkv + 2 * C, 3L * C, d_o, d_do, C, d_lse,
+                     d_grad, d_grad + C, d_grad + 2 * C, 3L * C, d_dsum, B, T, H, d, scale, causal};
+    int launches = 0;
+    e = kattn::launch_bwd(a, ctx->num_sms, s, &launches);
+    if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+    if (dk == dq + C && dv == dq + 2 * C && ld_dqkv == 3L * C) {
+        e = cudaMemcpyAsync(dq, d_grad, sizeof(float) * rows * 3 * C, cudaMemcpyDeviceToHost, s);
+    } else {
+        e = copy_rows(dq, ld_dqkv, d_grad, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = copy_rows(dk, ld_dqkv, d_grad + C, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = copy_rows(dv, ld_dqkv, d_grad + 2 * C, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "device-to-host copy");
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    return ok_with_launches(launches);
+}
+
+#pragma GCC visibility pop
+}  // extern "C"

@@ -1,0 +1,45 @@
+// Host-side launch interface between the C ABI (kattn_api.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace kattn {
+
+struct FwdArgs {
+    const float* q;
+    const float* k;
+    const float* v;
+    long ld_qkv;
+    float* o;
+    long ld_o;
+    float* lse;
+    int B, T, H, d;
+    float scale;
+    int causal;
+};
+
+struct BwdArgs {
+    const float* q;
+    const float* k;
+    const float* v;
+    long ld_qkv;
+    const float* o;
+    const float* dout;
+    long ld_o;
+    const float* lse;
+    float* dq;
+    float* dk;
+    float* dv;
+    long ld_d;
+    float* dsum;  // [B][H][T] workspace: rowsum(dout * o)
+    int B, T, H, d;
+    float scale;
+    int causal;
+};
+
+// Each returns the CUDA launch status and adds the number of kernels it
+// enqueued to *launches.
+cudaError_t launch_fwd(const FwdArgs& a, int num_sms, cudaStream_t stream, int* launches);
+cudaError_t launch_bwd(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches);
+
+}  // namespace kattn

@@ -1,0 +1,242 @@
+"""Python binding of libkerr_attn.so (the C ABI declared in include/kerr_attn.h).
+
+The library is the product: sm_100a CUDA kernels for kerr-engine's causal
+self-attention forward (src/pipeline.rs:305-347) and backward
+(ComputeBackend::attention_backward, src/backend.rs:223-231).  This module only
+marshals tensors into the C ABI; it has no compute path of its own and raises
+if the library is missing.
+
+Tensors: torch float32, CUDA for :func:`fwd` / :func:`bwd` (device pointers)
+and CPU (pinned or pageable) for :func:`fwd_host` / :func:`bwd_host`.  q, k, v,
+dq, dk, dv are [B, T, H*d] views whose last dimension is contiguous and whose
+rows may be strided (e.g. the q|k|v column blocks of one [B, T, 3C] buffer).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+
+_PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG_DIR, "lib", "libkerr_attn.so")
+
+KATTN_OK = 0
+KATTN_ERR_INVALID_ARGUMENT = 1
+KATTN_ERR_UNSUPPORTED = 2
+KATTN_ERR_MISALIGNED = 3
+KATTN_ERR_DEVICE = 4
+KATTN_ERR_CUDA = 5
+KATTN_ERR_OUT_OF_MEMORY = 6
+
+# Every function include/kerr_attn.h declares.
+EXPORTED_SYMBOLS = (
+    "kattn_version", "kattn_strerror", "kattn_last_error", "kattn_create", "kattn_destroy",
+    "kattn_fwd", "kattn_bwd", "kattn_fwd_host", "kattn_bwd_host", "kattn_last_launch_count",
+)
+
+
+class KattnError(RuntimeError):
+    def __init__(self, status: int, what: str, detail: str):
+        super().__init__(f"{what}: {detail} (status {status})")
+        self.status = status
+
+
+_lib = None
+_p = ctypes.c_void_p
+_l = ctypes.c_long
+_i = ctypes.c_int
+_fl = ctypes.c_float
+
+
+def build() -> str:
+    """Compile libkerr_attn.so in-tree with the package Makefile."""
+    subprocess.run(["make", "-s", "-C", _PKG_DIR], check=True)
+    return LIB_PATH
+
+
+def lib():
+    """Load libkerr_attn.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C {_PKG_DIR}`")
+    L = ctypes.CDLL(LIB_PATH)
+    L.kattn_version.restype = _i
+    L.kattn_strerror.argtypes = [_i]
+    L.kattn_strerror.restype = ctypes.c_char_p
+    L.kattn_last_error.restype = ctypes.c_char_p
+    L.kattn_last_launch_count.restype = _i
+    L.kattn_create.argtypes = [_i, ctypes.POINTER(_p)]
+    L.kattn_create.restype = _i
+    L.kattn_destroy.argtypes = [_p]
+    L.kattn_destroy.restype = _i
+    fwd_args = [_p, _p, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _fl, _i]
+    bwd_args = [_p, _p, _p, _p, _l, _p, _p, _l, _p, _p, _p, _p, _l, _i, _i, _i, _i, _fl, _i]
+    L.kattn_fwd.argtypes = fwd_args + [_p]
+    L.kattn_fwd.restype = _i
+    L.kattn_bwd.argtypes = bwd_args + [_p]
+    L.kattn_bwd.restype = _i
+    L.kattn_fwd_host.argtypes = fwd_args
+    L.kattn_fwd_host.restype = _i
+    L.kattn_bwd_host.argtypes = bwd_args
+    L.kattn_bwd_host.restype = _i
+    _lib = L
+    return L
+
+
+def strerror(status: int) -> str:
+    return lib().kattn_strerror(status).decode()
+
+
+def last_error() -> str:
+    return lib().kattn_last_error().decode()
+
+
+def last_launch_count() -> int:
+    return lib().kattn_last_launch_count()
+
+
+def _check(status: int, what: str):
+    if status != KATTN_OK:
+        raise KattnError(status, what, f"{strerror(status)}: {last_error()}")
+
+
+class Context:
+    """One kattn_ctx on a CUDA device (kattn_create / kattn_destroy)."""
+
+    def __init__(self, device: int = 0):
+        h = _p()
+        _check(lib().kattn_create(device, ctypes.byref(h)), "kattn_create")
+        self._h = h
+        self.device = device
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if self._h is not None and self._h.value:
+            _check(lib().kattn_destroy(self._h), "kattn_destroy")
+        self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _rows(t, name):
+    """(pointer, row stride) of a [B, T, C] float32 view with unit inner stride."""
+    import torch
+
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32")
+    if t.dim() != 3 or t.stride(2) != 1 or t.stride(0) != t.shape[1] * t.stride(1):
+        raise ValueError(f"{name} must be a [B, T, C] view with contiguous rows stacked over the batch")
+    return ctypes.c_void_p(t.data_ptr()), t.stride(1)
+
+
+def _vec(t, name):
+    import torch
+
+    if t.dtype != torch.float32 or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous float32 tensor")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream_ptr(stream, device):
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def fwd(ctx: Context, q, k, v, o, lse, n_head: int, causal: bool = True, scale: float | None = None,
+        stream=None) -> int:
+    """Enqueue the forward on `stream` (default: torch's current stream).
+    q, k, v, o: [B, T, C] CUDA views; lse: [B, H, T].  Returns kernels launched."""
+    B, T, C = q.shape
+    d = C // n_head
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    pq, ld = _rows(q, "q")
+    pk, ldk = _rows(k, "k")
+    pv, ldv = _rows(v, "v")
+    po, ldo = _rows(o, "o")
+    if not (ld == ldk == ldv):
+        raise ValueError("q, k, v must share one row stride")
+    st = lib().kattn_fwd(ctx.handle, pq, pk, pv, ld, po, ldo, _vec(lse, "lse"), B, T, n_head, d, sc,
+                         int(causal), _stream_ptr(stream, q.device))
+    _check(st, "kattn_fwd")
+    return last_launch_count()
+
+
+def bwd(ctx: Context, q, k, v, o, dout, lse, dq, dk, dv, n_head: int, causal: bool = True,
+        scale: float | None = None, stream=None) -> int:
+    """Enqueue the backward on `stream`.  dq, dk, dv are overwritten.
+    Returns kernels launched."""
+    B, T, C = q.shape
+    d = C // n_head
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    pq, ld = _rows(q, "q")
+    pk, ldk = _rows(k, "k")
+    pv, ldv = _rows(v, "v")
+    po, ldo = _rows(o, "o")
+    pdo, ldd_o = _rows(dout, "dout")
+    pdq, ldg = _rows(dq, "dq")
+    pdk, ldgk = _rows(dk, "dk")
+    pdv, ldgv = _rows(dv, "dv")
+    if not (ld == ldk == ldv) or ldo != ldd_o or not (ldg == ldgk == ldgv):
+        raise ValueError("stride groups (q,k,v), (o,dout), (dq,dk,dv) must each share one row stride")
+    st = lib().kattn_bwd(ctx.handle, pq, pk, pv, ld, po, pdo, ldo, _vec(lse, "lse"), pdq, pdk, pdv, ldg,
+                         B, T, n_head, d, sc, int(causal), _stream_ptr(stream, q.device))
+    _check(st, "kattn_bwd")
+    return last_launch_count()
+
+
+def fwd_host(ctx: Context, q, k, v, o, lse, n_head: int, causal: bool = True, scale: float | None = None) -> int:
+    """Synchronous forward on host (CPU) tensors through kattn_fwd_host."""
+    B, T, C = q.shape
+    d = C // n_head
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    pq, ld = _rows(q, "q")
+    pk, _ = _rows(k, "k")
+    pv, _ = _rows(v, "v")
+    po, ldo = _rows(o, "o")
+    st = lib().kattn_fwd_host(ctx.handle, pq, pk, pv, ld, po, ldo, _vec(lse, "lse"), B, T, n_head, d, sc,
+                              int(causal))
+    _check(st, "kattn_fwd_host")
+    return last_launch_count()
+
+
+def bwd_host(ctx: Context, q, k, v, o, dout, lse, dq, dk, dv, n_head: int, causal: bool = True,
+             scale: float | None = None) -> int:
+    """Synchronous backward on host (CPU) tensors through kattn_bwd_host."""
+    B, T, C = q.shape
+    d = C // n_head
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    pq, ld = _rows(q, "q")
+    pk, _ = _rows(k, "k")
+    pv, _ = _rows(v, "v")
+    po, ldo = _rows(o, "o")
+    pdo, _ = _rows(dout, "dout")
+    pdq, ldg = _rows(dq, "dq")
+    pdk, _ = _rows(dk, "dk")
+    pdv, _ = _rows(dv, "dv")
+    st = lib().kattn_bwd_host(ctx.handle, pq, pk, pv, ld, po, pdo, ldo, _vec(lse, "lse"), pdq, pdk, pdv, ldg,
+                              B, T, n_head, d, sc, int(causal))
+    _check(st, "kattn_bwd_host")
+    return last_launch_count()
+
+
+def split_qkv(qkv, n_embd: int):
+    """q, k, v column-block views of a [B, T, 3C] buffer (src/pipeline.rs:296-302)."""
+    return qkv[..., :n_embd], qkv[..., n_embd:2 * n_embd], qkv[..., 2 * n_embd:]

@@ -1,0 +1,108 @@
+"""ORACLE — test infrastructure only.
+
+ctypes wrapper over ``oracle/lib/libkattn_oracle.so``, the plain-C restatement
+of kerr-engine's CPU causal self-attention (forward: src/pipeline.rs:305-347;
+backward: src/backend.rs:344-373 -> src/backward.rs:464-514).  Only tests/,
+``__graft_entry__.smoke()`` and bench.py's CPU-baseline / reference arm may use
+it, and only as the checker or the timed CPU reference.  PARITY UNPINNED: the
+reference ships no golden vectors for attention; see kattn_oracle.h.
+
+Arrays are numpy float32.  A batch is q, k, v of shape [B, T, ld] (row stride
+ld >= C, head h in columns h*hd..(h+1)*hd), exactly the reference's per-sequence
+``[T][n_embd]`` rows stacked over the batch.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "lib", "libkattn_oracle.so")
+_lib = None
+
+_f = ctypes.POINTER(ctypes.c_float)
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.kattn_oracle_forward_batch.argtypes = [
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            _f, _f, _f, ctypes.c_long, _f, ctypes.c_long, _f, _f, ctypes.c_int]
+        L.kattn_oracle_forward_batch.restype = None
+        L.kattn_oracle_backward_batch.argtypes = [
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            _f, ctypes.c_long, _f, _f, _f, ctypes.c_long, _f,
+            _f, _f, _f, ctypes.c_long, ctypes.c_int]
+        L.kattn_oracle_backward_batch.restype = None
+        L.kattn_oracle_default_threads.argtypes = [ctypes.c_int]
+        L.kattn_oracle_default_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f)
+
+
+def _view(a, C):
+    """Return (base array, row stride) for a [B, T, >=C] float32 view whose rows
+    may be a column slice of a wider contiguous buffer."""
+    assert a.dtype == np.float32 and a.ndim == 3 and a.strides[2] == 4
+    ld = a.strides[1] // 4
+    assert a.strides[0] == a.shape[1] * a.strides[1]
+    return a, ld
+
+
+def _addr(a):
+    return ctypes.cast(ctypes.c_void_p(a.__array_interface__["data"][0]), _f)
+
+
+def default_threads(B: int) -> int:
+    return lib().kattn_oracle_default_threads(B)
+
+
+def forward(q, k, v, n_head: int, want_att: bool = True, threads: int = 0):
+    """Reference forward.  q, k, v: [B, T, C] float32 (may be strided column
+    slices of one [B, T, 3C] qkv buffer, as the reference splits it).
+    Returns (out [B,T,C], att [B,H,T,T] or None, lse [B,H,T])."""
+    B, T, C = q.shape
+    _, ld = _view(q, C)
+    assert k.strides == q.strides and v.strides == q.strides
+    out = np.empty((B, T, C), np.float32)
+    att = np.empty((B, n_head, T, T), np.float32) if want_att else None
+    lse = np.empty((B, n_head, T), np.float32)
+    lib().kattn_oracle_forward_batch(B, T, C, n_head, _addr(q), _addr(k), _addr(v), ld,
+                                     _ptr(out), C, _ptr(att), _ptr(lse), threads)
+    return out, att, lse
+
+
+def backward(d_out, q, k, v, att, n_head: int, threads: int = 0):
+    """Reference backward from the cached post-softmax weights.
+    d_out: [B,T,C] contiguous; q,k,v as in forward(); att: [B,H,T,T].
+    Returns (dq, dk, dv), each [B,T,C]."""
+    B, T, C = q.shape
+    _, ld = _view(q, C)
+    d_out = np.ascontiguousarray(d_out, np.float32)
+    att = np.ascontiguousarray(att, np.float32)
+    dq = np.empty((B, T, C), np.float32)
+    dk = np.empty((B, T, C), np.float32)
+    dv = np.empty((B, T, C), np.float32)
+    lib().kattn_oracle_backward_batch(B, T, C, n_head, _ptr(d_out), C, _addr(q), _addr(k), _addr(v),
+                                      ld, _ptr(att), _ptr(dq), _ptr(dk), _ptr(dv), C, threads)
+    return dq, dk, dv

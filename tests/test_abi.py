@@ -1,0 +1,106 @@
+"""CPU checks of the C ABI boundary: the library loads, exports exactly what
+include/kerr_attn.h declares, and rejects bad arguments before it touches a
+device (these calls make no compute call and need no GPU)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+
+import kerr_attn
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "kerr_attn.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int|const char\s*\*)\s*(kattn_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    if not os.path.exists(kerr_attn.LIB_PATH):
+        kerr_attn.build()
+    return kerr_attn.lib()
+
+
+def test_header_declares_the_binding_surface():
+    assert declared_functions() == sorted(kerr_attn.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(L):
+    out = subprocess.run(["nm", "-D", "--defined-only", kerr_attn.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    for name in declared_functions():
+        assert name in exported, name
+        assert hasattr(L, name)
+    # Nothing but the C ABI is visible.
+    assert exported == set(declared_functions())
+
+
+def test_strerror_and_version(L):
+    assert L.kattn_version() >= 100
+    names = {kerr_attn.strerror(s) for s in range(7)}
+    assert len(names) == 7
+    assert kerr_attn.strerror(0) == "ok"
+    assert kerr_attn.strerror(99) == "unknown status"
+
+
+def _fake_ctx():
+    # A non-NULL handle: every call below fails validation before reading it.
+    return ctypes.c_void_p(0x10)
+
+
+def _fwd(L, ctx, q=0x1000, ld=128, o=0x2000, ld_o=128, lse=0x3000, B=1, T=8, H=4, d=32, scale=0.17, causal=1):
+    return L.kattn_fwd(ctx, ctypes.c_void_p(q), ctypes.c_void_p(q + 512), ctypes.c_void_p(q + 1024), ld,
+                       ctypes.c_void_p(o), ld_o, ctypes.c_void_p(lse), B, T, H, d, scale, causal, None)
+
+
+def test_argument_validation(L):
+    ctx = _fake_ctx()
+    assert _fwd(L, None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert _fwd(L, ctx, d=48, H=2) == kerr_attn.KATTN_ERR_UNSUPPORTED
+    assert "head_dim 48" in kerr_attn.last_error()
+    assert _fwd(L, ctx, B=-1) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert _fwd(L, ctx, H=0) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert _fwd(L, ctx, causal=2) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert _fwd(L, ctx, scale=float("nan")) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert _fwd(L, ctx, ld=64) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT  # ld < H*d
+    assert _fwd(L, ctx, q=0x1004) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert _fwd(L, ctx, ld=130) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert _fwd(L, ctx, o=0) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert _fwd(L, ctx, lse=0x3002) == kerr_attn.KATTN_ERR_MISALIGNED
+
+
+def test_empty_problem_launches_nothing(L):
+    ctx = _fake_ctx()
+    assert _fwd(L, ctx, B=0, q=0, o=0, lse=0) == kerr_attn.KATTN_OK
+    assert kerr_attn.last_launch_count() == 0
+    assert _fwd(L, ctx, T=0, q=0, o=0, lse=0) == kerr_attn.KATTN_OK
+    st = L.kattn_bwd(ctx, None, None, None, 0, None, None, 0, None, None, None, None, 0, 4, 0, 2, 64, 0.125, 1,
+                     None)
+    assert st == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+
+
+def test_bwd_validation(L):
+    ctx = _fake_ctx()
+    p = [ctypes.c_void_p(0x1000 * (i + 1)) for i in range(9)]
+    args = [ctx, p[0], p[1], p[2], 128, p[3], p[4], 128, p[5], p[6], p[7], p[8], 128]
+    bad = list(args)
+    bad[9] = ctypes.c_void_p(0x9008)  # dq misaligned
+    assert L.kattn_bwd(*bad, 1, 8, 4, 32, 0.17, 1, None) == kerr_attn.KATTN_ERR_MISALIGNED
+    bad = list(args)
+    bad[12] = 100  # ld_dqkv < H*d
+    assert L.kattn_bwd(*bad, 1, 8, 4, 32, 0.17, 1, None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device error path")
+def test_create_without_device_fails_cleanly(L):
+    with pytest.raises(kerr_attn.KattnError) as e:
+        kerr_attn.Context(0)
+    assert e.value.status == kerr_attn.KATTN_ERR_DEVICE

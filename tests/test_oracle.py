@@ -1,0 +1,137 @@
+"""CPU checks of the oracle (the C restatement of the reference's attention).
+
+The reference ships no attention golden vectors (parity unpinned), so the
+oracle is checked (1) against an independent float64 autograd computation of
+causal softmax attention, (2) against algebraic known answers of the
+reference's formulas, and (3) against the committed fixtures it generated
+(tests/golden/make_golden.py), which pins it against accidental change.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import make_inputs, rel_err
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def torch_reference(q, k, v, dout, H, causal=True):
+    """float64 autograd reference (independent of the oracle's loop order)."""
+    B, T, C = q.shape
+    d = C // H
+    Q, K, V = (torch.tensor(np.ascontiguousarray(x), dtype=torch.float64, requires_grad=True) for x in (q, k, v))
+
+    def heads(x):
+        return x.view(B, T, H, d).transpose(1, 2)
+
+    s = heads(Q) @ heads(K).transpose(-1, -2) / np.sqrt(d)
+    if causal:
+        s = s.masked_fill(torch.triu(torch.ones(T, T, dtype=torch.bool), 1), float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    O = (s.softmax(-1) @ heads(V)).transpose(1, 2).reshape(B, T, C)
+    O.backward(torch.tensor(dout, dtype=torch.float64))
+    return O.detach().numpy(), lse.detach().numpy(), Q.grad.numpy(), K.grad.numpy(), V.grad.numpy()
+
+
+@pytest.mark.parametrize("B,T,H,d", [(1, 1, 1, 8), (2, 2, 2, 8), (1, 63, 4, 32), (2, 65, 2, 32),
+                                     (1, 130, 3, 64), (4, 64, 4, 32)])
+def test_oracle_matches_float64_autograd(oracle_lib, B, T, H, d):
+    qkv, dout = make_inputs(B, T, H, d, seed=T * 7 + d)
+    C = H * d
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    o, att, lse = oracle_lib.forward(q, k, v, H)
+    dq, dk, dv = oracle_lib.backward(dout, q, k, v, att, H)
+    ro, rlse, rdq, rdk, rdv = torch_reference(q, k, v, dout, H)
+    assert rel_err(o, ro) < 1e-5
+    assert rel_err(lse, rlse) < 1e-5
+    for g, r in ((dq, rdq), (dk, rdk), (dv, rdv)):
+        assert rel_err(g, r) < 1e-4
+
+
+def test_single_position_known_answer(oracle_lib):
+    # T = 1: the only weight is 1, so o = v, dv = dout, dq = dk = 0
+    # (src/pipeline.rs:326-345, src/backward.rs:488-515 with pos = 0).
+    qkv, dout = make_inputs(3, 1, 4, 32, seed=1)
+    C = 128
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    o, att, _ = oracle_lib.forward(q, k, v, 4)
+    assert np.array_equal(o, np.ascontiguousarray(v))
+    assert np.all(att == 1.0)
+    dq, dk, dv = oracle_lib.backward(dout, q, k, v, att, 4)
+    assert np.array_equal(dv, dout)
+    assert np.all(dq == 0) and np.all(dk == 0)
+
+
+def test_equal_keys_give_running_mean(oracle_lib):
+    # All keys equal: every causal row is uniform, o[t] = mean(v[0..t]).
+    B, T, H, d = 1, 40, 2, 32
+    C = H * d
+    qkv, _ = make_inputs(B, T, H, d, seed=3)
+    qkv[..., C:2 * C] = qkv[:, :1, C:2 * C]
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    o, att, _ = oracle_lib.forward(q, k, v, H)
+    mean = np.cumsum(v.astype(np.float64), axis=1) / np.arange(1, T + 1)[None, :, None]
+    assert rel_err(o, mean) < 1e-6
+    for t in range(T):
+        assert np.allclose(att[0, :, t, : t + 1], 1.0 / (t + 1), rtol=1e-6)
+
+
+def test_att_cache_layout(oracle_lib):
+    # AttnCache.att_weights rows sum to one on ki <= qi and stay -inf above the
+    # diagonal, as the reference copies its -inf-initialised scratch row.
+    qkv, _ = make_inputs(2, 17, 3, 8, seed=5)
+    C = 24
+    _, att, _ = oracle_lib.forward(qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:], 3)
+    T = 17
+    upper = np.triu(np.ones((T, T), bool), 1)
+    assert np.all(np.isneginf(att[..., upper]))
+    lower = np.where(upper, 0.0, att)
+    assert np.allclose(lower.sum(-1), 1.0, atol=1e-6)
+
+
+def test_strided_qkv_equals_packed(oracle_lib):
+    qkv, dout = make_inputs(2, 33, 2, 32, seed=9)
+    C = 64
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    o1, a1, l1 = oracle_lib.forward(q, k, v, 2)
+    qc, kc, vc = (np.ascontiguousarray(x) for x in (q, k, v))
+    o2, a2, l2 = oracle_lib.forward(qc, kc, vc, 2)
+    assert np.array_equal(o1, o2) and np.array_equal(a1, a2) and np.array_equal(l1, l2)
+    g1 = oracle_lib.backward(dout, q, k, v, a1, 2)
+    g2 = oracle_lib.backward(dout, qc, kc, vc, a2, 2)
+    for x, y in zip(g1, g2):
+        assert np.array_equal(x, y)
+
+
+def test_thread_count_does_not_change_results(oracle_lib):
+    qkv, dout = make_inputs(5, 20, 2, 16, seed=11)
+    C = 32
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    r1 = oracle_lib.forward(q, k, v, 2, threads=1)
+    r4 = oracle_lib.forward(q, k, v, 2, threads=4)
+    for x, y in zip(r1, r4):
+        assert np.array_equal(x, y)
+    g1 = oracle_lib.backward(dout, q, k, v, r1[1], 2, threads=1)
+    g3 = oracle_lib.backward(dout, q, k, v, r1[1], 2, threads=3)
+    for x, y in zip(g1, g3):
+        assert np.array_equal(x, y)
+
+
+def golden_cases():
+    return sorted(f for f in os.listdir(GOLDEN) if f.endswith(".npz"))
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_oracle_reproduces_golden(oracle_lib, name):
+    z = np.load(os.path.join(GOLDEN, name))
+    H = int(z["n_head"])
+    C = z["qkv"].shape[-1] // 3
+    qkv = z["qkv"]
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    o, att, lse = oracle_lib.forward(q, k, v, H)
+    assert np.array_equal(o, z["o"])
+    assert np.array_equal(lse, z["lse"])
+    dq, dk, dv = oracle_lib.backward(z["dout"], q, k, v, att, H)
+    assert np.array_equal(dq, z["dq"]) and np.array_equal(dk, z["dk"]) and np.array_equal(dv, z["dv"])
