@@ -71,7 +71,7 @@ class ClockSampler(threading.Thread):
         self.period = period_s
         self.samples = []
         self.reasons = set()
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         self.max_mhz = None
         self.ok = False
         try:
@@ -96,7 +96,7 @@ class ClockSampler(threading.Thread):
     def run(self):
         if not self.ok:
             return
-        while not self._stop.is_set():
+        while not self._halt.is_set():
             try:
                 self.sample()
             except Exception:
@@ -104,7 +104,7 @@ class ClockSampler(threading.Thread):
             time.sleep(self.period)
 
     def stop(self):
-        self._stop.set()
+        self._halt.set()
         if self.ok:
             self.join(timeout=2)
             if not self.samples:
@@ -206,6 +206,8 @@ def run_ours(args):
     B, T, H, d, NB = W["batch_per_gpu"], W["seq_len"], W["n_head"], W["head_dim"], W["blocks"]
     C = H * d
     ctx = kerr_attn.Context(local)
+    ctx.set_path({"auto": kerr_attn.PATH_AUTO, "ffma": kerr_attn.PATH_FFMA,
+                  "tensor": kerr_attn.PATH_TENSOR}[args.path])
 
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
@@ -318,6 +320,7 @@ def run_ours(args):
     fwd_tflops = work["fwd_flops"] / (fwd_ms / 1e3) / 1e12
     traffic = profiled_traffic("attn_bwd_f32")
 
+    ctx.check_device()
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -326,7 +329,7 @@ def run_ours(args):
         "e2e": {"value": tokens_per_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "api": "kattn_fwd_host + kattn_bwd_host per block, pinned host buffers"},
-        "gpu_launches": launches,
+        "gpu_launches": launches, "kernel_path": args.path,
         "roofline": {
             "kernel": "kattn_bwd call (attn_bwd_rowdot + attn_bwd_f32), 768-dim block",
             "bound": "hbm", "achieved": bwd_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -365,6 +368,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=("auto", "ffma", "tensor"), default="auto",
+                    help="kernel family (auto: tensor cores where supported)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

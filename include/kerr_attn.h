@@ -56,7 +56,16 @@ enum {
     KATTN_ERR_MISALIGNED = 3,       /* pointer not 16-byte aligned or ld % 4 != 0 */
     KATTN_ERR_DEVICE = 4,           /* no CUDA device, or not an sm_100 part */
     KATTN_ERR_CUDA = 5,             /* a CUDA runtime call failed */
-    KATTN_ERR_OUT_OF_MEMORY = 6     /* device or pinned allocation failed */
+    KATTN_ERR_OUT_OF_MEMORY = 6,    /* device or pinned allocation failed */
+    KATTN_ERR_DEVICE_TIMEOUT = 7    /* a kernel gave up a bounded wait on the tensor core */
+};
+
+/* Kernel families (kattn_set_path).  AUTO uses the tensor-core kernels where
+ * they exist (head_dim 64) and the FFMA kernels elsewhere. */
+enum {
+    KATTN_PATH_AUTO = 0,
+    KATTN_PATH_FFMA = 1,   /* f32 CUDA-core kernels, every supported head_dim */
+    KATTN_PATH_TENSOR = 2  /* tcgen05 bf16x3 kernels; head_dim 64 only */
 };
 
 /* Library version, major*10000 + minor*100 + patch. */
@@ -73,6 +82,16 @@ const char* kattn_last_error(void);
  * or is not compute capability 10.0. */
 int kattn_create(int device, kattn_ctx** out);
 int kattn_destroy(kattn_ctx* ctx);
+
+/* Select the kernel family for later calls on this context (no counterpart
+ * in the reference, whose backend choice is src/backend.rs:22-47).
+ * KATTN_ERR_INVALID_ARGUMENT for an unknown value. */
+int kattn_set_path(kattn_ctx* ctx, int path);
+
+/* Waits for the context's device to finish its work and reports whether any
+ * kernel gave up a bounded wait since the last check (KATTN_ERR_DEVICE_TIMEOUT,
+ * after which results of the affected calls are undefined); clears the flag. */
+int kattn_check_device(kattn_ctx* ctx);
 
 /* Forward.  o[b,t,h,:] = sum_{j<=t} softmax_j(scale * q[b,t,h,:]·k[b,j,h,:]) v[b,j,h,:]
  * (j < T instead of j <= t when causal == 0); lse[b,h,t] as above. */

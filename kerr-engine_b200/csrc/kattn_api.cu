@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "kattn_launch.h"
@@ -16,6 +17,8 @@
 struct kattn_ctx {
     int device = 0;
     int num_sms = 0;
+    std::atomic<int> path{KATTN_PATH_AUTO};
+    int* d_status = nullptr;        // device word set by kernels whose bounded waits give up
     cudaStream_t stream = nullptr;  // used by the host-buffer entry points
     std::mutex host_mu;             // serialises the host-buffer entry points
     char* arena = nullptr;          // device staging for the host-buffer entry points
@@ -135,6 +138,19 @@ int ok_with_launches(int n) {
     return KATTN_OK;
 }
 
+// Forward launch on the kernel family the context selects.
+cudaError_t dispatch_fwd(kattn_ctx* ctx, const kattn::FwdArgs& a, cudaStream_t s, int* launches) {
+    const int path = ctx->path.load(std::memory_order_relaxed);
+    if (path != KATTN_PATH_FFMA && kattn::fwd_tc_supported(a)) return kattn::launch_fwd_tc(a, ctx->d_status, s, launches);
+    return kattn::launch_fwd(a, ctx->num_sms, s, launches);
+}
+
+int path_check(const kattn_ctx* ctx, int d) {
+    if (ctx->path.load(std::memory_order_relaxed) == KATTN_PATH_TENSOR && d != 64)
+        return fail(KATTN_ERR_UNSUPPORTED, "the tensor-core path supports head_dim 64 only (got %d)", d);
+    return KATTN_OK;
+}
+
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 int ensure_arena(kattn_ctx* ctx, size_t bytes) {
@@ -180,6 +196,7 @@ const char* kattn_strerror(int status) {
         case KATTN_ERR_DEVICE: return "no usable sm_100 CUDA device";
         case KATTN_ERR_CUDA: return "CUDA runtime error";
         case KATTN_ERR_OUT_OF_MEMORY: return "out of memory";
+        case KATTN_ERR_DEVICE_TIMEOUT: return "a kernel gave up a bounded wait on the device";
         default: return "unknown status";
     }
 }
@@ -215,6 +232,14 @@ int kattn_create(int device, kattn_ctx** out) {
         delete ctx;
         return cuda_fail(e, "cudaStreamCreate");
     }
+    e = cudaMalloc(&ctx->d_status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(ctx->stream);
+        if (ctx->d_status) cudaFree(ctx->d_status);
+        delete ctx;
+        return cuda_fail(e, "status word");
+    }
     // kattn_bwd takes its workspace from the stream-ordered pool: keep freed
     // blocks cached in the pool instead of returning them at each sync.
     cudaMemPool_t pool;
@@ -238,9 +263,32 @@ int kattn_destroy(kattn_ctx* ctx) {
             cudaStreamDestroy(ctx->stream);
         }
         if (ctx->arena) cudaFree(ctx->arena);
+        if (ctx->d_status) cudaFree(ctx->d_status);
     }
     delete ctx;
     return status;
+}
+
+int kattn_set_path(kattn_ctx* ctx, int path) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    if (path != KATTN_PATH_AUTO && path != KATTN_PATH_FFMA && path != KATTN_PATH_TENSOR)
+        return fail(KATTN_ERR_INVALID_ARGUMENT, "unknown path %d", path);
+    ctx->path.store(path);
+    return KATTN_OK;
+}
+
+int kattn_check_device(kattn_ctx* ctx) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+    int flag = 0;
+    e = cudaMemcpy(&flag, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && flag != 0) e = cudaMemset(ctx->d_status, 0, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "status word");
+    if (flag != 0) return fail(KATTN_ERR_DEVICE_TIMEOUT, "a kernel reported a wait timeout (flags 0x%x)", flag);
+    return KATTN_OK;
 }
 
 int kattn_fwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv, float* o, long ld_o,
@@ -250,9 +298,10 @@ int kattn_fwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, lo
     if (B == 0 || T == 0) return ok_with_launches(0);
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    KATTN_TRY(path_check(ctx, d));
     kattn::FwdArgs a{q, k, v, ld_qkv, o, ld_o, lse, B, T, H, d, scale, causal};
     int launches = 0;
-    cudaError_t e = kattn::launch_fwd(a, ctx->num_sms, static_cast<cudaStream_t>(stream), &launches);
+    cudaError_t e = dispatch_fwd(ctx, a, static_cast<cudaStream_t>(stream), &launches);
     if (e != cudaSuccess) return cuda_fail(e, "forward launch");
     return ok_with_launches(launches);
 }
@@ -307,9 +356,10 @@ int kattn_fwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* 
         if (e == cudaSuccess) e = copy_rows(dqkv + 2 * C, 3L * C, v, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
     }
     if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
+    KATTN_TRY(path_check(ctx, d));
     kattn::FwdArgs a{dqkv, dqkv + C, dqkv + 2 * C, 3L * C, d_o, C, d_lse, B, T, H, d, scale, causal};
     int launches = 0;
-    e = kattn::launch_fwd(a, ctx->num_sms, s, &launches);
+    e = dispatch_fwd(ctx, a, s, &launches);
     if (e != cudaSuccess) return cuda_fail(e, "forward launch");
     e = copy_rows(o, ld_o, d_o, C, C, rows, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess)

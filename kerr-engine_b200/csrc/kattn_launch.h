@@ -42,4 +42,9 @@ struct BwdArgs {
 cudaError_t launch_fwd(const FwdArgs& a, int num_sms, cudaStream_t stream, int* launches);
 cudaError_t launch_bwd(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches);
 
+// Tensor-core (tcgen05) kernels.  `status` is a device word the kernels set
+// (bit 0) when a bounded wait on the tensor core gives up.
+bool fwd_tc_supported(const FwdArgs& a);
+cudaError_t launch_fwd_tc(const FwdArgs& a, int* status, cudaStream_t stream, int* launches);
+
 }  // namespace kattn

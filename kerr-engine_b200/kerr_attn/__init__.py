@@ -28,10 +28,16 @@ KATTN_ERR_MISALIGNED = 3
 KATTN_ERR_DEVICE = 4
 KATTN_ERR_CUDA = 5
 KATTN_ERR_OUT_OF_MEMORY = 6
+KATTN_ERR_DEVICE_TIMEOUT = 7
+
+PATH_AUTO = 0
+PATH_FFMA = 1
+PATH_TENSOR = 2
 
 # Every function include/kerr_attn.h declares.
 EXPORTED_SYMBOLS = (
     "kattn_version", "kattn_strerror", "kattn_last_error", "kattn_create", "kattn_destroy",
+    "kattn_set_path", "kattn_check_device",
     "kattn_fwd", "kattn_bwd", "kattn_fwd_host", "kattn_bwd_host", "kattn_last_launch_count",
 )
 
@@ -72,6 +78,10 @@ def lib():
     L.kattn_create.restype = _i
     L.kattn_destroy.argtypes = [_p]
     L.kattn_destroy.restype = _i
+    L.kattn_set_path.argtypes = [_p, _i]
+    L.kattn_set_path.restype = _i
+    L.kattn_check_device.argtypes = [_p]
+    L.kattn_check_device.restype = _i
     fwd_args = [_p, _p, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _fl, _i]
     bwd_args = [_p, _p, _p, _p, _l, _p, _p, _l, _p, _p, _p, _p, _l, _i, _i, _i, _i, _fl, _i]
     L.kattn_fwd.argtypes = fwd_args + [_p]
@@ -115,6 +125,14 @@ class Context:
     @property
     def handle(self):
         return self._h
+
+    def set_path(self, path: int):
+        """Kernel family for later calls: PATH_AUTO, PATH_FFMA or PATH_TENSOR."""
+        _check(lib().kattn_set_path(self._h, path), "kattn_set_path")
+
+    def check_device(self):
+        """Synchronise the device; raise if a kernel gave up a bounded wait."""
+        _check(lib().kattn_check_device(self._h), "kattn_check_device")
 
     def close(self):
         if self._h is not None and self._h.value:

@@ -23,15 +23,28 @@ GRAD_TOL = 1e-3
 
 
 @pytest.fixture(scope="module")
-def ctx():
+def module_ctx():
     c = kerr_attn.Context(0)
     yield c
     c.close()
 
 
-def gpu_fwd_bwd(ctx, qkv, dout, H, causal=True, stream=None):
+@pytest.fixture
+def ctx(module_ctx):
+    module_ctx.set_path(kerr_attn.PATH_AUTO)
+    yield module_ctx
+    module_ctx.check_device()
+
+
+PATHS = {"ffma": kerr_attn.PATH_FFMA, "tensor": kerr_attn.PATH_TENSOR}
+
+
+def gpu_fwd_bwd(ctx, qkv, dout, H, causal=True, stream=None, path="auto"):
     B, T, C3 = qkv.shape
     C = C3 // 3
+    if path == "tensor" and C // H != 64:
+        pytest.skip("the tensor-core path covers head_dim 64")
+    ctx.set_path(PATHS.get(path, kerr_attn.PATH_AUTO))
     dev = torch.device("cuda", 0)
     qkv_d = torch.from_numpy(qkv).to(dev)
     q, k, v = kerr_attn.split_qkv(qkv_d, C)
@@ -43,6 +56,7 @@ def gpu_fwd_bwd(ctx, qkv, dout, H, causal=True, stream=None):
     dq, dk, dv = kerr_attn.split_qkv(dqkv, C)
     n_b = kerr_attn.bwd(ctx, q, k, v, o, dout_d, lse, dq, dk, dv, H, causal=causal, stream=stream)
     torch.cuda.synchronize()
+    ctx.check_device()
     assert n_f == 1 and n_b == 2
     return (o.cpu().numpy(), lse.cpu().numpy(), dq.cpu().numpy(), dk.cpu().numpy(), dv.cpu().numpy())
 
@@ -80,27 +94,30 @@ SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("path", ["ffma", "tensor"])
 @pytest.mark.parametrize("B,T,H,d", SHAPES)
-def test_parity_with_oracle(ctx, oracle_lib, B, T, H, d):
+def test_parity_with_oracle(ctx, oracle_lib, B, T, H, d, path):
     qkv, dout = make_inputs(B, T, H, d, seed=B * 1000 + T + d)
-    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H), oracle_fwd_bwd(oracle_lib, qkv, dout, H))
+    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, path=path), oracle_fwd_bwd(oracle_lib, qkv, dout, H))
 
 
+@pytest.mark.parametrize("path", ["ffma", "tensor"])
 @pytest.mark.parametrize("name", sorted(f for f in os.listdir(GOLDEN) if f.endswith(".npz")))
-def test_parity_with_golden(ctx, name):
+def test_parity_with_golden(ctx, name, path):
     z = np.load(os.path.join(GOLDEN, name))
-    got = gpu_fwd_bwd(ctx, z["qkv"], z["dout"], int(z["n_head"]))
+    got = gpu_fwd_bwd(ctx, z["qkv"], z["dout"], int(z["n_head"]), path=path)
     assert_parity(got, (z["o"], z["lse"], z["dq"], z["dk"], z["dv"]))
 
 
+@pytest.mark.parametrize("path", ["ffma", "tensor"])
 @pytest.mark.parametrize("B,T,H,d,sigma", [(64, 256, 4, 32, None), (16, 256, 12, 64, None),
                                            (16, 256, 12, 64, 1.0)])
-def test_full_size_against_oracle(ctx, oracle_lib, B, T, H, d, sigma):
+def test_full_size_against_oracle(ctx, oracle_lib, B, T, H, d, sigma, path):
     # The attention micro-benchmark (B=64, H=4, T=256, d=32) and the 768-dim
     # model's per-layer batch (B=16, H=12, T=256, d=64) at full size; sigma=1
     # gives sharper softmax rows than the 1/sqrt(d) default.
     qkv, dout = make_inputs(B, T, H, d, seed=2024, qkv_sigma=sigma)
-    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H), oracle_fwd_bwd(oracle_lib, qkv, dout, H))
+    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, path=path), oracle_fwd_bwd(oracle_lib, qkv, dout, H))
 
 
 def torch_f64(qkv, dout, H, causal):
@@ -123,20 +140,23 @@ def torch_f64(qkv, dout, H, causal):
             g[..., :C].cpu().numpy(), g[..., C:2 * C].cpu().numpy(), g[..., 2 * C:].cpu().numpy())
 
 
-@pytest.mark.parametrize("B,T,H,d", [(2, 64, 2, 32), (1, 100, 2, 64), (2, 200, 1, 128)])
-def test_non_causal_against_float64(ctx, B, T, H, d):
+@pytest.mark.parametrize("path", ["ffma", "tensor"])
+@pytest.mark.parametrize("B,T,H,d", [(2, 64, 2, 32), (1, 100, 2, 64), (2, 200, 1, 128), (1, 300, 3, 64)])
+def test_non_causal_against_float64(ctx, B, T, H, d, path):
     qkv, dout = make_inputs(B, T, H, d, seed=77 + T)
-    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, causal=False), torch_f64(qkv, dout, H, causal=False))
+    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, causal=False, path=path), torch_f64(qkv, dout, H, causal=False))
 
 
-def test_long_context_against_float64(ctx):
+@pytest.mark.parametrize("path", ["ffma", "tensor"])
+def test_long_context_against_float64(ctx, path):
     # Long-context sweep shape (H=12, d=64) at T=2048 for one sequence,
     # q, k, v ~ N(0, 1)/8.
     qkv, dout = make_inputs(1, 2048, 12, 64, seed=5, qkv_sigma=1.0 / 8)
-    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, 12), torch_f64(qkv, dout, 12, causal=True))
+    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, 12, path=path), torch_f64(qkv, dout, 12, causal=True))
 
 
-def test_full_size_identities(ctx):
+@pytest.mark.parametrize("path", ["ffma", "tensor"])
+def test_full_size_identities(ctx, path):
     # Size-independent identities of causal softmax attention at the 768-dim
     # layer size: sum_t dV[t] = sum_t dO[t] and sum_t dK[t] = 0 per (b, h)
     # (softmax rows sum to one); constant values give o = v; adding one vector
@@ -144,7 +164,7 @@ def test_full_size_identities(ctx):
     B, T, H, d = 16, 256, 12, 64
     C = H * d
     qkv, dout = make_inputs(B, T, H, d, seed=99)
-    o, lse, dq, dk, dv = gpu_fwd_bwd(ctx, qkv, dout, H)
+    o, lse, dq, dk, dv = gpu_fwd_bwd(ctx, qkv, dout, H, path=path)
     sdv = dv.astype(np.float64).reshape(B, T, H, d).sum(1)
     sdo = dout.astype(np.float64).reshape(B, T, H, d).sum(1)
     assert rel_err(sdv, sdo) < 1e-4
@@ -153,13 +173,13 @@ def test_full_size_identities(ctx):
 
     const = qkv.copy()
     const[..., 2 * C:] = qkv[:, :1, 2 * C:]
-    o_c = gpu_fwd_bwd(ctx, const, dout, H)[0]
+    o_c = gpu_fwd_bwd(ctx, const, dout, H, path=path)[0]
     assert rel_err(o_c, np.broadcast_to(qkv[:, :1, 2 * C:], o_c.shape)) < 1e-5
 
     shifted = qkv.copy()
     rng = np.random.default_rng(3)
     shifted[..., C:2 * C] += (rng.standard_normal((1, 1, C)) * 0.1).astype(np.float32)
-    o_s = gpu_fwd_bwd(ctx, shifted, dout, H)[0]
+    o_s = gpu_fwd_bwd(ctx, shifted, dout, H, path=path)[0]
     assert rel_err(o_s, o) < 1e-4
 
 
