@@ -145,6 +145,14 @@ cudaError_t dispatch_fwd(kattn_ctx* ctx, const kattn::FwdArgs& a, cudaStream_t s
     return kattn::launch_fwd(a, ctx->num_sms, s, launches);
 }
 
+// Backward launch on the kernel family the context selects.
+cudaError_t dispatch_bwd(kattn_ctx* ctx, const kattn::BwdArgs& a, cudaStream_t s, int* launches) {
+    const int path = ctx->path.load(std::memory_order_relaxed);
+    if (path != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a))
+        return kattn::launch_bwd_tc(a, ctx->num_sms, ctx->d_status, s, launches);
+    return kattn::launch_bwd(a, ctx->num_sms, s, launches);
+}
+
 int path_check(const kattn_ctx* ctx, int d) {
     if (ctx->path.load(std::memory_order_relaxed) == KATTN_PATH_TENSOR && d != 64)
         return fail(KATTN_ERR_UNSUPPORTED, "the tensor-core path supports head_dim 64 only (got %d)", d);
@@ -322,7 +330,7 @@ int kattn_bwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, lo
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(workspace)");
     kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, dsum, B, T, H, d, scale, causal};
     int launches = 0;
-    e = kattn::launch_bwd(a, ctx->num_sms, s, &launches);
+    e = dispatch_bwd(ctx, a, s, &launches);
     cudaError_t ef = cudaFreeAsync(dsum, s);
     if (e != cudaSuccess) return cuda_fail(e, "backward launch");
     if (ef != cudaSuccess) return cuda_fail(ef, "cudaFreeAsync(workspace)");
@@ -407,10 +415,11 @@ int kattn_bwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* 
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(d_lse, lse, sizeof(float) * static_cast<size_t>(B) * H * T, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
+    KATTN_TRY(path_check(ctx, d));
     kattn::BwdArgs a{d_qkv, d_qkv + C, d_qkv + 2 * C, 3L * C, d_o, d_do, C, d_lse,
                      d_grad, d_grad + C, d_grad + 2 * C, 3L * C, d_dsum, B, T, H, d, scale, causal};
     int launches = 0;
-    e = kattn::launch_bwd(a, ctx->num_sms, s, &launches);
+    e = dispatch_bwd(ctx, a, s, &launches);
     if (e != cudaSuccess) return cuda_fail(e, "backward launch");
     if (dk == dq + C && dv == dq + 2 * C && ld_dqkv == 3L * C) {
         e = cudaMemcpyAsync(dq, d_grad, sizeof(float) * rows * 3 * C, cudaMemcpyDeviceToHost, s);

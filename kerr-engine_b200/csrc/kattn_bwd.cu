@@ -308,8 +308,7 @@ __global__ void __launch_bounds__(BWD_NT, (D <= 64 ? 2 : 1)) attn_bwd_f32(const 
     }
 }
 
-template <int D>
-static cudaError_t launch_bwd_d(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches) {
+static BwdParams make_params(const BwdArgs& a) {
     BwdParams p;
     p.q = a.q;
     p.k = a.k;
@@ -331,17 +330,37 @@ static cudaError_t launch_bwd_d(const BwdArgs& a, int num_sms, cudaStream_t stre
     p.scale_log2 = a.scale * kLog2e;
     p.causal = a.causal;
     p.n_tiles = (a.T + BWD_BM - 1) / BWD_BM;
+    return p;
+}
 
-    const long nrows = static_cast<long>(a.B) * a.T * a.H;
+template <int D>
+static cudaError_t launch_prep_d(const BwdParams& p, int num_sms, cudaStream_t stream, int* launches) {
+    const long nrows = static_cast<long>(p.B) * p.T * p.H;
     const long rows_per_block = (256 / 32) * (32 / (D / 4));
     long blocks = (nrows + rows_per_block - 1) / rows_per_block;
     const long cap = static_cast<long>(num_sms > 0 ? num_sms : 148) * 8;
     if (blocks > cap) blocks = cap;
     attn_bwd_rowdot<D><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    *launches += 1;
+    if (e == cudaSuccess) *launches += 1;
+    return e;
+}
 
+cudaError_t launch_bwd_prep(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches) {
+    const BwdParams p = make_params(a);
+    switch (a.d) {
+        case 32: return launch_prep_d<32>(p, num_sms, stream, launches);
+        case 64: return launch_prep_d<64>(p, num_sms, stream, launches);
+        case 128: return launch_prep_d<128>(p, num_sms, stream, launches);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int D>
+static cudaError_t launch_bwd_d(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches) {
+    const BwdParams p = make_params(a);
+    cudaError_t e = launch_prep_d<D>(p, num_sms, stream, launches);
+    if (e != cudaSuccess) return e;
     const size_t smem = sizeof(BwdSmem<D>);
     e = cudaFuncSetAttribute(attn_bwd_f32<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;

@@ -20,6 +20,7 @@
 #include "kattn_common.cuh"
 #include "kattn_launch.h"
 #include "sm100.cuh"
+#include "tc_tiles.cuh"
 
 namespace kattn {
 using namespace sm100;
@@ -65,43 +66,6 @@ struct Params {
     int n_qtiles;
     int n_ktiles;
 };
-
-// Rows [row0, row0 + R) of one head slice (row stride ld floats, 64 columns)
-// -> bf16 hi / lo tiles in the 128B-swizzled layout, scaled by `mul`, zero
-// beyond row T.  Thread i handles (row, 8-float chunk) pairs.
-template <int R>
-__device__ __forceinline__ void stage_rows(uint8_t* hi, uint8_t* lo, const float* g, long ld, int row0, int T,
-                                           float mul, int tid) {
-    constexpr int ITEMS = R * 8 / NT;
-    float4 a[ITEMS], b[ITEMS];
-#pragma unroll
-    for (int it = 0; it < ITEMS; ++it) {
-        const int i = tid + it * NT;
-        const int r = i >> 3;
-        const int ch = i & 7;
-        a[it] = make_float4(0.f, 0.f, 0.f, 0.f);
-        b[it] = a[it];
-        if (row0 + r < T) {
-            const float4* s = reinterpret_cast<const float4*>(g + static_cast<long>(row0 + r) * ld + ch * 8);
-            a[it] = __ldg(s);
-            b[it] = __ldg(s + 1);
-        }
-    }
-#pragma unroll
-    for (int it = 0; it < ITEMS; ++it) {
-        const int i = tid + it * NT;
-        const int r = i >> 3;
-        const int ch = i & 7;
-        uint4 h, l;
-        split2(a[it].x * mul, a[it].y * mul, h.x, l.x);
-        split2(a[it].z * mul, a[it].w * mul, h.y, l.y);
-        split2(b[it].x * mul, b[it].y * mul, h.z, l.z);
-        split2(b[it].z * mul, b[it].w * mul, h.w, l.w);
-        const uint32_t off = sw128(r, ch);
-        *reinterpret_cast<uint4*>(hi + off) = h;
-        *reinterpret_cast<uint4*>(lo + off) = l;
-    }
-}
 
 __device__ __forceinline__ void issue_s(const Smem& sm, uint32_t tm, int stage) {
     constexpr uint32_t idesc = idesc_bf16(BM, BN, 0, 0);
@@ -158,12 +122,12 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         mbar_init(&sm.bar_s, 1);
         mbar_init(&sm.bar_o, 1);
     }
-    stage_rows<BM>(sm.qh, sm.ql, qg, p.ld_qkv, q0, p.T, p.scale_log2, tid);
-    stage_rows<BN>(sm.kh[0], sm.kl[0], kg, p.ld_qkv, 0, p.T, 1.f, tid);
-    stage_rows<BN>(sm.vh[0], sm.vl[0], vg, p.ld_qkv, 0, p.T, 1.f, tid);
+    tc::stage_rows<BM, NT>(sm.qh, sm.ql, qg, p.ld_qkv, q0, p.T, p.scale_log2, tid);
+    tc::stage_rows<BN, NT>(sm.kh[0], sm.kl[0], kg, p.ld_qkv, 0, p.T, 1.f, tid);
+    tc::stage_rows<BN, NT>(sm.vh[0], sm.vl[0], vg, p.ld_qkv, 0, p.T, 1.f, tid);
     if (n_kv > 1) {
-        stage_rows<BN>(sm.kh[1], sm.kl[1], kg, p.ld_qkv, BN, p.T, 1.f, tid);
-        stage_rows<BN>(sm.vh[1], sm.vl[1], vg, p.ld_qkv, BN, p.T, 1.f, tid);
+        tc::stage_rows<BN, NT>(sm.kh[1], sm.kl[1], kg, p.ld_qkv, BN, p.T, 1.f, tid);
+        tc::stage_rows<BN, NT>(sm.vh[1], sm.vl[1], vg, p.ld_qkv, BN, p.T, 1.f, tid);
     }
     fence_async_smem();
     tc_fence_before();
@@ -263,8 +227,8 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         }
         // Key / value tile j+2 into the stage that tile j used (its MMAs are done).
         if (j + 2 < n_kv) {
-            stage_rows<BN>(sm.kh[stage], sm.kl[stage], kg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
-            stage_rows<BN>(sm.vh[stage], sm.vl[stage], vg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
+            tc::stage_rows<BN, NT>(sm.kh[stage], sm.kl[stage], kg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
+            tc::stage_rows<BN, NT>(sm.vh[stage], sm.vl[stage], vg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
             fence_async_smem();
         }
     }
@@ -275,8 +239,8 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         if (tid == 0) {
             mma_commit(&sm.bar_o);
         }
-        mbar_wait(&sm.bar_o, 0, 1u << 16);
-        mbar_wait(&sm.bar_o, 1, 1u << 16);
+        mbar_wait(&sm.bar_o, 0, 10000000ull);
+        mbar_wait(&sm.bar_o, 1, 10000000ull);
     } else {
         // Normalise and stage O through shared memory (reusing the Q tiles,
         // float4 chunks XOR-swizzled by row) for coalesced global stores.

@@ -46,5 +46,10 @@ cudaError_t launch_bwd(const BwdArgs& a, int num_sms, cudaStream_t stream, int* 
 // (bit 0) when a bounded wait on the tensor core gives up.
 bool fwd_tc_supported(const FwdArgs& a);
 cudaError_t launch_fwd_tc(const FwdArgs& a, int* status, cudaStream_t stream, int* launches);
+bool bwd_tc_supported(const BwdArgs& a);
+cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches);
+
+// D = rowsum(dout * o) into a.dsum and dq = 0 (first kernel of every backward).
+cudaError_t launch_bwd_prep(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches);
 
 }  // namespace kattn

@@ -25,6 +25,11 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+// Arrive (release, CTA scope) once on the barrier.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -37,15 +42,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after
-// `limit` polls (each try_wait itself blocks for a bounded, hardware-chosen
-// time) and returns false; the caller records the timeout and unwinds.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 22)) {
-    for (uint32_t i = 0; i < limit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (i > 64) __nanosleep(64);
+// `limit_ns` of wall time (default one second) and returns false; the caller
+// records the timeout and unwinds.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 1000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+        __nanosleep(32);
     }
-    return false;
+    return true;
+}
+
+// mbar_wait with a warp-uniform outcome (required before warp-collective
+// tcgen05.ld / st): true only if every lane of the warp saw the phase complete.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+    const bool ok = mbar_wait(bar, parity);
+    return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------- fences

@@ -1,0 +1,50 @@
+// Global f32 rows -> bf16 hi/lo operand tiles for the tcgen05 kernels.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace kattn {
+namespace tc {
+
+// Rows [row0, row0 + R) of one 64-column head slice (row stride ld floats)
+// -> bf16 hi / lo tiles of R rows x 128 bytes in the 128B-swizzled layout,
+// multiplied by `mul`, zero beyond row T.  NTH threads cooperate; thread `t`
+// handles (row, 8-float chunk) items t, t + NTH, ...  All loads are issued
+// before the first conversion so they are in flight together.
+template <int R, int NTH>
+__device__ __forceinline__ void stage_rows(uint8_t* hi, uint8_t* lo, const float* g, long ld, int row0, int T,
+                                           float mul, int t) {
+    static_assert((R * 8) % NTH == 0, "tile items must divide evenly");
+    constexpr int ITEMS = R * 8 / NTH;
+    float4 a[ITEMS], b[ITEMS];
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+        const int i = t + it * NTH;
+        const int r = i >> 3;
+        const int ch = i & 7;
+        a[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+        b[it] = a[it];
+        if (row0 + r < T) {
+            const float4* s = reinterpret_cast<const float4*>(g + static_cast<long>(row0 + r) * ld + ch * 8);
+            a[it] = __ldg(s);
+            b[it] = __ldg(s + 1);
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < ITEMS; ++it) {
+        const int i = t + it * NTH;
+        const int r = i >> 3;
+        const int ch = i & 7;
+        uint4 h, l;
+        sm100::split2(a[it].x * mul, a[it].y * mul, h.x, l.x);
+        sm100::split2(a[it].z * mul, a[it].w * mul, h.y, l.y);
+        sm100::split2(b[it].x * mul, b[it].y * mul, h.z, l.z);
+        sm100::split2(b[it].z * mul, b[it].w * mul, h.w, l.w);
+        const uint32_t off = sm100::sw128(r, ch);
+        *reinterpret_cast<uint4*>(hi + off) = h;
+        *reinterpret_cast<uint4*>(lo + off) = l;
+    }
+}
+
+}  // namespace tc
+}  // namespace kattn
