@@ -108,6 +108,31 @@ int kattn_bwd(kattn_ctx* ctx,
               float* dq, float* dk, float* dv, long ld_dqkv,
               int B, int T, int H, int d, float scale, int causal, void* stream);
 
+/* Largest B*H*T that kattn_bwd_noalloc accepts (its fixed workspace: 4 MiB
+ * of device memory per GPU that loads the library, held until exit). */
+#define KATTN_NOALLOC_MAX_ROWS (1L << 20)
+
+/* kattn_bwd for callers that cannot allocate device memory: a framework that
+ * accounts for every byte through its own caching allocator, or a runtime
+ * that reserves all device memory up front, cannot let a library take
+ * memory from the device's stream-ordered pool as kattn_bwd does for its
+ * [B][H][T] workspace.  This variant allocates nothing: the workspace is a
+ * fixed array in the library's device image, whose address kattn_create
+ * looks up once per context (so create the context before relying on this
+ * call).  Same arguments, results and launches as kattn_bwd.
+ *   - B*H*T above KATTN_NOALLOC_MAX_ROWS fails with KATTN_ERR_INVALID_ARGUMENT.
+ *   - Every call on a device shares the one array and it keeps the last
+ *     call's contents; each call writes every workspace element it reads
+ *     before reading it, so nothing needs clearing between calls.
+ *   - Calls whose kernels overlap on the GPU (other streams, other threads,
+ *     other contexts on the same device) race on the array: serialise them.
+ * No counterpart in the reference (its CPU and wgpu backends allocate per call). */
+int kattn_bwd_noalloc(kattn_ctx* ctx,
+                      const float* q, const float* k, const float* v, long ld_qkv,
+                      const float* o, const float* dout, long ld_o, const float* lse,
+                      float* dq, float* dk, float* dv, long ld_dqkv,
+                      int B, int T, int H, int d, float scale, int causal, void* stream);
+
 /* Host-buffer forms: same arguments as above, but every pointer is host
  * memory (pinned or pageable).  The call copies inputs to device buffers owned
  * by the context, runs the kernels, copies the outputs back and returns when

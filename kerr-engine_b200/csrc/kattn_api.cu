@@ -23,7 +23,13 @@ struct kattn_ctx {
     std::mutex host_mu;             // serialises the host-buffer entry points
     char* arena = nullptr;          // device staging for the host-buffer entry points
     size_t arena_bytes = 0;
+    float* noalloc_ws = nullptr;    // device address of g_noalloc_ws on this device
 };
+
+// Fixed backward workspace of kattn_bwd_noalloc: [B][H][T] floats, shared by
+// every call on a device.  In host code the name is only a stand-in: the
+// device address comes from cudaGetSymbolAddress (kattn_create, per device).
+static __device__ __align__(256) float g_noalloc_ws[KATTN_NOALLOC_MAX_ROWS];
 
 namespace {
 
@@ -250,6 +256,14 @@ int kattn_create(int device, kattn_ctx** out) {
     }
     // kattn_bwd takes its workspace from the stream-ordered pool: keep freed
     // blocks cached in the pool instead of returning them at each sync.
+    // Device address of the fixed workspace (this device is current here).
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ctx->noalloc_ws), g_noalloc_ws);
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(ctx->stream);
+        cudaFree(ctx->d_status);
+        delete ctx;
+        return cuda_fail(e, "cudaGetSymbolAddress(workspace)");
+    }
     cudaMemPool_t pool;
     if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
         uint64_t keep = UINT64_MAX;
@@ -334,6 +348,30 @@ int kattn_bwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, lo
     cudaError_t ef = cudaFreeAsync(dsum, s);
     if (e != cudaSuccess) return cuda_fail(e, "backward launch");
     if (ef != cudaSuccess) return cuda_fail(ef, "cudaFreeAsync(workspace)");
+    return ok_with_launches(launches);
+}
+
+int kattn_bwd_noalloc(kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv,
+                      const float* o, const float* dout, long ld_o, const float* lse, float* dq, float* dk,
+                      float* dv, long ld_dqkv, int B, int T, int H, int d, float scale, int causal,
+                      void* stream) {
+    g_last_launches = 0;
+    KATTN_TRY(bwd_checks(ctx, q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, B, T, H, d, scale, causal,
+                         true));
+    if (B == 0 || T == 0) return ok_with_launches(0);
+    const long rows = static_cast<long>(B) * H * T;
+    if (rows > KATTN_NOALLOC_MAX_ROWS)
+        return fail(KATTN_ERR_INVALID_ARGUMENT,
+                    "B*H*T = %ld exceeds the fixed workspace of the allocation-free backward (%ld)", rows,
+                    static_cast<long>(KATTN_NOALLOC_MAX_ROWS));
+    KATTN_TRY(path_check(ctx, d));
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, ctx->noalloc_ws,
+                     B, T, H, d, scale, causal};
+    int launches = 0;
+    cudaError_t e = dispatch_bwd(ctx, a, static_cast<cudaStream_t>(stream), &launches);
+    if (e != cudaSuccess) return cuda_fail(e, "backward launch");
     return ok_with_launches(launches);
 }
 

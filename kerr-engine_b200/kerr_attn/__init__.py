@@ -39,7 +39,11 @@ EXPORTED_SYMBOLS = (
     "kattn_version", "kattn_strerror", "kattn_last_error", "kattn_create", "kattn_destroy",
     "kattn_set_path", "kattn_check_device",
     "kattn_fwd", "kattn_bwd", "kattn_fwd_host", "kattn_bwd_host", "kattn_last_launch_count",
+    "kattn_bwd_noalloc",
 )
+
+# Largest B*H*T that kattn_bwd_noalloc accepts (KATTN_NOALLOC_MAX_ROWS).
+NOALLOC_MAX_ROWS = 1 << 20
 
 
 class KattnError(RuntimeError):
@@ -88,6 +92,8 @@ def lib():
     L.kattn_fwd.restype = _i
     L.kattn_bwd.argtypes = bwd_args + [_p]
     L.kattn_bwd.restype = _i
+    L.kattn_bwd_noalloc.argtypes = bwd_args + [_p]
+    L.kattn_bwd_noalloc.restype = _i
     L.kattn_fwd_host.argtypes = fwd_args
     L.kattn_fwd_host.restype = _i
     L.kattn_bwd_host.argtypes = bwd_args
@@ -217,6 +223,30 @@ def bwd(ctx: Context, q, k, v, o, dout, lse, dq, dk, dv, n_head: int, causal: bo
     st = lib().kattn_bwd(ctx.handle, pq, pk, pv, ld, po, pdo, ldo, _vec(lse, "lse"), pdq, pdk, pdv, ldg,
                          B, T, n_head, d, sc, int(causal), _stream_ptr(stream, q.device))
     _check(st, "kattn_bwd")
+    return last_launch_count()
+
+
+def bwd_noalloc(ctx: Context, q, k, v, o, dout, lse, dq, dk, dv, n_head: int, causal: bool = True,
+                scale: float | None = None, stream=None) -> int:
+    """kattn_bwd_noalloc: the backward for callers that cannot allocate device
+    memory; its workspace is the library's fixed device array (B*H*T up to
+    NOALLOC_MAX_ROWS; calls that overlap on the GPU race on it)."""
+    B, T, C = q.shape
+    d = C // n_head
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    pq, ld = _rows(q, "q")
+    pk, ldk = _rows(k, "k")
+    pv, ldv = _rows(v, "v")
+    po, ldo = _rows(o, "o")
+    pdo, ldd_o = _rows(dout, "dout")
+    pdq, ldg = _rows(dq, "dq")
+    pdk, ldgk = _rows(dk, "dk")
+    pdv, ldgv = _rows(dv, "dv")
+    if not (ld == ldk == ldv) or ldo != ldd_o or not (ldg == ldgk == ldgv):
+        raise ValueError("stride groups (q,k,v), (o,dout), (dq,dk,dv) must each share one row stride")
+    st = lib().kattn_bwd_noalloc(ctx.handle, pq, pk, pv, ld, po, pdo, ldo, _vec(lse, "lse"), pdq, pdk, pdv, ldg,
+                                 B, T, n_head, d, sc, int(causal), _stream_ptr(stream, q.device))
+    _check(st, "kattn_bwd_noalloc")
     return last_launch_count()
 
 
