@@ -11,19 +11,29 @@
 //   dP^T = V dO^T     M=128 N=64                    SS, both K-major
 //   P = exp2(S^T * scale*log2e - lse*log2e),  dS = P * (dP^T - D)   (threads)
 //   dV  += P^T dO     M=128 N=64 K=64    TS: P from TMEM, dO MN-major
-//   dK  += dS^T Q     M=128 N=64 K=64    SS: dS^T K-major, Q MN-major
-//   dQ_i = dS K       M=64  N=64 K=128   SS: dS^T read MN-major, K MN-major;
+//   dK  += dS^T Q     M=128 N=64 K=64    TS: dS from TMEM, Q MN-major
+//   dQ_i = dS K       M=64  N=64 K=128   SS: dS^T (shared) read MN-major, K MN-major;
 //                     added into global dq with vector reductions.
 // D = rowsum(dO * O) and the zeroed dq come from attn_bwd_rowdot.
 //
-// Warp roles (288 threads, one CTA per SM):
-//   warps 0-3  elementwise: thread t owns key row t (TMEM lane t); also the
-//              dQ and final dK / dV epilogues
-//   warps 4-7  loaders: K, V once; then Q, dO, lse, D per query tile into a
-//              2-stage ring (full / empty mbarriers)
-//   warp 8     one lane issues every tcgen05.mma and commit
-// S^T / dP^T are double-buffered in TMEM so the tensor core computes tile
-// i+1 while the elementwise warps work on tile i.
+// Warp roles (416 threads, one CTA per SM):
+//   warps 0-7   elementwise.  Warp w reads TMEM lanes 32*(w%4).. (key rows)
+//               and query columns 32*(w/4)..+31 of each 64-column tile; it
+//               also adds its half of the dQ tile into dq and, at the end,
+//               stores its half of the dK / dV rows.
+//   warps 8-11  loaders: Q, dO, lse, D per query tile into a 3-stage ring.
+//   warp 12     one lane issues every tcgen05.mma and commit, from
+//               descriptors built once, in whichever order its inputs become
+//               ready (a tile's S^T / dP^T as soon as the tile is loaded and
+//               its TMEM buffer is free; a tile's gradients as soon as its P
+//               and dS are written).
+// Everything a query tile touches is double-buffered (S^T / dP^T in TMEM,
+// dS^T in shared memory, the dQ accumulator in TMEM), so the tensor core runs
+// tile i's gradient products while the elementwise warps work on tile i+1.
+// P and dS are packed over their own S^T / dP^T columns: for query columns
+// 32h..32h+31, bf16 hi goes to columns 32h..32h+15 and lo to 32h+16..32h+31,
+// which the owning warp has already read; the tensor core runs one thread's
+// MMAs in issue order, so the next S^T lands only after dV / dK read them.
 #include <atomic>
 
 #include "kattn_common.cuh"
@@ -39,16 +49,17 @@ namespace {
 constexpr int BK = 128;  // key rows per CTA
 constexpr int BQ = 64;   // query rows per tile
 constexpr int D = 64;
-constexpr int NCOMP = 128;
-constexpr int NLOAD = 128;
-constexpr int NTHREADS = NCOMP + NLOAD + 32;
+constexpr int NELEM = 256;  // elementwise threads (warps 0-7)
+constexpr int NLOAD = 128;  // loader threads (warps 8-11)
+constexpr int NTHREADS = NELEM + NLOAD + 32;
+constexpr int MMA_WARP = (NELEM + NLOAD) / 32;
+constexpr int STAGES = 3;  // query-tile ring depth (Q, dO, lse, D)
 
-// TMEM columns (512 allocated)
-__device__ __forceinline__ uint32_t col_s(int s) { return s ? 128u : 0u; }
-__device__ __forceinline__ uint32_t col_dp(int s) { return s ? 192u : 64u; }
-constexpr uint32_t COL_PH = 256;  // P^T hi: 64 queries as 32 bf16x2 columns
-constexpr uint32_t COL_PL = 288;  // P^T lo
-constexpr uint32_t COL_DQ = 320;  // dQ tile (M=64 layout)
+// TMEM columns (512 allocated).  Buffer b: S^T (then P packed) at col_s(b),
+// dP^T (then dS packed) at col_dp(b), dQ tile (M=64 layout) at col_dq(b).
+__device__ __forceinline__ uint32_t col_s(int b) { return b ? 128u : 0u; }
+__device__ __forceinline__ uint32_t col_dp(int b) { return b ? 192u : 64u; }
+__device__ __forceinline__ uint32_t col_dq(int b) { return b ? 320u : 256u; }
 constexpr uint32_t COL_DV = 384;
 constexpr uint32_t COL_DK = 448;
 constexpr uint32_t TMEM_COLS = 512;
@@ -58,22 +69,24 @@ struct alignas(1024) Smem {
     uint8_t kl[BK * 128];
     uint8_t vh[BK * 128];
     uint8_t vl[BK * 128];
-    uint8_t qh[2][BQ * 128];  // [query][64 bf16]
-    uint8_t ql[2][BQ * 128];
-    uint8_t gh[2][BQ * 128];  // dO
-    uint8_t gl[2][BQ * 128];
-    uint8_t sh[BK * 128];  // dS^T [key][64 queries]
-    uint8_t sl[BK * 128];
-    float lse2[2][BQ];  // lse * log2(e), +inf beyond T
-    float dsum[2][BQ];  // D, 0 beyond T
+    uint8_t qh[STAGES][BQ * 128];  // [query][64 bf16]
+    uint8_t ql[STAGES][BQ * 128];
+    uint8_t gh[STAGES][BQ * 128];  // dO
+    uint8_t gl[STAGES][BQ * 128];
+    uint8_t sh[2][BK * 128];  // dS^T [key][64 queries], per TMEM buffer
+    uint8_t sl[2][BK * 128];
+    float lse2[STAGES][BQ];  // lse * log2(e), +inf beyond T
+    float dsum[STAGES][BQ];  // D, 0 beyond T
     uint64_t kv_full;
-    uint64_t full[2];
-    uint64_t empty[2];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
     uint64_t bar_s[2];
-    uint64_t pds;
-    uint64_t bar_d;
+    uint64_t pds[2];  // P / dS of the tile in buffer b written
+    uint64_t bar_d[2];
     uint32_t tmem_slot;
 };
+
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory (plus alignment slack) exceeds 227 KB");
 
 struct Params {
     const float* q;
@@ -97,75 +110,106 @@ struct Params {
     int n_qtiles;  // 64-row query tiles
 };
 
-// S^T and dP^T of the query tile in stage s into TMEM buffer s.
-__device__ __forceinline__ void issue_sdp(const Smem& sm, uint32_t tm, int s) {
+// Shared-memory descriptors, built once by the issuing thread (two ring
+// stages / two buffers, selected without indexing so they stay in registers).
+// A K-major k-step advances 32 bytes inside the swizzled row; an MN-major
+// k-step advances 16 rows (2048 bytes).  The K-major and MN-major
+// descriptors of one tile differ only in the leading-byte offset.
+struct Descs {
+    uint64_t kh, kl, vh, vl;      // K / V, K-major (S^T, dP^T A operands)
+    uint64_t kh_mn, kl_mn;        // K, MN-major (dQ B operand)
+    uint64_t qh, ql, gh, gl;      // Q / dO ring stage 0, K-major; stage s is STAGE_BYTES * s further
+    uint64_t s0h, s0l, s1h, s1l;  // dS^T buffer 0 / 1, MN-major (dQ A)
+};
+
+constexpr uint32_t STAGE_BYTES = BQ * 128;  // one stage of one Q / dO tile
+constexpr uint32_t MN_LBO_Q = BQ * 128;     // leading-byte offset of a 64-row MN-major tile
+constexpr uint32_t MN_LBO_K = BK * 128;
+
+__device__ __forceinline__ uint64_t as_mn(uint64_t kdesc, uint32_t lbo) {
+    return (kdesc & ~(static_cast<uint64_t>(0x3FFFu) << 16)) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16);
+}
+
+__device__ __forceinline__ void make_descs(const Smem& sm, Descs& d) {
+    d.kh = smem_desc(smem_u32(sm.kh), 16, 1024);
+    d.kl = smem_desc(smem_u32(sm.kl), 16, 1024);
+    d.vh = smem_desc(smem_u32(sm.vh), 16, 1024);
+    d.vl = smem_desc(smem_u32(sm.vl), 16, 1024);
+    d.kh_mn = as_mn(d.kh, MN_LBO_K);
+    d.kl_mn = as_mn(d.kl, MN_LBO_K);
+    d.qh = smem_desc(smem_u32(sm.qh[0]), 16, 1024);
+    d.ql = smem_desc(smem_u32(sm.ql[0]), 16, 1024);
+    d.gh = smem_desc(smem_u32(sm.gh[0]), 16, 1024);
+    d.gl = smem_desc(smem_u32(sm.gl[0]), 16, 1024);
+    d.s0h = smem_desc(smem_u32(sm.sh[0]), MN_LBO_K, 1024);
+    d.s0l = smem_desc(smem_u32(sm.sl[0]), MN_LBO_K, 1024);
+    d.s1h = smem_desc(smem_u32(sm.sh[1]), MN_LBO_K, 1024);
+    d.s1l = smem_desc(smem_u32(sm.sl[1]), MN_LBO_K, 1024);
+}
+
+// S^T and dP^T of the query tile in ring stage s into TMEM buffer b.
+__device__ __forceinline__ void issue_sdp(const Descs& d, uint32_t tm, int s, int b) {
     constexpr uint32_t idesc = idesc_bf16(BK, BQ, 0, 0);
-    const uint32_t kh = smem_u32(sm.kh), kl = smem_u32(sm.kl), vh = smem_u32(sm.vh), vl = smem_u32(sm.vl);
-    const uint32_t qh = smem_u32(sm.qh[s]), ql = smem_u32(sm.ql[s]), gh = smem_u32(sm.gh[s]), gl = smem_u32(sm.gl[s]);
+    const uint32_t cs = tm + col_s(b), cp = tm + col_dp(b);
+    const uint32_t so = s * STAGE_BYTES;
+    const uint64_t qh = desc_add(d.qh, so), ql = desc_add(d.ql, so);
+    const uint64_t gh = desc_add(d.gh, so), gl = desc_add(d.gl, so);
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
         const uint32_t o = ks * 32;
-        const uint64_t akh = smem_desc(kh + o, 16, 1024), akl = smem_desc(kl + o, 16, 1024);
-        const uint64_t bqh = smem_desc(qh + o, 16, 1024), bql = smem_desc(ql + o, 16, 1024);
-        mma_ss(tm + col_s(s), akh, bqh, idesc, ks > 0);
-        mma_ss(tm + col_s(s), akh, bql, idesc, 1);
-        mma_ss(tm + col_s(s), akl, bqh, idesc, 1);
-        const uint64_t avh = smem_desc(vh + o, 16, 1024), avl = smem_desc(vl + o, 16, 1024);
-        const uint64_t bgh = smem_desc(gh + o, 16, 1024), bgl = smem_desc(gl + o, 16, 1024);
-        mma_ss(tm + col_dp(s), avh, bgh, idesc, ks > 0);
-        mma_ss(tm + col_dp(s), avh, bgl, idesc, 1);
-        mma_ss(tm + col_dp(s), avl, bgh, idesc, 1);
+        mma_ss(cs, desc_add(d.kh, o), desc_add(qh, o), idesc, ks > 0);
+        mma_ss(cs, desc_add(d.kh, o), desc_add(ql, o), idesc, 1);
+        mma_ss(cs, desc_add(d.kl, o), desc_add(qh, o), idesc, 1);
+        mma_ss(cp, desc_add(d.vh, o), desc_add(gh, o), idesc, ks > 0);
+        mma_ss(cp, desc_add(d.vh, o), desc_add(gl, o), idesc, 1);
+        mma_ss(cp, desc_add(d.vl, o), desc_add(gh, o), idesc, 1);
     }
 }
 
-// dV += P^T dO, dK += dS^T Q (stage s), dQ = dS K.
-__device__ __forceinline__ void issue_grads(const Smem& sm, uint32_t tm, int s, bool first) {
+// dV += P^T dO, dK += dS^T Q (ring stage s, buffer b), dQ_b = dS K.
+__device__ __forceinline__ void issue_grads(const Descs& d, uint32_t tm, int s, int b, bool first) {
     constexpr uint32_t idesc_kv = idesc_bf16(BK, D, 0, 1);
     constexpr uint32_t idesc_q = idesc_bf16(BQ, D, 1, 1);
-    const uint32_t qh = smem_u32(sm.qh[s]), ql = smem_u32(sm.ql[s]), gh = smem_u32(sm.gh[s]), gl = smem_u32(sm.gl[s]);
-    const uint32_t sh = smem_u32(sm.sh), sl = smem_u32(sm.sl);
+    const uint32_t so = s * STAGE_BYTES;
+    const uint64_t qh = as_mn(desc_add(d.qh, so), MN_LBO_Q), ql = as_mn(desc_add(d.ql, so), MN_LBO_Q);
+    const uint64_t gh = as_mn(desc_add(d.gh, so), MN_LBO_Q), gl = as_mn(desc_add(d.gl, so), MN_LBO_Q);
 #pragma unroll
     for (int ks = 0; ks < BQ / 16; ++ks) {
         const uint32_t acc = (first && ks == 0) ? 0u : 1u;
-        const uint64_t bgh = smem_desc(gh + ks * 2048, BQ * 128, 1024), bgl = smem_desc(gl + ks * 2048, BQ * 128, 1024);
-        mma_ts(tm + COL_DV, tm + COL_PH + ks * 8, bgh, idesc_kv, acc);
-        mma_ts(tm + COL_DV, tm + COL_PH + ks * 8, bgl, idesc_kv, 1);
-        mma_ts(tm + COL_DV, tm + COL_PL + ks * 8, bgh, idesc_kv, 1);
-        const uint64_t ash = smem_desc(sh + ks * 32, 16, 1024), asl = smem_desc(sl + ks * 32, 16, 1024);
-        const uint64_t bqh = smem_desc(qh + ks * 2048, BQ * 128, 1024), bql = smem_desc(ql + ks * 2048, BQ * 128, 1024);
-        mma_ss(tm + COL_DK, ash, bqh, idesc_kv, acc);
-        mma_ss(tm + COL_DK, ash, bql, idesc_kv, 1);
-        mma_ss(tm + COL_DK, asl, bqh, idesc_kv, 1);
+        const uint32_t pk = 32 * (ks >> 1) + 8 * (ks & 1);  // packed column of this 16-query step
+        const uint32_t o = ks * 2048;
+        const uint32_t ph = tm + col_s(b) + pk, gph = tm + col_dp(b) + pk;
+        mma_ts(tm + COL_DV, ph, desc_add(gh, o), idesc_kv, acc);
+        mma_ts(tm + COL_DV, ph, desc_add(gl, o), idesc_kv, 1);
+        mma_ts(tm + COL_DV, ph + 16, desc_add(gh, o), idesc_kv, 1);
+        mma_ts(tm + COL_DK, gph, desc_add(qh, o), idesc_kv, acc);
+        mma_ts(tm + COL_DK, gph, desc_add(ql, o), idesc_kv, 1);
+        mma_ts(tm + COL_DK, gph + 16, desc_add(qh, o), idesc_kv, 1);
     }
-    const uint32_t kh = smem_u32(sm.kh), kl = smem_u32(sm.kl);
+    const uint32_t cq = tm + col_dq(b);
+    const uint64_t sh = b ? d.s1h : d.s0h, sl = b ? d.s1l : d.s0l;
 #pragma unroll
     for (int ks = 0; ks < BK / 16; ++ks) {
-        const uint64_t ash = smem_desc(sh + ks * 2048, BK * 128, 1024), asl = smem_desc(sl + ks * 2048, BK * 128, 1024);
-        const uint64_t bkh = smem_desc(kh + ks * 2048, BK * 128, 1024), bkl = smem_desc(kl + ks * 2048, BK * 128, 1024);
-        mma_ss(tm + COL_DQ, ash, bkh, idesc_q, ks > 0);
-        mma_ss(tm + COL_DQ, ash, bkl, idesc_q, 1);
-        mma_ss(tm + COL_DQ, asl, bkh, idesc_q, 1);
+        const uint32_t o = ks * 2048;
+        mma_ss(cq, desc_add(sh, o), desc_add(d.kh_mn, o), idesc_q, ks > 0);
+        mma_ss(cq, desc_add(sh, o), desc_add(d.kl_mn, o), idesc_q, 1);
+        mma_ss(cq, desc_add(sl, o), desc_add(d.kh_mn, o), idesc_q, 1);
     }
 }
 
-// dQ tile (M=64 accumulator: query row 16w + l sits in lane 32w + l, l < 16)
-// scaled and added into global dq.
-__device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int warp, int lane, int q0, float* dqg) {
-    float v0[32], v1[32];
-    const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
-    tmem_ld32(lb + tm + COL_DQ, v0);
-    tmem_ld32(lb + tm + COL_DQ + 32, v1);
+// Half of a dQ tile (M=64 accumulator: query row 16*qd + l sits in lane
+// 32*qd + l, l < 16), columns 32*half..+31, scaled and added into dq.
+__device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int half, int lane,
+                                            int q0, float* dqg) {
+    float v[32];
+    tmem_ld32((static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b) + 32 * half, v);
     tmem_wait_ld();
-    const int r = q0 + warp * 16 + lane;
+    const int r = q0 + qd * 16 + lane;
     if (lane < 16 && r < p.T) {
-        float* dst = dqg + static_cast<long>(r) * p.ld_d;
+        float* dst = dqg + static_cast<long>(r) * p.ld_d + 32 * half;
 #pragma unroll
         for (int c = 0; c < 32; c += 4)
-            red_add_v4(dst + c, v0[c] * p.scale, v0[c + 1] * p.scale, v0[c + 2] * p.scale, v0[c + 3] * p.scale);
-#pragma unroll
-        for (int c = 0; c < 32; c += 4)
-            red_add_v4(dst + 32 + c, v1[c] * p.scale, v1[c + 1] * p.scale, v1[c + 2] * p.scale,
-                       v1[c + 3] * p.scale);
+            red_add_v4(dst + c, v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale, v[c + 3] * p.scale);
     }
 }
 
@@ -199,15 +243,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         tmem_relinquish();
     }
     if (tid == 0) {
-        mbar_init(&sm.kv_full, NLOAD);
-        mbar_init(&sm.full[0], NLOAD);
-        mbar_init(&sm.full[1], NLOAD);
-        mbar_init(&sm.empty[0], 1);
-        mbar_init(&sm.empty[1], 1);
-        mbar_init(&sm.bar_s[0], 1);
-        mbar_init(&sm.bar_s[1], 1);
-        mbar_init(&sm.pds, NCOMP);
-        mbar_init(&sm.bar_d, 1);
+        mbar_init(&sm.kv_full, NELEM);
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&sm.full[i], NLOAD);
+            mbar_init(&sm.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.bar_s[i], 1);
+            mbar_init(&sm.bar_d[i], 1);
+        }
+        mbar_init(&sm.pds[0], NELEM);
+        mbar_init(&sm.pds[1], NELEM);
     }
     tc_fence_before();
     __syncthreads();
@@ -215,154 +261,184 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     const uint32_t tm = sm.tmem_slot;
     bool failed = false;
 
-    if (warp >= 4 && warp < 8) {
+    if (warp >= NELEM / 32 && warp < MMA_WARP) {
         // ------------------------------------------------------------ loaders
-        const int t = tid - NCOMP;
-        tc::stage_rows<BK, NLOAD>(sm.kh, sm.kl, kg, p.ld_qkv, k0, p.T, 1.f, t);
-        tc::stage_rows<BK, NLOAD>(sm.vh, sm.vl, vg, p.ld_qkv, k0, p.T, 1.f, t);
-        fence_async_smem();
-        mbar_arrive(&sm.kv_full);
+        const int t = tid - NELEM;
         for (int n = 0; n < n_it; ++n) {
-            const int s = n & 1;
+            const int s = n % STAGES;
             const int q0 = (it0 + n) * BQ;
-            if (n >= 2 && !mbar_wait(&sm.empty[s], ((n - 2) >> 1) & 1)) {
+            if (n >= STAGES && !mbar_wait(&sm.empty[s], ((n - STAGES) / STAGES) & 1)) {
                 failed = true;
                 break;
             }
-            tc::stage_rows<BQ, NLOAD>(sm.qh[s], sm.ql[s], qg, p.ld_qkv, q0, p.T, 1.f, t);
-            tc::stage_rows<BQ, NLOAD>(sm.gh[s], sm.gl[s], dog, p.ld_o, q0, p.T, 1.f, t);
             if (t < BQ) {
                 const bool ok = q0 + t < p.T;
                 sm.lse2[s][t] = ok ? lseg[q0 + t] * kLog2e : INFINITY;
                 sm.dsum[s][t] = ok ? dsg[q0 + t] : 0.f;
             }
+            tc::stage_rows2<BQ, NLOAD>(sm.qh[s], sm.ql[s], qg, p.ld_qkv, sm.gh[s], sm.gl[s], dog, p.ld_o, q0, p.T, t);
             fence_async_smem();
             mbar_arrive(&sm.full[s]);
         }
-    } else if (warp == 8) {
+    } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
+            Descs d;
+            make_descs(sm, d);
             failed = !mbar_wait(&sm.kv_full, 0);
-            for (int n = 0; n < 2 && n < n_it && !failed; ++n) {
-                if (!mbar_wait(&sm.full[n], 0)) {
-                    failed = true;
-                    break;
-                }
-                tc_fence_after();
-                issue_sdp(sm, tm, n);
-                mma_commit(&sm.bar_s[n]);
-            }
-            for (int n = 0; n < n_it && !failed; ++n) {
-                const int s = n & 1;
-                if (!mbar_wait(&sm.pds, n & 1)) {
-                    failed = true;
-                    break;
-                }
-                tc_fence_after();
-                issue_grads(sm, tm, s, n == 0);
-                mma_commit(&sm.empty[s]);
-                mma_commit(&sm.bar_d);
-                if (n + 2 < n_it) {
-                    if (!mbar_wait(&sm.full[s], ((n + 2) >> 1) & 1)) {
-                        failed = true;
-                        break;
-                    }
+            // sdp(n) needs tile n loaded and, for n >= 2, grads(n-2) issued
+            // (TMEM buffer n&1; the tensor core runs this thread's MMAs in
+            // order).  grads(n) needs P / dS of tile n written.
+            int ns = 0, ng = 0;
+            uint64_t t_idle = 0;
+            while (ng < n_it && !failed) {
+                bool progressed = false;
+                if (ns < n_it && ns < ng + 2 && mbar_try_wait(&sm.full[ns % STAGES], (ns / STAGES) & 1)) {
                     tc_fence_after();
-                    issue_sdp(sm, tm, s);
-                    mma_commit(&sm.bar_s[s]);
+                    issue_sdp(d, tm, ns % STAGES, ns & 1);
+                    mma_commit(&sm.bar_s[ns & 1]);
+                    ++ns;
+                    progressed = true;
+                }
+                if (ng < ns && mbar_try_wait(&sm.pds[ng & 1], (ng >> 1) & 1)) {
+                    tc_fence_after();
+                    issue_grads(d, tm, ng % STAGES, ng & 1, ng == 0);
+                    mma_commit(&sm.empty[ng % STAGES]);
+                    mma_commit(&sm.bar_d[ng & 1]);
+                    ++ng;
+                    progressed = true;
+                }
+                if (progressed) {
+                    t_idle = 0;
+                } else {
+                    const uint64_t now = globaltimer_ns();
+                    if (t_idle == 0) t_idle = now;
+                    else if (now - t_idle > 1000000000ull) failed = true;
+                    __nanosleep(20);
                 }
             }
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------------------ elementwise (key row j)
-        const int j = k0 + tid;
-        const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
+        // ------------------------------------------------------------ elementwise
+        const int qd = warp & 3;          // TMEM lane quadrant: key rows 32*qd..
+        const int half = warp >> 2;       // query columns 32*half..+31
+        const int row = qd * 32 + lane;   // key row inside the tile
+        const int j = k0 + row;
+        const uint32_t lb = static_cast<uint32_t>(qd * 32) << 16;
+        tc::stage_rows2<BK, NELEM>(sm.kh, sm.kl, kg, p.ld_qkv, sm.vh, sm.vl, vg, p.ld_qkv, k0, p.T, tid);
+        fence_async_smem();
+        mbar_arrive(&sm.kv_full);
+
         for (int n = 0; n < n_it; ++n) {
-            const int s = n & 1;
+            const int s = n % STAGES;  // ring stage of this query tile
+            const int buf = n & 1;     // TMEM / dS buffer
             const int q0 = (it0 + n) * BQ;
             // full[s]: the loaders' lse / D writes for this tile are visible.
-            if (!mbar_wait_warp(&sm.bar_s[s], (n >> 1) & 1) || !mbar_wait_warp(&sm.full[s], (n >> 1) & 1)) {
+            if (!mbar_wait_warp(&sm.bar_s[buf], (n >> 1) & 1) || !mbar_wait_warp(&sm.full[s], (n / STAGES) & 1)) {
                 failed = true;
                 break;
             }
-            if (n > 0) {
-                // dQ of the previous tile; its MMAs also finished reading P^T and dS^T.
-                if (!mbar_wait_warp(&sm.bar_d, (n - 1) & 1)) {
-                    failed = true;
-                    break;
-                }
-                tc_fence_after();
-                dq_epilogue(p, tm, warp, lane, q0 - BQ, dqg);
+            if (n >= 2 && !mbar_wait_warp(&sm.bar_d[buf], ((n - 2) >> 1) & 1)) {
+                failed = true;  // dS^T buffer `buf` is read by tile n-2's dQ product
+                break;
             }
             tc_fence_after();
             const bool need_mask = (p.causal && q0 < k0 + BK - 1) || q0 + BQ > p.T || k0 + BK > p.T;
+            // Valid query columns of this key row in this warp's half: bit i set
+            // when query q0 + 32*half + i attends to key j (causal: q >= j) and
+            // both are below T.
+            uint32_t vmask = 0xffffffffu;
+            if (need_mask) {
+                const int c0 = q0 + 32 * half;
+                const int lo = p.causal ? max(0, j - c0) : 0;
+                const int hi = (j < p.T) ? min(32, p.T - c0) : 0;
+                vmask = (lo >= hi) ? 0u : ((hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~((lo >= 32) ? 0xffffffffu : ((1u << lo) - 1u)));
+            }
+            const uint32_t cs = lb + tm + col_s(buf) + 32 * half, cp = lb + tm + col_dp(buf) + 32 * half;
+            float sv[32], dp[32];
+            tmem_ld32(cs, sv);
+            tmem_ld32(cp, dp);
+            tmem_wait_ld();
+            uint32_t ph[16], pl[16], gh[16], gl[16];
+            const float4* l4 = reinterpret_cast<const float4*>(&sm.lse2[s][32 * half]);
+            const float4* d4 = reinterpret_cast<const float4*>(&sm.dsum[s][32 * half]);
 #pragma unroll
-            for (int c = 0; c < BQ; c += 32) {
-                float sv[32], dp[32];
-                tmem_ld32(lb + tm + col_s(s) + c, sv);
-                tmem_ld32(lb + tm + col_dp(s) + c, dp);
-                tmem_wait_ld();
-                uint32_t ph[16], pl[16], gh[16], gl[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    float p0 = ex2(fmaf(sv[i], p.scale_log2, -sm.lse2[s][c + i]));
-                    float p1 = ex2(fmaf(sv[i + 1], p.scale_log2, -sm.lse2[s][c + i + 1]));
-                    if (need_mask) {
-                        const int qi = q0 + c + i;
-                        if ((p.causal && qi < j) || qi >= p.T || j >= p.T) p0 = 0.f;
-                        if ((p.causal && qi + 1 < j) || qi + 1 >= p.T || j >= p.T) p1 = 0.f;
-                    }
-                    const float g0 = p0 * (dp[i] - sm.dsum[s][c + i]);
-                    const float g1 = p1 * (dp[i + 1] - sm.dsum[s][c + i + 1]);
-                    split2(p0, p1, ph[i >> 1], pl[i >> 1]);
-                    split2(g0, g1, gh[i >> 1], gl[i >> 1]);
-                }
-                tmem_st16(lb + tm + COL_PH + c / 2, ph);
-                tmem_st16(lb + tm + COL_PL + c / 2, pl);
+            for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 lv = l4[i4], dv = d4[i4];
+                const float lse_[4] = {lv.x, lv.y, lv.z, lv.w};
+                const float ds_[4] = {dv.x, dv.y, dv.z, dv.w};
+                float pr[4], gr[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const uint32_t off = sw128(tid, c / 8 + u);
-                    *reinterpret_cast<uint4*>(sm.sh + off) =
-                        make_uint4(gh[4 * u], gh[4 * u + 1], gh[4 * u + 2], gh[4 * u + 3]);
-                    *reinterpret_cast<uint4*>(sm.sl + off) =
-                        make_uint4(gl[4 * u], gl[4 * u + 1], gl[4 * u + 2], gl[4 * u + 3]);
+                    const int i = 4 * i4 + u;
+                    float pv = ex2(fmaf(sv[i], p.scale_log2, -lse_[u]));
+                    pv = ((vmask >> i) & 1u) ? pv : 0.f;
+                    pr[u] = pv;
+                    gr[u] = pv * (dp[i] - ds_[u]);
                 }
+                split2(pr[0], pr[1], ph[2 * i4], pl[2 * i4]);
+                split2(pr[2], pr[3], ph[2 * i4 + 1], pl[2 * i4 + 1]);
+                split2(gr[0], gr[1], gh[2 * i4], gl[2 * i4]);
+                split2(gr[2], gr[3], gh[2 * i4 + 1], gl[2 * i4 + 1]);
+            }
+            // P and dS packed over the columns just read (see the header).
+            tmem_st16(cs, ph);
+            tmem_st16(cs + 16, pl);
+            tmem_st16(cp, gh);
+            tmem_st16(cp + 16, gl);
+            // dS^T row for the dQ product: query chunks 4*half..4*half+3.
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t off = sw128(row, 4 * half + u);
+                *reinterpret_cast<uint4*>(sm.sh[buf] + off) =
+                    make_uint4(gh[4 * u], gh[4 * u + 1], gh[4 * u + 2], gh[4 * u + 3]);
+                *reinterpret_cast<uint4*>(sm.sl[buf] + off) =
+                    make_uint4(gl[4 * u], gl[4 * u + 1], gl[4 * u + 2], gl[4 * u + 3]);
             }
             tmem_wait_st();
             fence_async_smem();
             tc_fence_before();
-            mbar_arrive(&sm.pds);
+            mbar_arrive(&sm.pds[buf]);
+            if (n >= 1) {
+                // dQ of the previous tile, while the tensor core works on this one.
+                const int pb = (n - 1) & 1;
+                if (!mbar_wait_warp(&sm.bar_d[pb], ((n - 1) >> 1) & 1)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                dq_epilogue(p, tm, pb, qd, half, lane, q0 - BQ, dqg);
+                tc_fence_before();
+            }
         }
         if (!failed) {
-            if (!mbar_wait_warp(&sm.bar_d, (n_it - 1) & 1)) {
+            const int lbuf = (n_it - 1) & 1;
+            if (!mbar_wait_warp(&sm.bar_d[lbuf], ((n_it - 1) >> 1) & 1)) {
                 failed = true;
             } else {
                 tc_fence_after();
-                dq_epilogue(p, tm, warp, lane, (it0 + n_it - 1) * BQ, dqg);
-                // dK, dV for this key row: the TMEM loads are warp-collective and
-                // run on every lane; only rows below T are stored.
-                float* dkr = p.dk + (base + j) * p.ld_d + h * D;
-                float* dvr = p.dv + (base + j) * p.ld_d + h * D;
-                const bool store = j < p.T;
+                dq_epilogue(p, tm, lbuf, qd, half, lane, (it0 + n_it - 1) * BQ, dqg);
+                // dK, dV columns 32*half..+31 of this key row.  The TMEM loads are
+                // warp-collective and run on every lane; rows past T are not stored.
                 float a[32];
+                const bool store = j < p.T;
+                float* dvr = p.dv + (base + j) * p.ld_d + h * D + 32 * half;
+                float* dkr = p.dk + (base + j) * p.ld_d + h * D + 32 * half;
+                tmem_ld32(lb + tm + COL_DV + 32 * half, a);
+                tmem_wait_ld();
+                if (store) {
 #pragma unroll
-                for (int c = 0; c < D; c += 32) {
-                    tmem_ld32(lb + tm + COL_DV + c, a);
-                    tmem_wait_ld();
-                    if (store) {
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(dvr + i) = make_float4(a[i], a[i + 1], a[i + 2], a[i + 3]);
+                }
+                tmem_ld32(lb + tm + COL_DK + 32 * half, a);
+                tmem_wait_ld();
+                if (store) {
 #pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            *reinterpret_cast<float4*>(dvr + c + i) = make_float4(a[i], a[i + 1], a[i + 2], a[i + 3]);
-                    }
-                    tmem_ld32(lb + tm + COL_DK + c, a);
-                    tmem_wait_ld();
-                    if (store) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            *reinterpret_cast<float4*>(dkr + c + i) = make_float4(
-                                a[i] * p.scale, a[i + 1] * p.scale, a[i + 2] * p.scale, a[i + 3] * p.scale);
-                    }
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(dkr + i) =
+                            make_float4(a[i] * p.scale, a[i + 1] * p.scale, a[i + 2] * p.scale, a[i + 3] * p.scale);
                 }
             }
         }
@@ -407,7 +483,7 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static std::atomic<uint64_t> attr_done{0};
+    static std::atomic<uint64_t> attr_done{0};  // one bit per device: the attribute is per device
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_done.load(std::memory_order_relaxed) & bit)) {
         e = cudaFuncSetAttribute(attn_bwd_tc64, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

@@ -8,13 +8,14 @@
 //
 // CTA = 128 query rows of one (batch, head) slab, 128 threads; thread t owns
 // query row t (TMEM lane t).  Per 64-row key tile j:
-//   S_j = Q K_j^T           tcgen05.mma SS, M=128 N=64, 3 x 4 k-steps   -> TMEM
-//   softmax (online, log2 domain) in registers; P_j hi/lo -> TMEM
-//   O_j = P_j V_j           tcgen05.mma TS (P from TMEM), V MN-major    -> TMEM
-//   O  <- O * alpha + O_j   in registers
-// S_{j+1} is issued right behind O_j, so the tensor core computes it while the
-// threads fold O_j in and stage key/value tile j+2.  ~99 KB of shared memory
-// and 256 TMEM columns per CTA: two CTAs share an SM.
+//   S_j = Q K_j^T        tcgen05.mma SS, M=128 N=64, 3 x 4 k-steps -> TMEM buffer j&1
+//   softmax (online, log2 domain) in registers; P_j hi/lo written over S_j
+//   O_j = P_j V_j        tcgen05.mma TS (P from TMEM), V MN-major  -> TMEM buffer j&1
+//   O <- O * alpha + O_j in registers, one tile later
+// PV_j and S_{j+1} are issued together; while they run the threads fold in
+// O_{j-1} and stage K_{j+2} and V_{j+1} (K and V tiles have separate
+// lifetimes: K_j is free once S_j is done, V_j once PV_j is).  ~99 KB of
+// shared memory and 256 TMEM columns per CTA: two CTAs share an SM.
 #include <atomic>
 
 #include "kattn_common.cuh"
@@ -32,11 +33,11 @@ constexpr int BN = 64;   // key rows per tile
 constexpr int NT = 128;
 constexpr int D = 64;
 
-// TMEM columns
-constexpr uint32_t COL_S = 0;    // S tile, 64 f32 columns
-constexpr uint32_t COL_PH = 64;  // P hi, 64 bf16 packed in 32 columns
-constexpr uint32_t COL_PL = 96;  // P lo
-constexpr uint32_t COL_O = 128;  // O tile, 64 f32 columns
+// TMEM columns.  Buffer b: S at col_s(b) (64 f32 columns; P packed over it:
+// for key columns 32c..32c+31, bf16 hi in columns 32c..32c+15 and lo in
+// 32c+16..32c+31), the P V tile at col_o(b) (64 f32 columns).
+__device__ __forceinline__ uint32_t col_s(int b) { return b ? 64u : 0u; }
+__device__ __forceinline__ uint32_t col_o(int b) { return b ? 192u : 128u; }
 constexpr uint32_t TMEM_COLS = 256;
 
 struct alignas(1024) Smem {
@@ -46,8 +47,8 @@ struct alignas(1024) Smem {
     uint8_t kl[2][BN * 128];
     uint8_t vh[2][BN * 128];
     uint8_t vl[2][BN * 128];
-    uint64_t bar_s;
-    uint64_t bar_o;
+    uint64_t bar_s[2];
+    uint64_t bar_o[2];
     uint32_t tmem_slot;
 };
 
@@ -67,30 +68,50 @@ struct Params {
     int n_ktiles;
 };
 
-__device__ __forceinline__ void issue_s(const Smem& sm, uint32_t tm, int stage) {
+// Shared-memory descriptors of the Q tile and of K / V stage 0 (stage 1 is
+// STAGE_BYTES further), built once by the issuing thread.
+constexpr uint32_t STAGE_BYTES = BN * 128;
+struct Descs {
+    uint64_t qh, ql, kh, kl, vh, vl;
+};
+
+__device__ __forceinline__ Descs make_descs(const Smem& sm) {
+    Descs d;
+    d.qh = smem_desc(smem_u32(sm.qh), 16, 1024);
+    d.ql = smem_desc(smem_u32(sm.ql), 16, 1024);
+    d.kh = smem_desc(smem_u32(sm.kh[0]), 16, 1024);
+    d.kl = smem_desc(smem_u32(sm.kl[0]), 16, 1024);
+    d.vh = smem_desc(smem_u32(sm.vh[0]), BN * 128, 1024);  // MN-major (P V B operand)
+    d.vl = smem_desc(smem_u32(sm.vl[0]), BN * 128, 1024);
+    return d;
+}
+
+// S = Q K^T of the key tile in stage `stage` into TMEM buffer b.
+__device__ __forceinline__ void issue_s(const Descs& d, uint32_t tm, int stage, int b) {
     constexpr uint32_t idesc = idesc_bf16(BM, BN, 0, 0);
-    const uint32_t qh = smem_u32(sm.qh), ql = smem_u32(sm.ql);
-    const uint32_t kh = smem_u32(sm.kh[stage]), kl = smem_u32(sm.kl[stage]);
+    const uint32_t so = stage * STAGE_BYTES;
+    const uint64_t kh = desc_add(d.kh, so), kl = desc_add(d.kl, so);
 #pragma unroll
     for (int s = 0; s < D / 16; ++s) {
-        const uint64_t aqh = smem_desc(qh + s * 32, 16, 1024), aql = smem_desc(ql + s * 32, 16, 1024);
-        const uint64_t bkh = smem_desc(kh + s * 32, 16, 1024), bkl = smem_desc(kl + s * 32, 16, 1024);
-        mma_ss(tm + COL_S, aqh, bkh, idesc, s > 0);
-        mma_ss(tm + COL_S, aqh, bkl, idesc, 1);
-        mma_ss(tm + COL_S, aql, bkh, idesc, 1);
+        const uint32_t o = s * 32;
+        mma_ss(tm + col_s(b), desc_add(d.qh, o), desc_add(kh, o), idesc, s > 0);
+        mma_ss(tm + col_s(b), desc_add(d.qh, o), desc_add(kl, o), idesc, 1);
+        mma_ss(tm + col_s(b), desc_add(d.ql, o), desc_add(kh, o), idesc, 1);
     }
 }
 
-__device__ __forceinline__ void issue_pv(const Smem& sm, uint32_t tm, int stage) {
+// O_tile = P V of the key tile in stage `stage`, P packed over S buffer b.
+__device__ __forceinline__ void issue_pv(const Descs& d, uint32_t tm, int stage, int b) {
     constexpr uint32_t idesc = idesc_bf16(BM, D, 0, 1);
-    const uint32_t vh = smem_u32(sm.vh[stage]), vl = smem_u32(sm.vl[stage]);
+    const uint32_t so = stage * STAGE_BYTES;
+    const uint64_t vh = desc_add(d.vh, so), vl = desc_add(d.vl, so);
 #pragma unroll
     for (int s = 0; s < BN / 16; ++s) {
-        const uint64_t bvh = smem_desc(vh + s * 2048, BN * 128, 1024);
-        const uint64_t bvl = smem_desc(vl + s * 2048, BN * 128, 1024);
-        mma_ts(tm + COL_O, tm + COL_PH + s * 8, bvh, idesc, s > 0);
-        mma_ts(tm + COL_O, tm + COL_PH + s * 8, bvl, idesc, 1);
-        mma_ts(tm + COL_O, tm + COL_PL + s * 8, bvh, idesc, 1);
+        const uint32_t o = s * 2048;
+        const uint32_t ph = tm + col_s(b) + 32 * (s >> 1) + 8 * (s & 1);
+        mma_ts(tm + col_o(b), ph, desc_add(vh, o), idesc, s > 0);
+        mma_ts(tm + col_o(b), ph, desc_add(vl, o), idesc, 1);
+        mma_ts(tm + col_o(b), ph + 16, desc_add(vh, o), idesc, 1);
     }
 }
 
@@ -119,38 +140,51 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         tmem_relinquish();
     }
     if (tid == 0) {
-        mbar_init(&sm.bar_s, 1);
-        mbar_init(&sm.bar_o, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.bar_s[i], 1);
+            mbar_init(&sm.bar_o[i], 1);
+        }
     }
+    tc::stage_rows2<BN, NT>(sm.kh[0], sm.kl[0], kg, p.ld_qkv, sm.vh[0], sm.vl[0], vg, p.ld_qkv, 0, p.T, tid);
     tc::stage_rows<BM, NT>(sm.qh, sm.ql, qg, p.ld_qkv, q0, p.T, p.scale_log2, tid);
-    tc::stage_rows<BN, NT>(sm.kh[0], sm.kl[0], kg, p.ld_qkv, 0, p.T, 1.f, tid);
-    tc::stage_rows<BN, NT>(sm.vh[0], sm.vl[0], vg, p.ld_qkv, 0, p.T, 1.f, tid);
-    if (n_kv > 1) {
-        tc::stage_rows<BN, NT>(sm.kh[1], sm.kl[1], kg, p.ld_qkv, BN, p.T, 1.f, tid);
-        tc::stage_rows<BN, NT>(sm.vh[1], sm.vl[1], vg, p.ld_qkv, BN, p.T, 1.f, tid);
-    }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = sm.tmem_slot;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-
+    Descs dsc;
     if (tid == 0) {
-        issue_s(sm, tm, 0);
-        mma_commit(&sm.bar_s);
+        dsc = make_descs(sm);
+        issue_s(dsc, tm, 0, 0);
+        mma_commit(&sm.bar_s[0]);
     }
+    if (n_kv > 1) tc::stage_rows<BN, NT>(sm.kh[1], sm.kl[1], kg, p.ld_qkv, BN, p.T, 1.f, tid);
+    fence_async_smem();
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 
     float o[D];
 #pragma unroll
     for (int c = 0; c < D; ++c) o[c] = 0.f;
     float m = -INFINITY, l = 0.f;
+    float alpha_prev = 1.f;  // rescale factor of the tile whose P V is still pending
     bool failed = false;
 
+    // O <- O * alpha + (P V tile in buffer b).
+    auto fold = [&](int b, float alpha) {
+        float sv[32];
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+            tmem_ld32(lane_base + tm + col_o(b) + c, sv);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha, sv[i]);
+        }
+    };
+
     for (int j = 0; j < n_kv; ++j) {
-        const int stage = j & 1;
+        const int bf = j & 1;  // TMEM buffer / smem stage of tile j
         const int k0 = j * BN;
-        const bool ok_s = mbar_wait(&sm.bar_s, j & 1);
+        const bool ok_s = mbar_wait(&sm.bar_s[bf], (j >> 1) & 1);
         if (__syncthreads_or(!ok_s)) {
             failed = true;
             break;
@@ -158,46 +192,48 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         tc_fence_after();
         const bool need_mask = (p.causal && k0 + BN - 1 > q0) || k0 + BN > p.T;
 
-        // Pass 1: tile row max.
-        float sv[32];
-        float tmax = -INFINITY;
+        // Tile row max over the 64 scores (masked columns to -inf), eight
+        // independent chains.  Columns >= nv of this row are masked.
+        float sv[BN];
+        tmem_ld32(lane_base + tm + col_s(bf), *reinterpret_cast<float(*)[32]>(&sv[0]));
+        tmem_ld32(lane_base + tm + col_s(bf) + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
+        tmem_wait_ld();
+        if (need_mask) {
+            const int nv = min(p.T - k0, p.causal ? row - k0 + 1 : BN);
 #pragma unroll
-        for (int c = 0; c < BN; c += 32) {
-            tmem_ld32(lane_base + tm + COL_S + c, sv);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int col = k0 + c + i;
-                if (need_mask && ((p.causal && col > row) || col >= p.T)) sv[i] = -INFINITY;
-                tmax = fmaxf(tmax, sv[i]);
-            }
+            for (int i = 0; i < BN; ++i) sv[i] = (i < nv) ? sv[i] : -INFINITY;
         }
+        float mx[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx[u] = fmaxf(sv[u], sv[u + 8]);
+#pragma unroll
+        for (int i = 16; i < BN; i += 8)
+#pragma unroll
+            for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], sv[i + u]);
+        const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
         const float mn = fmaxf(m, tmax);
         const float ms = (mn == -INFINITY) ? 0.f : mn;
         const float alpha = ex2(m - ms);
         m = mn;
 
-        // Pass 2: probabilities -> TMEM as bf16 hi / lo.
-        float rs = 0.f;
+        // Probabilities, packed bf16 hi / lo over the S columns just read.
+        float acc8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc8[u] = 0.f;
 #pragma unroll
         for (int c = 0; c < BN; c += 32) {
-            tmem_ld32(lane_base + tm + COL_S + c, sv);
-            tmem_wait_ld();
             uint32_t ph[16], pl[16];
 #pragma unroll
             for (int i = 0; i < 32; i += 2) {
-                float e0 = ex2(sv[i] - ms), e1 = ex2(sv[i + 1] - ms);
-                if (need_mask) {
-                    const int col = k0 + c + i;
-                    if ((p.causal && col > row) || col >= p.T) e0 = 0.f;
-                    if ((p.causal && col + 1 > row) || col + 1 >= p.T) e1 = 0.f;
-                }
-                rs += e0 + e1;
+                const float e0 = ex2(sv[c + i] - ms), e1 = ex2(sv[c + i + 1] - ms);
+                acc8[(i >> 1) & 7] += e0 + e1;
                 split2(e0, e1, ph[i / 2], pl[i / 2]);
             }
-            tmem_st16(lane_base + tm + COL_PH + c / 2, ph);
-            tmem_st16(lane_base + tm + COL_PL + c / 2, pl);
+            tmem_st16(lane_base + tm + col_s(bf) + c, ph);
+            tmem_st16(lane_base + tm + col_s(bf) + c + 16, pl);
         }
+        const float rs = ((acc8[0] + acc8[1]) + (acc8[2] + acc8[3])) + ((acc8[4] + acc8[5]) + (acc8[6] + acc8[7]));
         l = l * alpha + rs;
         tmem_wait_st();
         tc_fence_before();
@@ -205,42 +241,51 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
 
         if (tid == 0) {
             tc_fence_after();
-            issue_pv(sm, tm, stage);
-            mma_commit(&sm.bar_o);
+            issue_pv(dsc, tm, bf, bf);
+            mma_commit(&sm.bar_o[bf]);
             if (j + 1 < n_kv) {
-                issue_s(sm, tm, stage ^ 1);
-                mma_commit(&sm.bar_s);
+                issue_s(dsc, tm, bf ^ 1, bf ^ 1);
+                mma_commit(&sm.bar_s[bf ^ 1]);
             }
         }
-        const bool ok_o = mbar_wait(&sm.bar_o, j & 1);
+        if (j >= 1) {
+            // Fold in the previous tile's P V (its buffer is the other one).
+            const bool ok_o = mbar_wait(&sm.bar_o[bf ^ 1], ((j - 1) >> 1) & 1);
+            if (__syncthreads_or(!ok_o)) {
+                failed = true;
+                break;
+            }
+            tc_fence_after();
+            fold(bf ^ 1, alpha_prev);
+        }
+        alpha_prev = alpha;
+        // K_{j+2} into this tile's K stage (S_j is done); V_{j+1} into the
+        // other V stage (PV_{j-1} is done).  Both become visible to the tensor
+        // core at the next iteration's barrier.
+        const bool kn = j + 2 < n_kv, vn = j + 1 < n_kv && j >= 1;
+        if (kn) tc::stage_rows<BN, NT>(sm.kh[bf], sm.kl[bf], kg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
+        if (vn) tc::stage_rows<BN, NT>(sm.vh[bf ^ 1], sm.vl[bf ^ 1], vg, p.ld_qkv, (j + 1) * BN, p.T, 1.f, tid);
+        if (j == 0 && n_kv > 1) tc::stage_rows<BN, NT>(sm.vh[1], sm.vl[1], vg, p.ld_qkv, BN, p.T, 1.f, tid);
+        if (kn || vn || j == 0) fence_async_smem();
+    }
+
+    if (!failed) {
+        const int jl = n_kv - 1;
+        const bool ok_o = mbar_wait(&sm.bar_o[jl & 1], (jl >> 1) & 1);
         if (__syncthreads_or(!ok_o)) {
             failed = true;
-            break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < D; c += 32) {
-            tmem_ld32(lane_base + tm + COL_O + c, sv);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha, sv[i]);
-        }
-        // Key / value tile j+2 into the stage that tile j used (its MMAs are done).
-        if (j + 2 < n_kv) {
-            tc::stage_rows<BN, NT>(sm.kh[stage], sm.kl[stage], kg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
-            tc::stage_rows<BN, NT>(sm.vh[stage], sm.vl[stage], vg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
-            fence_async_smem();
+        } else {
+            tc_fence_after();
+            fold(jl & 1, alpha_prev);
         }
     }
 
     if (failed) {
         if (tid == 0) atomicOr(p.status, 1);
         // Let any MMA still in flight drain (bounded) before the columns are freed.
-        if (tid == 0) {
-            mma_commit(&sm.bar_o);
-        }
-        mbar_wait(&sm.bar_o, 0, 10000000ull);
-        mbar_wait(&sm.bar_o, 1, 10000000ull);
+        if (tid == 0) mma_commit(&sm.bar_s[0]);
+        mbar_wait(&sm.bar_s[0], 0, 10000000ull);
+        mbar_wait(&sm.bar_s[0], 1, 10000000ull);
     } else {
         // Normalise and stage O through shared memory (reusing the Q tiles,
         // float4 chunks XOR-swizzled by row) for coalesced global stores.

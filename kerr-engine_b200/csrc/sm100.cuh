@@ -133,6 +133,10 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     return d;
 }
 
+// Descriptor advanced by `bytes` (a multiple of 16) along its start address;
+// valid while the address stays inside the 256 KB shared window.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+
 // Instruction descriptor for kind::f16 with bf16 A and B, f32 accumulator.
 // a_mn / b_mn: operand is MN-major (1) or K-major (0).
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_mn) {
