@@ -18,10 +18,11 @@
 //
 // Warp roles (416 threads, one CTA per SM):
 //   warps 0-7   elementwise.  Warp w reads TMEM lanes 32*(w%4).. (key rows)
-//               and query columns 32*(w/4)..+31 of each 64-column tile; it
-//               also adds its half of the dQ tile into dq and, at the end,
-//               stores its half of the dK / dV rows.
-//   warps 8-11  loaders: Q, dO, lse, D per query tile into a 3-stage ring.
+//               and query columns 32*(w/4)..+31 of each 64-column tile; at
+//               the end it stores its half of the dK / dV rows.
+//   warps 8-11  loaders: Q, dO, lse, D per query tile into a 3-stage ring;
+//               they also add each finished dQ tile into dq (reductions), so
+//               that wait stays off the elementwise warps.
 //   warp 12     one lane issues every tcgen05.mma and commit, from
 //               descriptors built once, in whichever order its inputs become
 //               ready (a tile's S^T / dP^T as soon as the tile is loaded and
@@ -31,7 +32,7 @@
 // dS^T in shared memory, the dQ accumulator in TMEM), so the tensor core runs
 // tile i's gradient products while the elementwise warps work on tile i+1.
 // P and dS are packed over their own S^T / dP^T columns: for query columns
-// 32h..32h+31, bf16 hi goes to columns 32h..32h+15 and lo to 32h+16..32h+31,
+// 16c..16c+15, bf16 hi goes to columns 16c..16c+7 and lo to 16c+8..16c+15,
 // which the owning warp has already read; the tensor core runs one thread's
 // MMAs in issue order, so the next S^T lands only after dV / dK read them.
 #include <atomic>
@@ -81,8 +82,9 @@ struct alignas(1024) Smem {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
     uint64_t bar_s[2];
-    uint64_t pds[2];  // P / dS of the tile in buffer b written
-    uint64_t bar_d[2];
+    uint64_t pds[2];      // P / dS of the tile in buffer b written
+    uint64_t bar_d[2];    // gradient products of the tile in buffer b done
+    uint64_t dq_free[2];  // dQ accumulator b read out by the loaders
     uint32_t tmem_slot;
 };
 
@@ -176,15 +178,14 @@ __device__ __forceinline__ void issue_grads(const Descs& d, uint32_t tm, int s, 
 #pragma unroll
     for (int ks = 0; ks < BQ / 16; ++ks) {
         const uint32_t acc = (first && ks == 0) ? 0u : 1u;
-        const uint32_t pk = 32 * (ks >> 1) + 8 * (ks & 1);  // packed column of this 16-query step
         const uint32_t o = ks * 2048;
-        const uint32_t ph = tm + col_s(b) + pk, gph = tm + col_dp(b) + pk;
+        const uint32_t ph = tm + col_s(b) + 16 * ks, gph = tm + col_dp(b) + 16 * ks;  // hi; lo is 8 further
         mma_ts(tm + COL_DV, ph, desc_add(gh, o), idesc_kv, acc);
         mma_ts(tm + COL_DV, ph, desc_add(gl, o), idesc_kv, 1);
-        mma_ts(tm + COL_DV, ph + 16, desc_add(gh, o), idesc_kv, 1);
+        mma_ts(tm + COL_DV, ph + 8, desc_add(gh, o), idesc_kv, 1);
         mma_ts(tm + COL_DK, gph, desc_add(qh, o), idesc_kv, acc);
         mma_ts(tm + COL_DK, gph, desc_add(ql, o), idesc_kv, 1);
-        mma_ts(tm + COL_DK, gph + 16, desc_add(qh, o), idesc_kv, 1);
+        mma_ts(tm + COL_DK, gph + 8, desc_add(qh, o), idesc_kv, 1);
     }
     const uint32_t cq = tm + col_dq(b);
     const uint64_t sh = b ? d.s1h : d.s0h, sl = b ? d.s1l : d.s0l;
@@ -197,19 +198,25 @@ __device__ __forceinline__ void issue_grads(const Descs& d, uint32_t tm, int s, 
     }
 }
 
-// Half of a dQ tile (M=64 accumulator: query row 16*qd + l sits in lane
-// 32*qd + l, l < 16), columns 32*half..+31, scaled and added into dq.
-__device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int half, int lane,
-                                            int q0, float* dqg) {
-    float v[32];
-    tmem_ld32((static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b) + 32 * half, v);
+// A dQ tile (M=64 accumulator: query row 16*qd + l sits in lane 32*qd + l,
+// l < 16), scaled and added into dq by the loader warp of lane quadrant qd.
+__device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int lane, int q0,
+                                            float* dqg) {
+    float v0[32], v1[32];
+    const uint32_t ta = (static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b);
+    tmem_ld32(ta, v0);
+    tmem_ld32(ta + 32, v1);
     tmem_wait_ld();
     const int r = q0 + qd * 16 + lane;
     if (lane < 16 && r < p.T) {
-        float* dst = dqg + static_cast<long>(r) * p.ld_d + 32 * half;
+        float* dst = dqg + static_cast<long>(r) * p.ld_d;
 #pragma unroll
         for (int c = 0; c < 32; c += 4)
-            red_add_v4(dst + c, v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale, v[c + 3] * p.scale);
+            red_add_v4(dst + c, v0[c] * p.scale, v0[c + 1] * p.scale, v0[c + 2] * p.scale, v0[c + 3] * p.scale);
+#pragma unroll
+        for (int c = 0; c < 32; c += 4)
+            red_add_v4(dst + 32 + c, v1[c] * p.scale, v1[c + 1] * p.scale, v1[c + 2] * p.scale,
+                       v1[c + 3] * p.scale);
     }
 }
 
@@ -251,6 +258,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.bar_s[i], 1);
             mbar_init(&sm.bar_d[i], 1);
+            mbar_init(&sm.dq_free[i], NLOAD);
         }
         mbar_init(&sm.pds[0], NELEM);
         mbar_init(&sm.pds[1], NELEM);
@@ -263,22 +271,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
 
     if (warp >= NELEM / 32 && warp < MMA_WARP) {
         // ------------------------------------------------------------ loaders
+        // Iteration n stages query tile n, then adds tile n-2's dQ into dq
+        // (gradient products finish in tile order, and loading runs ahead).
         const int t = tid - NELEM;
-        for (int n = 0; n < n_it; ++n) {
-            const int s = n % STAGES;
-            const int q0 = (it0 + n) * BQ;
-            if (n >= STAGES && !mbar_wait(&sm.empty[s], ((n - STAGES) / STAGES) & 1)) {
-                failed = true;
-                break;
+        const int qd = warp & 3;
+        auto dq_out = [&](int m) -> bool {
+            if (!mbar_wait_warp(&sm.bar_d[m & 1], (m >> 1) & 1)) return false;
+            tc_fence_after();
+            dq_epilogue(p, tm, m & 1, qd, lane, (it0 + m) * BQ, dqg);
+            tc_fence_before();
+            mbar_arrive(&sm.dq_free[m & 1]);
+            return true;
+        };
+        for (int n = 0; n < n_it + 2 && !failed; ++n) {
+            if (n < n_it) {
+                const int s = n % STAGES;
+                const int q0 = (it0 + n) * BQ;
+                if (n >= STAGES && !mbar_wait_warp(&sm.empty[s], ((n - STAGES) / STAGES) & 1)) {
+                    failed = true;  // warp-uniform: the dQ epilogue below is warp-collective
+                    break;
+                }
+                if (t < BQ) {
+                    const bool ok = q0 + t < p.T;
+                    sm.lse2[s][t] = ok ? lseg[q0 + t] * kLog2e : INFINITY;
+                    sm.dsum[s][t] = ok ? dsg[q0 + t] : 0.f;
+                }
+                tc::stage_rows2<BQ, NLOAD>(sm.qh[s], sm.ql[s], qg, p.ld_qkv, sm.gh[s], sm.gl[s], dog, p.ld_o, q0, p.T,
+                                           t);
+                fence_async_smem();
+                mbar_arrive(&sm.full[s]);
             }
-            if (t < BQ) {
-                const bool ok = q0 + t < p.T;
-                sm.lse2[s][t] = ok ? lseg[q0 + t] * kLog2e : INFINITY;
-                sm.dsum[s][t] = ok ? dsg[q0 + t] : 0.f;
-            }
-            tc::stage_rows2<BQ, NLOAD>(sm.qh[s], sm.ql[s], qg, p.ld_qkv, sm.gh[s], sm.gl[s], dog, p.ld_o, q0, p.T, t);
-            fence_async_smem();
-            mbar_arrive(&sm.full[s]);
+            if (n >= 2 && !dq_out(n - 2)) failed = true;
         }
     } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
@@ -300,7 +323,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                     ++ns;
                     progressed = true;
                 }
-                if (ng < ns && mbar_try_wait(&sm.pds[ng & 1], (ng >> 1) & 1)) {
+                if (ng < ns && mbar_try_wait(&sm.pds[ng & 1], (ng >> 1) & 1) &&
+                    (ng < 2 || mbar_try_wait(&sm.dq_free[ng & 1], ((ng - 2) >> 1) & 1))) {
                     tc_fence_after();
                     issue_grads(d, tm, ng % STAGES, ng & 1, ng == 0);
                     mma_commit(&sm.empty[ng % STAGES]);
@@ -322,7 +346,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     } else {
         // ------------------------------------------------------------ elementwise
         const int qd = warp & 3;          // TMEM lane quadrant: key rows 32*qd..
-        const int half = warp >> 2;       // query columns 32*half..+31
+        const int hf = warp >> 2;         // query columns 32*hf..+31 (two 16-column chunks)
         const int row = qd * 32 + lane;   // key row inside the tile
         const int j = k0 + row;
         const uint32_t lb = static_cast<uint32_t>(qd * 32) << 16;
@@ -345,72 +369,65 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
             }
             tc_fence_after();
             const bool need_mask = (p.causal && q0 < k0 + BK - 1) || q0 + BQ > p.T || k0 + BK > p.T;
-            // Valid query columns of this key row in this warp's half: bit i set
-            // when query q0 + 32*half + i attends to key j (causal: q >= j) and
-            // both are below T.
+            // Valid query columns of this key row in this warp's 32: bit i set when
+            // query q0 + 32*hf + i attends to key j (causal: q >= j), both below T.
             uint32_t vmask = 0xffffffffu;
             if (need_mask) {
-                const int c0 = q0 + 32 * half;
+                const int c0 = q0 + 32 * hf;
                 const int lo = p.causal ? max(0, j - c0) : 0;
                 const int hi = (j < p.T) ? min(32, p.T - c0) : 0;
-                vmask = (lo >= hi) ? 0u : ((hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~((lo >= 32) ? 0xffffffffu : ((1u << lo) - 1u)));
+                vmask = (lo >= hi) ? 0u
+                                   : ((hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) &
+                                      ~((lo >= 32) ? 0xffffffffu : ((1u << lo) - 1u)));
             }
-            const uint32_t cs = lb + tm + col_s(buf) + 32 * half, cp = lb + tm + col_dp(buf) + 32 * half;
+            const uint32_t cs = lb + tm + col_s(buf) + 32 * hf, cp = lb + tm + col_dp(buf) + 32 * hf;
             float sv[32], dp[32];
             tmem_ld32(cs, sv);
             tmem_ld32(cp, dp);
             tmem_wait_ld();
-            uint32_t ph[16], pl[16], gh[16], gl[16];
-            const float4* l4 = reinterpret_cast<const float4*>(&sm.lse2[s][32 * half]);
-            const float4* d4 = reinterpret_cast<const float4*>(&sm.dsum[s][32 * half]);
+            const float4* l4 = reinterpret_cast<const float4*>(&sm.lse2[s][32 * hf]);
+            const float4* d4 = reinterpret_cast<const float4*>(&sm.dsum[s][32 * hf]);
 #pragma unroll
-            for (int i4 = 0; i4 < 8; ++i4) {
-                const float4 lv = l4[i4], dv = d4[i4];
-                const float lse_[4] = {lv.x, lv.y, lv.z, lv.w};
-                const float ds_[4] = {dv.x, dv.y, dv.z, dv.w};
-                float pr[4], gr[4];
+            for (int c = 0; c < 2; ++c) {  // 16-column chunk: packed hi at +0, lo at +8
+                uint32_t ph[8], pl[8], gh[8], gl[8];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int i = 4 * i4 + u;
-                    float pv = ex2(fmaf(sv[i], p.scale_log2, -lse_[u]));
-                    pv = ((vmask >> i) & 1u) ? pv : 0.f;
-                    pr[u] = pv;
-                    gr[u] = pv * (dp[i] - ds_[u]);
+                for (int i4 = 0; i4 < 4; ++i4) {
+                    const float4 lv = l4[4 * c + i4], dv = d4[4 * c + i4];
+                    const float lse_[4] = {lv.x, lv.y, lv.z, lv.w};
+                    const float ds_[4] = {dv.x, dv.y, dv.z, dv.w};
+                    float pr[4], gr[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int i = 16 * c + 4 * i4 + u;
+                        float pv = ex2(fmaf(sv[i], p.scale_log2, -lse_[u]));
+                        pv = ((vmask >> i) & 1u) ? pv : 0.f;
+                        pr[u] = pv;
+                        gr[u] = pv * (dp[i] - ds_[u]);
+                    }
+                    split2(pr[0], pr[1], ph[2 * i4], pl[2 * i4]);
+                    split2(pr[2], pr[3], ph[2 * i4 + 1], pl[2 * i4 + 1]);
+                    split2(gr[0], gr[1], gh[2 * i4], gl[2 * i4]);
+                    split2(gr[2], gr[3], gh[2 * i4 + 1], gl[2 * i4 + 1]);
                 }
-                split2(pr[0], pr[1], ph[2 * i4], pl[2 * i4]);
-                split2(pr[2], pr[3], ph[2 * i4 + 1], pl[2 * i4 + 1]);
-                split2(gr[0], gr[1], gh[2 * i4], gl[2 * i4]);
-                split2(gr[2], gr[3], gh[2 * i4 + 1], gl[2 * i4 + 1]);
-            }
-            // P and dS packed over the columns just read (see the header).
-            tmem_st16(cs, ph);
-            tmem_st16(cs + 16, pl);
-            tmem_st16(cp, gh);
-            tmem_st16(cp + 16, gl);
-            // dS^T row for the dQ product: query chunks 4*half..4*half+3.
+                // P and dS packed over the columns just read (see the header).
+                tmem_st8(cs + 16 * c, ph);
+                tmem_st8(cs + 16 * c + 8, pl);
+                tmem_st8(cp + 16 * c, gh);
+                tmem_st8(cp + 16 * c + 8, gl);
+                // dS^T row for the dQ product: query chunks 4*hf + 2*c, +1.
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t off = sw128(row, 4 * half + u);
-                *reinterpret_cast<uint4*>(sm.sh[buf] + off) =
-                    make_uint4(gh[4 * u], gh[4 * u + 1], gh[4 * u + 2], gh[4 * u + 3]);
-                *reinterpret_cast<uint4*>(sm.sl[buf] + off) =
-                    make_uint4(gl[4 * u], gl[4 * u + 1], gl[4 * u + 2], gl[4 * u + 3]);
+                for (int u = 0; u < 2; ++u) {
+                    const uint32_t off = sw128(row, 4 * hf + 2 * c + u);
+                    *reinterpret_cast<uint4*>(sm.sh[buf] + off) =
+                        make_uint4(gh[4 * u], gh[4 * u + 1], gh[4 * u + 2], gh[4 * u + 3]);
+                    *reinterpret_cast<uint4*>(sm.sl[buf] + off) =
+                        make_uint4(gl[4 * u], gl[4 * u + 1], gl[4 * u + 2], gl[4 * u + 3]);
+                }
             }
             tmem_wait_st();
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(&sm.pds[buf]);
-            if (n >= 1) {
-                // dQ of the previous tile, while the tensor core works on this one.
-                const int pb = (n - 1) & 1;
-                if (!mbar_wait_warp(&sm.bar_d[pb], ((n - 1) >> 1) & 1)) {
-                    failed = true;
-                    break;
-                }
-                tc_fence_after();
-                dq_epilogue(p, tm, pb, qd, half, lane, q0 - BQ, dqg);
-                tc_fence_before();
-            }
         }
         if (!failed) {
             const int lbuf = (n_it - 1) & 1;
@@ -418,21 +435,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 failed = true;
             } else {
                 tc_fence_after();
-                dq_epilogue(p, tm, lbuf, qd, half, lane, (it0 + n_it - 1) * BQ, dqg);
-                // dK, dV columns 32*half..+31 of this key row.  The TMEM loads are
+                // dK, dV columns 32*hf..+31 of this key row.  The TMEM loads are
                 // warp-collective and run on every lane; rows past T are not stored.
                 float a[32];
                 const bool store = j < p.T;
-                float* dvr = p.dv + (base + j) * p.ld_d + h * D + 32 * half;
-                float* dkr = p.dk + (base + j) * p.ld_d + h * D + 32 * half;
-                tmem_ld32(lb + tm + COL_DV + 32 * half, a);
+                float* dvr = p.dv + (base + j) * p.ld_d + h * D + 32 * hf;
+                float* dkr = p.dk + (base + j) * p.ld_d + h * D + 32 * hf;
+                tmem_ld32(lb + tm + COL_DV + 32 * hf, a);
                 tmem_wait_ld();
                 if (store) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
                         *reinterpret_cast<float4*>(dvr + i) = make_float4(a[i], a[i + 1], a[i + 2], a[i + 3]);
                 }
-                tmem_ld32(lb + tm + COL_DK + 32 * half, a);
+                tmem_ld32(lb + tm + COL_DK + 32 * hf, a);
                 tmem_wait_ld();
                 if (store) {
 #pragma unroll
