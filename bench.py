@@ -126,17 +126,25 @@ def measured_peaks():
     return {"hbm_gbs": FALLBACK_HBM_GBS}, "fallback"
 
 
-def profiled_traffic(name: str):
-    """DRAM bytes per launch of `name` from the committed ncu summary, if any."""
+def profiled_traffic(*names: str):
+    """Sum of the DRAM bytes per launch (read + write) that the committed ncu
+    summary profiles/traffic.txt records for the named kernels; None if any
+    is missing.  Lines read: `<kernel> <bytes per launch> ...`."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")
     if not os.path.exists(path):
         return None
+    table = {}
     with open(path) as f:
         for line in f:
             parts = line.split()
-            if len(parts) >= 2 and parts[0] == name:
-                return float(parts[1])
-    return None
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    table[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    if not all(n in table for n in names):
+        return None
+    return sum(table[n] for n in names)
 
 
 def cpu_sample(n_seq: int, T: int, H: int, d: int, seed: int = 7):
@@ -191,10 +199,11 @@ def run_ours(args):
     import torch.distributed as dist
 
     import kerr_attn
+    from kerr_attn.dist import max_over_ranks as _max_over_ranks
+    from kerr_attn.dist import sync as _sync
+    from kerr_attn.dist import world as _world
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, local, world = _world()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
     torch.cuda.set_device(local)
@@ -241,17 +250,10 @@ def run_ours(args):
         return n
 
     def sync_all():
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
+        _sync(dev)
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max_over_ranks(x, dev)
 
     for _ in range(args.warmup):
         step()
@@ -314,11 +316,27 @@ def run_ours(args):
     props = torch.cuda.get_device_properties(dev)
     ck = clocks.summary()
     sm_mhz = ck["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
-    ffma_peak_tflops = props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12
+    tensor_path = args.path != "ffma" and d == 64
     bwd_gbs = work["bwd_bytes"] / (bwd_ms / 1e3) / 1e9
     bwd_tflops = work["bwd_flops"] / (bwd_ms / 1e3) / 1e12
     fwd_tflops = work["fwd_flops"] / (fwd_ms / 1e3) / 1e12
-    traffic = profiled_traffic("attn_bwd_f32")
+    if tensor_path:
+        kernels = ("attn_bwd_rowdot", "attn_bwd_tc64")
+        bf16_peak = peaks.get("bf16_tflops")
+        pipe = {"name": "tcgen05 kind::f16 (bf16x3: 3 MMAs per product)",
+                "achieved_tflops": bwd_tflops, "executed_tflops": 3 * bwd_tflops,
+                "peak_tflops": bf16_peak, "frac": (3 * bwd_tflops / bf16_peak) if bf16_peak else None,
+                "peak_source": f"{peak_src} dense bf16 (burst)",
+                "algorithmic_flops_per_launch": work["bwd_flops"]}
+    else:
+        kernels = ("attn_bwd_rowdot", "attn_bwd_f32")
+        ffma_peak_tflops = props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12
+        pipe = {"name": "fp32 FFMA (CUDA cores)", "achieved_tflops": bwd_tflops,
+                "peak_tflops": ffma_peak_tflops, "frac": bwd_tflops / ffma_peak_tflops,
+                "peak_source": "nominal: SMs x 128 FMA/clk x 2 x median sampled SM clock",
+                "algorithmic_flops_per_launch": work["bwd_flops"]}
+    traffic = profiled_traffic(*kernels)
+    fwd_kernel = "attn_fwd_tc64" if tensor_path else "attn_fwd_f32"
 
     ctx.check_device()
     line = {
@@ -331,16 +349,16 @@ def run_ours(args):
                 "api": "kattn_fwd_host + kattn_bwd_host per block, pinned host buffers"},
         "gpu_launches": launches, "kernel_path": args.path,
         "roofline": {
-            "kernel": "kattn_bwd call (attn_bwd_rowdot + attn_bwd_f32), 768-dim block",
+            "kernel": f"kattn_bwd call = {kernels[0]} + {kernels[1]} (2 launches), one 768-dim block",
             "bound": "hbm", "achieved": bwd_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": bwd_gbs / peaks["hbm_gbs"], "traffic": traffic, "peak_source": peak_src,
             "algorithmic_bytes_per_launch": work["bwd_bytes"], "launch_ms": bwd_ms,
-            "pipe": {"name": "fp32 FFMA (SIMT)", "achieved_tflops": bwd_tflops,
-                     "peak_tflops": ffma_peak_tflops, "frac": bwd_tflops / ffma_peak_tflops,
-                     "peak_source": "nominal: SMs x 128 FMA/clk x 2 x median sampled SM clock",
-                     "algorithmic_flops_per_launch": work["bwd_flops"]},
-            "fwd": {"launch_ms": fwd_ms, "achieved_tflops": fwd_tflops, "frac_ffma": fwd_tflops / ffma_peak_tflops,
-                    "achieved_gbs": work["fwd_bytes"] / (fwd_ms / 1e3) / 1e9},
+            "pipe": pipe,
+            "fwd": {"kernel": fwd_kernel, "launch_ms": fwd_ms, "achieved_tflops": fwd_tflops,
+                    "achieved_gbs": work["fwd_bytes"] / (fwd_ms / 1e3) / 1e9,
+                    "frac_hbm": work["fwd_bytes"] / (fwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                    "traffic": profiled_traffic(fwd_kernel),
+                    "algorithmic_bytes_per_launch": work["fwd_bytes"]},
         },
         "clocks": ck,
     }
