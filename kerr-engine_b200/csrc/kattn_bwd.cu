@@ -48,6 +48,7 @@ struct BwdParams {
 // D/4 lanes per (b, t, h) row, one float4 each.
 template <int D>
 __global__ void __launch_bounds__(256) attn_bwd_rowdot(const BwdParams p) {
+    pdl_enter();
     constexpr int LPR = D / 4;
     constexpr int RPW = 32 / LPR;
     const long nrows = static_cast<long>(p.B) * p.T * p.H;
@@ -99,6 +100,7 @@ __device__ __forceinline__ float f4get(const float4& v, int u) {
 
 template <int D>
 __global__ void __launch_bounds__(BWD_NT, (D <= 64 ? 2 : 1)) attn_bwd_f32(const BwdParams p) {
+    pdl_enter();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     BwdSmem<D>& sm = *reinterpret_cast<BwdSmem<D>*>(smem_raw);
     constexpr int LDD = BwdSmem<D>::LDD;
@@ -340,8 +342,7 @@ static cudaError_t launch_prep_d(const BwdParams& p, int num_sms, cudaStream_t s
     long blocks = (nrows + rows_per_block - 1) / rows_per_block;
     const long cap = static_cast<long>(num_sms > 0 ? num_sms : 148) * 8;
     if (blocks > cap) blocks = cap;
-    attn_bwd_rowdot<D><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(attn_bwd_rowdot<D>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }
@@ -365,8 +366,7 @@ static cudaError_t launch_bwd_d(const BwdArgs& a, int num_sms, cudaStream_t stre
     e = cudaFuncSetAttribute(attn_bwd_f32<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const long nblocks = static_cast<long>(p.n_tiles) * a.B * a.H;
-    attn_bwd_f32<D><<<static_cast<unsigned>(nblocks), BWD_NT, smem, stream>>>(p);
-    e = cudaGetLastError();
+    e = launch_pdl(attn_bwd_f32<D>, dim3(static_cast<unsigned>(nblocks)), dim3(BWD_NT), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

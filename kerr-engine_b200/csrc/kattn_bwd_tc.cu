@@ -221,6 +221,7 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
+    pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -507,8 +508,7 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
         attr_done.fetch_or(bit);
     }
     const long nblocks = static_cast<long>(p.n_ktiles) * a.B * a.H;
-    attn_bwd_tc64<<<static_cast<unsigned>(nblocks), NTHREADS, smem, stream>>>(p);
-    e = cudaGetLastError();
+    e = launch_pdl(attn_bwd_tc64, dim3(static_cast<unsigned>(nblocks)), dim3(NTHREADS), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

@@ -34,6 +34,16 @@ __device__ __forceinline__ void red_add_v2(float* gptr, float a, float b) {
     asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(gptr), "f"(a), "f"(b) : "memory");
 }
 
+// Programmatic dependent launch.  Every kernel of this library waits for the
+// grid it was launched behind to finish (and its memory to be visible) before
+// touching global memory, then lets the next grid start launching: that
+// grid's CTAs take SM slots as this grid drains and wait there, instead of
+// paying the launch latency after it.  Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Reductions over the 16 lanes that share a row (lane bits 0..3).
 __device__ __forceinline__ float max16(float x) {
 #pragma unroll

@@ -45,6 +45,7 @@ struct FwdParams {
 
 template <int D>
 __global__ void __launch_bounds__(FWD_NT, (D <= 64 ? 2 : 1)) attn_fwd_f32(const FwdParams p) {
+    pdl_enter();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem<D>& sm = *reinterpret_cast<FwdSmem<D>*>(smem_raw);
     constexpr int LDD = FwdSmem<D>::LDD;
@@ -243,8 +244,7 @@ static cudaError_t launch_fwd_d(const FwdArgs& a, cudaStream_t stream) {
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const long nblocks = static_cast<long>(p.n_tiles) * a.B * a.H;
-    attn_fwd_f32<D><<<static_cast<unsigned>(nblocks), FWD_NT, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(attn_fwd_f32<D>, dim3(static_cast<unsigned>(nblocks)), dim3(FWD_NT), smem, stream, p);
 }
 
 cudaError_t launch_fwd(const FwdArgs& a, int /*num_sms*/, cudaStream_t stream, int* launches) {

@@ -116,6 +116,7 @@ __device__ __forceinline__ void issue_pv(const Descs& d, uint32_t tm, int stage,
 }
 
 __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
+    pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -347,8 +348,7 @@ cudaError_t launch_fwd_tc(const FwdArgs& a, int* status, cudaStream_t stream, in
         attr_done.fetch_or(bit);
     }
     const long nblocks = static_cast<long>(p.n_qtiles) * a.B * a.H;
-    attn_fwd_tc64<<<static_cast<unsigned>(nblocks), NT, smem, stream>>>(p);
-    e = cudaGetLastError();
+    e = launch_pdl(attn_fwd_tc64, dim3(static_cast<unsigned>(nblocks)), dim3(NT), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }
