@@ -4,9 +4,12 @@
 // attn_backward_scores / attn_backward_dkv), recomputing the probabilities
 // from the forward's log-sum-exp instead of reading a cached [H][T][T] P.
 //
-// CTA = one 128-row key tile of one (batch, head) slab; it keeps K, V and the
-// dK, dV accumulators resident and walks the 64-row query tiles on or below
-// the diagonal.  Products (bf16x3: hi*hi + hi*lo + lo*hi, f32 accumulation):
+// Work item = one 128-row key tile of one (batch, head) slab: K, V and the
+// dK, dV accumulators stay resident while the item walks the 64-row query
+// tiles on or below the diagonal.  The kernel is persistent (one CTA per SM):
+// CTA c takes items c, 2G-1-c, 2G+c, ... of the list ordered longest first
+// (a snake order, which evens out the tile counts per CTA), and its query
+// tiles form one pipeline across item boundaries.  Products (bf16x3: hi*hi + hi*lo + lo*hi, f32 accumulation):
 //   S^T  = K Q^T      M=128 (keys) N=64 (queries)   SS, both K-major
 //   dP^T = V dO^T     M=128 N=64                    SS, both K-major
 //   P = exp2(S^T * scale*log2e - lse*log2e),  dS = P * (dP^T - D)   (threads)
@@ -19,7 +22,11 @@
 // Warp roles (416 threads, one CTA per SM):
 //   warps 0-7   elementwise.  Warp w reads TMEM lanes 32*(w%4).. (key rows)
 //               and query columns 32*(w/4)..+31 of each 64-column tile; at
-//               the end it stores its half of the dK / dV rows.
+//               the end of an item it stores its half of the dK / dV rows.
+//               They also stage K / V: the next item's rows are loaded into
+//               registers at the end of an item and written to shared memory
+//               as soon as the item's last dQ product (the last reader of K)
+//               is done, while the tensor core still runs its dV / dK.
 //   warps 8-11  loaders: Q, dO, lse, D per query tile into a 3-stage ring;
 //               they also add each finished dQ tile into dq (reductions), so
 //               that wait stays off the elementwise warps.
@@ -78,7 +85,8 @@ struct alignas(1024) Smem {
     uint8_t sl[2][BK * 128];
     float lse2[STAGES][BQ];  // lse * log2(e), +inf beyond T
     float dsum[STAGES][BQ];  // D, 0 beyond T
-    uint64_t kv_full;
+    uint64_t kv_full;  // an item's K / V staged (phase r: the CTA's item r)
+    uint64_t kv_free;  // an item's last dQ product done: K / V may be replaced
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
     uint64_t bar_s[2];
@@ -110,6 +118,57 @@ struct Params {
     int causal;
     int n_ktiles;  // 128-row key tiles
     int n_qtiles;  // 64-row query tiles
+    int n_work;    // work items: n_ktiles * B * H
+};
+
+// The r-th work item of CTA c in a grid of G: the snake order over the item
+// list (key tile 0 of every slab first: it sees the most query tiles).
+__device__ __forceinline__ int item_id(int c, int r, int G) { return r * G + ((r & 1) ? G - 1 - c : c); }
+
+// A work item: key tile jt of slab (b, h).
+struct Item {
+    int b, h, k0, it0, n_it;
+};
+
+__device__ __forceinline__ Item make_item(const Params& p, int w) {
+    const int nslab = p.B * p.H;
+    const int jt = w / nslab;
+    const int slab = w - jt * nslab;
+    Item it;
+    it.b = slab / p.H;
+    it.h = slab - it.b * p.H;
+    it.k0 = jt * BK;
+    it.it0 = p.causal ? it.k0 / BQ : 0;  // first query tile with a row >= k0
+    it.n_it = p.n_qtiles - it.it0;
+    return it;
+}
+
+// Position in a CTA's sequence of query tiles: item round r (item id w, -1
+// past the last), tile n of the item's n_it.
+struct Cursor {
+    int r, w, n, n_it, it0;
+    __device__ __forceinline__ void set(const Params& p, int c, int G) {
+        w = item_id(c, r, G);
+        n = 0;
+        if (w < p.n_work) {
+            const Item it = make_item(p, w);
+            n_it = it.n_it;
+            it0 = it.it0;
+        } else {
+            w = -1;
+        }
+    }
+    __device__ __forceinline__ void start(const Params& p, int c, int G) {
+        r = 0;
+        set(p, c, G);
+    }
+    __device__ __forceinline__ void next(const Params& p, int c, int G) {
+        if (++n == n_it) {
+            ++r;
+            set(p, c, G);
+        }
+    }
+    __device__ __forceinline__ bool valid() const { return w >= 0; }
 };
 
 // Shared-memory descriptors, built once by the issuing thread (two ring
@@ -168,10 +227,23 @@ __device__ __forceinline__ void issue_sdp(const Descs& d, uint32_t tm, int s, in
     }
 }
 
-// dV += P^T dO, dK += dS^T Q (ring stage s, buffer b), dQ_b = dS K.
-__device__ __forceinline__ void issue_grads(const Descs& d, uint32_t tm, int s, int b, bool first) {
-    constexpr uint32_t idesc_kv = idesc_bf16(BK, D, 0, 1);
+// dQ_b = dS K (dS^T of buffer b from shared memory, K MN-major).
+__device__ __forceinline__ void issue_dq(const Descs& d, uint32_t tm, int b) {
     constexpr uint32_t idesc_q = idesc_bf16(BQ, D, 1, 1);
+    const uint32_t cq = tm + col_dq(b);
+    const uint64_t sh = b ? d.s1h : d.s0h, sl = b ? d.s1l : d.s0l;
+#pragma unroll
+    for (int ks = 0; ks < BK / 16; ++ks) {
+        const uint32_t o = ks * 2048;
+        mma_ss(cq, desc_add(sh, o), desc_add(d.kh_mn, o), idesc_q, ks > 0);
+        mma_ss(cq, desc_add(sh, o), desc_add(d.kl_mn, o), idesc_q, 1);
+        mma_ss(cq, desc_add(sl, o), desc_add(d.kh_mn, o), idesc_q, 1);
+    }
+}
+
+// dV += P^T dO, dK += dS^T Q (P, dS from TMEM buffer b; dO, Q of ring stage s).
+__device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, int b, bool first) {
+    constexpr uint32_t idesc_kv = idesc_bf16(BK, D, 0, 1);
     const uint32_t so = s * STAGE_BYTES;
     const uint64_t qh = as_mn(desc_add(d.qh, so), MN_LBO_Q), ql = as_mn(desc_add(d.ql, so), MN_LBO_Q);
     const uint64_t gh = as_mn(desc_add(d.gh, so), MN_LBO_Q), gl = as_mn(desc_add(d.gl, so), MN_LBO_Q);
@@ -186,15 +258,6 @@ __device__ __forceinline__ void issue_grads(const Descs& d, uint32_t tm, int s, 
         mma_ts(tm + COL_DK, gph, desc_add(qh, o), idesc_kv, acc);
         mma_ts(tm + COL_DK, gph, desc_add(ql, o), idesc_kv, 1);
         mma_ts(tm + COL_DK, gph + 8, desc_add(qh, o), idesc_kv, 1);
-    }
-    const uint32_t cq = tm + col_dq(b);
-    const uint64_t sh = b ? d.s1h : d.s0h, sl = b ? d.s1l : d.s0l;
-#pragma unroll
-    for (int ks = 0; ks < BK / 16; ++ks) {
-        const uint32_t o = ks * 2048;
-        mma_ss(cq, desc_add(sh, o), desc_add(d.kh_mn, o), idesc_q, ks > 0);
-        mma_ss(cq, desc_add(sh, o), desc_add(d.kl_mn, o), idesc_q, 1);
-        mma_ss(cq, desc_add(sl, o), desc_add(d.kh_mn, o), idesc_q, 1);
     }
 }
 
@@ -225,26 +288,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-    const int nslab = p.B * p.H;
-    const int jt = static_cast<int>(blockIdx.x / nslab);  // key tile 0 sees the most query tiles: first
-    const int slab = static_cast<int>(blockIdx.x % nslab);
-    const int b = slab / p.H;
-    const int h = slab % p.H;
+    const int c = static_cast<int>(blockIdx.x);
+    const int G = static_cast<int>(gridDim.x);
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const int k0 = jt * BK;
-    const int it0 = p.causal ? k0 / BQ : 0;  // first query tile with a row >= k0
-    const int n_it = p.n_qtiles - it0;
-
-    const long base = static_cast<long>(b) * p.T;
-    const float* qg = p.q + base * p.ld_qkv + h * D;
-    const float* kg = p.k + base * p.ld_qkv + h * D;
-    const float* vg = p.v + base * p.ld_qkv + h * D;
-    const float* dog = p.dout + base * p.ld_o + h * D;
-    const float* lseg = p.lse + (static_cast<long>(b) * p.H + h) * p.T;
-    const float* dsg = p.dsum + (static_cast<long>(b) * p.H + h) * p.T;
-    float* dqg = p.dq + base * p.ld_d + h * D;
 
     if (warp == 0) {
         tmem_alloc(&sm.tmem_slot, TMEM_COLS);
@@ -252,6 +300,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     }
     if (tid == 0) {
         mbar_init(&sm.kv_full, NELEM);
+        mbar_init(&sm.kv_free, 1);
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&sm.full[i], NLOAD);
             mbar_init(&sm.empty[i], 1);
@@ -272,65 +321,93 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
 
     if (warp >= NELEM / 32 && warp < MMA_WARP) {
         // ------------------------------------------------------------ loaders
-        // Iteration n stages query tile n, then adds tile n-2's dQ into dq
-        // (gradient products finish in tile order, and loading runs ahead).
+        // Step n stages the CTA's query tile n, then adds tile n-2's dQ into
+        // dq (gradient products finish in tile order, and loading runs ahead).
         const int t = tid - NELEM;
         const int qd = warp & 3;
-        auto dq_out = [&](int m) -> bool {
-            if (!mbar_wait_warp(&sm.bar_d[m & 1], (m >> 1) & 1)) return false;
-            tc_fence_after();
-            dq_epilogue(p, tm, m & 1, qd, lane, (it0 + m) * BQ, dqg);
-            tc_fence_before();
-            mbar_arrive(&sm.dq_free[m & 1]);
-            return true;
-        };
-        for (int n = 0; n < n_it + 2 && !failed; ++n) {
-            if (n < n_it) {
+        Cursor cl, cq;  // tile to load, tile whose dQ is added
+        cl.start(p, c, G);
+        cq.start(p, c, G);
+        for (int n = 0; !failed; ++n) {
+            if (cl.valid()) {
+                const Item it = make_item(p, cl.w);
+                const long base = static_cast<long>(it.b) * p.T;
                 const int s = n % STAGES;
-                const int q0 = (it0 + n) * BQ;
+                const int q0 = (cl.it0 + cl.n) * BQ;
                 if (n >= STAGES && !mbar_wait_warp(&sm.empty[s], ((n - STAGES) / STAGES) & 1)) {
                     failed = true;  // warp-uniform: the dQ epilogue below is warp-collective
                     break;
                 }
                 if (t < BQ) {
+                    const long bh = (static_cast<long>(it.b) * p.H + it.h) * p.T;
                     const bool ok = q0 + t < p.T;
-                    sm.lse2[s][t] = ok ? lseg[q0 + t] * kLog2e : INFINITY;
-                    sm.dsum[s][t] = ok ? dsg[q0 + t] : 0.f;
+                    sm.lse2[s][t] = ok ? p.lse[bh + q0 + t] * kLog2e : INFINITY;
+                    sm.dsum[s][t] = ok ? p.dsum[bh + q0 + t] : 0.f;
                 }
-                tc::stage_rows2<BQ, NLOAD>(sm.qh[s], sm.ql[s], qg, p.ld_qkv, sm.gh[s], sm.gl[s], dog, p.ld_o, q0, p.T,
-                                           t);
+                tc::stage_rows2<BQ, NLOAD>(sm.qh[s], sm.ql[s], p.q + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.gh[s],
+                                           sm.gl[s], p.dout + base * p.ld_o + it.h * D, p.ld_o, q0, p.T, t);
                 fence_async_smem();
                 mbar_arrive(&sm.full[s]);
+                cl.next(p, c, G);
             }
-            if (n >= 2 && !dq_out(n - 2)) failed = true;
+            if (n >= 2) {
+                if (!cq.valid()) break;
+                const int m = n - 2;
+                if (!mbar_wait_warp(&sm.bar_d[m & 1], (m >> 1) & 1)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                const Item it = make_item(p, cq.w);
+                float* dqg = p.dq + static_cast<long>(it.b) * p.T * p.ld_d + it.h * D;
+                dq_epilogue(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg);
+                tc_fence_before();
+                mbar_arrive(&sm.dq_free[m & 1]);
+                cq.next(p, c, G);
+            }
         }
     } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             Descs d;
             make_descs(sm, d);
-            failed = !mbar_wait(&sm.kv_full, 0);
-            // sdp(n) needs tile n loaded and, for n >= 2, grads(n-2) issued
-            // (TMEM buffer n&1; the tensor core runs this thread's MMAs in
-            // order).  grads(n) needs P / dS of tile n written.
-            int ns = 0, ng = 0;
+            // sdp(n) needs tile n loaded, for n >= 2 grads(n-2) issued (TMEM
+            // buffer n&1; the tensor core runs this thread's MMAs in order)
+            // and, for an item's first tile, the item's K / V staged.
+            // grads(n) needs P / dS of tile n written and, for n >= 2, dQ
+            // buffer n&1 read out.  An item's last dQ product commits kv_free.
+            Cursor cs, cg;
+            cs.start(p, c, G);
+            cg.start(p, c, G);
+            int ns = 0, ng = 0, kv_round = -1;
             uint64_t t_idle = 0;
-            while (ng < n_it && !failed) {
+            while (cg.valid() && !failed) {
                 bool progressed = false;
-                if (ns < n_it && ns < ng + 2 && mbar_try_wait(&sm.full[ns % STAGES], (ns / STAGES) & 1)) {
-                    tc_fence_after();
-                    issue_sdp(d, tm, ns % STAGES, ns & 1);
-                    mma_commit(&sm.bar_s[ns & 1]);
-                    ++ns;
-                    progressed = true;
+                if (cs.valid() && ns < ng + 2) {
+                    bool kv_ok = kv_round >= cs.r;
+                    if (!kv_ok && mbar_try_wait(&sm.kv_full, cs.r & 1)) {
+                        kv_round = cs.r;
+                        kv_ok = true;
+                    }
+                    if (kv_ok && mbar_try_wait(&sm.full[ns % STAGES], (ns / STAGES) & 1)) {
+                        tc_fence_after();
+                        issue_sdp(d, tm, ns % STAGES, ns & 1);
+                        mma_commit(&sm.bar_s[ns & 1]);
+                        ++ns;
+                        cs.next(p, c, G);
+                        progressed = true;
+                    }
                 }
                 if (ng < ns && mbar_try_wait(&sm.pds[ng & 1], (ng >> 1) & 1) &&
                     (ng < 2 || mbar_try_wait(&sm.dq_free[ng & 1], ((ng - 2) >> 1) & 1))) {
                     tc_fence_after();
-                    issue_grads(d, tm, ng % STAGES, ng & 1, ng == 0);
+                    issue_dq(d, tm, ng & 1);
+                    if (cg.n == cg.n_it - 1) mma_commit(&sm.kv_free);
+                    issue_dkv(d, tm, ng % STAGES, ng & 1, cg.n == 0);
                     mma_commit(&sm.empty[ng % STAGES]);
                     mma_commit(&sm.bar_d[ng & 1]);
                     ++ng;
+                    cg.next(p, c, G);
                     progressed = true;
                 }
                 if (progressed) {
@@ -349,99 +426,132 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         const int qd = warp & 3;          // TMEM lane quadrant: key rows 32*qd..
         const int hf = warp >> 2;         // query columns 32*hf..+31 (two 16-column chunks)
         const int row = qd * 32 + lane;   // key row inside the tile
-        const int j = k0 + row;
         const uint32_t lb = static_cast<uint32_t>(qd * 32) << 16;
-        tc::stage_rows2<BK, NELEM>(sm.kh, sm.kl, kg, p.ld_qkv, sm.vh, sm.vl, vg, p.ld_qkv, k0, p.T, tid);
+        int w = item_id(c, 0, G);
+        Item it = make_item(p, w);
+        {
+            const long base = static_cast<long>(it.b) * p.T;
+            tc::stage_rows2<BK, NELEM>(sm.kh, sm.kl, p.k + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.vh, sm.vl,
+                                       p.v + base * p.ld_qkv + it.h * D, p.ld_qkv, it.k0, p.T, tid);
+        }
         fence_async_smem();
         mbar_arrive(&sm.kv_full);
 
-        for (int n = 0; n < n_it; ++n) {
-            const int s = n % STAGES;  // ring stage of this query tile
-            const int buf = n & 1;     // TMEM / dS buffer
-            const int q0 = (it0 + n) * BQ;
-            // full[s]: the loaders' lse / D writes for this tile are visible.
-            if (!mbar_wait_warp(&sm.bar_s[buf], (n >> 1) & 1) || !mbar_wait_warp(&sm.full[s], (n / STAGES) & 1)) {
-                failed = true;
-                break;
+        int g = 0;  // the CTA's query-tile sequence number
+        for (int r = 0; !failed; ++r) {
+            const int j = it.k0 + row;
+            for (int n = 0; n < it.n_it; ++n, ++g) {
+                const int s = g % STAGES;  // ring stage of this query tile
+                const int buf = g & 1;     // TMEM / dS buffer
+                const int q0 = (it.it0 + n) * BQ;
+                // full[s]: the loaders' lse / D writes for this tile are visible.
+                if (!mbar_wait_warp(&sm.bar_s[buf], (g >> 1) & 1) ||
+                    !mbar_wait_warp(&sm.full[s], (g / STAGES) & 1)) {
+                    failed = true;
+                    break;
+                }
+                if (g >= 2 && !mbar_wait_warp(&sm.bar_d[buf], ((g - 2) >> 1) & 1)) {
+                    failed = true;  // dS^T buffer `buf` is read by tile g-2's dQ product
+                    break;
+                }
+                tc_fence_after();
+                const bool need_mask =
+                    (p.causal && q0 < it.k0 + BK - 1) || q0 + BQ > p.T || it.k0 + BK > p.T;
+                // Valid query columns of this key row in this warp's 32: bit i set when
+                // query q0 + 32*hf + i attends to key j (causal: q >= j), both below T.
+                uint32_t vmask = 0xffffffffu;
+                if (need_mask) {
+                    const int c0 = q0 + 32 * hf;
+                    const int lo = p.causal ? max(0, j - c0) : 0;
+                    const int hi = (j < p.T) ? min(32, p.T - c0) : 0;
+                    vmask = (lo >= hi) ? 0u
+                                       : ((hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) &
+                                          ~((lo >= 32) ? 0xffffffffu : ((1u << lo) - 1u)));
+                }
+                const uint32_t cs = lb + tm + col_s(buf) + 32 * hf, cp = lb + tm + col_dp(buf) + 32 * hf;
+                float sv[32], dp[32];
+                tmem_ld32(cs, sv);
+                tmem_ld32(cp, dp);
+                tmem_wait_ld();
+                const float4* l4 = reinterpret_cast<const float4*>(&sm.lse2[s][32 * hf]);
+                const float4* d4 = reinterpret_cast<const float4*>(&sm.dsum[s][32 * hf]);
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {  // 16-column chunk: packed hi at +0, lo at +8
+                    uint32_t ph[8], pl[8], gh[8], gl[8];
+#pragma unroll
+                    for (int i4 = 0; i4 < 4; ++i4) {
+                        const float4 lv = l4[4 * cc + i4], dv = d4[4 * cc + i4];
+                        const float lse_[4] = {lv.x, lv.y, lv.z, lv.w};
+                        const float ds_[4] = {dv.x, dv.y, dv.z, dv.w};
+                        float pr[4], gr[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int i = 16 * cc + 4 * i4 + u;
+                            float pv = ex2(fmaf(sv[i], p.scale_log2, -lse_[u]));
+                            pv = ((vmask >> i) & 1u) ? pv : 0.f;
+                            pr[u] = pv;
+                            gr[u] = pv * (dp[i] - ds_[u]);
+                        }
+                        split2(pr[0], pr[1], ph[2 * i4], pl[2 * i4]);
+                        split2(pr[2], pr[3], ph[2 * i4 + 1], pl[2 * i4 + 1]);
+                        split2(gr[0], gr[1], gh[2 * i4], gl[2 * i4]);
+                        split2(gr[2], gr[3], gh[2 * i4 + 1], gl[2 * i4 + 1]);
+                    }
+                    // P and dS packed over the columns just read (see the header).
+                    tmem_st8(cs + 16 * cc, ph);
+                    tmem_st8(cs + 16 * cc + 8, pl);
+                    tmem_st8(cp + 16 * cc, gh);
+                    tmem_st8(cp + 16 * cc + 8, gl);
+                    // dS^T row for the dQ product: query chunks 4*hf + 2*cc, +1.
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint32_t off = sw128(row, 4 * hf + 2 * cc + u);
+                        *reinterpret_cast<uint4*>(sm.sh[buf] + off) =
+                            make_uint4(gh[4 * u], gh[4 * u + 1], gh[4 * u + 2], gh[4 * u + 3]);
+                        *reinterpret_cast<uint4*>(sm.sl[buf] + off) =
+                            make_uint4(gl[4 * u], gl[4 * u + 1], gl[4 * u + 2], gl[4 * u + 3]);
+                    }
+                }
+                tmem_wait_st();
+                fence_async_smem();
+                tc_fence_before();
+                mbar_arrive(&sm.pds[buf]);
             }
-            if (n >= 2 && !mbar_wait_warp(&sm.bar_d[buf], ((n - 2) >> 1) & 1)) {
-                failed = true;  // dS^T buffer `buf` is read by tile n-2's dQ product
+            if (failed) break;
+
+            // Item end.  The next item's K / V rows go into registers now and
+            // into shared memory once this item's last dQ product is done.
+            const int wn = item_id(c, r + 1, G);
+            const bool has_next = wn < p.n_work;
+            Item nx = it;
+            if (has_next) {
+                nx = make_item(p, wn);
+                const long base = static_cast<long>(nx.b) * p.T;
+                tc::Rows2<BK, NELEM> kv;
+                kv.load(p.k + base * p.ld_qkv + nx.h * D, p.ld_qkv, p.v + base * p.ld_qkv + nx.h * D, p.ld_qkv,
+                        nx.k0, p.T, tid);
+                if (!mbar_wait_warp(&sm.kv_free, r & 1)) {
+                    failed = true;
+                    break;
+                }
+                kv.store(sm.kh, sm.kl, sm.vh, sm.vl, tid);
+                fence_async_smem();
+                mbar_arrive(&sm.kv_full);
+            }
+            const int gl_ = g - 1;  // this item's last tile
+            if (!mbar_wait_warp(&sm.bar_d[gl_ & 1], (gl_ >> 1) & 1)) {
+                failed = true;
                 break;
             }
             tc_fence_after();
-            const bool need_mask = (p.causal && q0 < k0 + BK - 1) || q0 + BQ > p.T || k0 + BK > p.T;
-            // Valid query columns of this key row in this warp's 32: bit i set when
-            // query q0 + 32*hf + i attends to key j (causal: q >= j), both below T.
-            uint32_t vmask = 0xffffffffu;
-            if (need_mask) {
-                const int c0 = q0 + 32 * hf;
-                const int lo = p.causal ? max(0, j - c0) : 0;
-                const int hi = (j < p.T) ? min(32, p.T - c0) : 0;
-                vmask = (lo >= hi) ? 0u
-                                   : ((hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) &
-                                      ~((lo >= 32) ? 0xffffffffu : ((1u << lo) - 1u)));
-            }
-            const uint32_t cs = lb + tm + col_s(buf) + 32 * hf, cp = lb + tm + col_dp(buf) + 32 * hf;
-            float sv[32], dp[32];
-            tmem_ld32(cs, sv);
-            tmem_ld32(cp, dp);
-            tmem_wait_ld();
-            const float4* l4 = reinterpret_cast<const float4*>(&sm.lse2[s][32 * hf]);
-            const float4* d4 = reinterpret_cast<const float4*>(&sm.dsum[s][32 * hf]);
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {  // 16-column chunk: packed hi at +0, lo at +8
-                uint32_t ph[8], pl[8], gh[8], gl[8];
-#pragma unroll
-                for (int i4 = 0; i4 < 4; ++i4) {
-                    const float4 lv = l4[4 * c + i4], dv = d4[4 * c + i4];
-                    const float lse_[4] = {lv.x, lv.y, lv.z, lv.w};
-                    const float ds_[4] = {dv.x, dv.y, dv.z, dv.w};
-                    float pr[4], gr[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int i = 16 * c + 4 * i4 + u;
-                        float pv = ex2(fmaf(sv[i], p.scale_log2, -lse_[u]));
-                        pv = ((vmask >> i) & 1u) ? pv : 0.f;
-                        pr[u] = pv;
-                        gr[u] = pv * (dp[i] - ds_[u]);
-                    }
-                    split2(pr[0], pr[1], ph[2 * i4], pl[2 * i4]);
-                    split2(pr[2], pr[3], ph[2 * i4 + 1], pl[2 * i4 + 1]);
-                    split2(gr[0], gr[1], gh[2 * i4], gl[2 * i4]);
-                    split2(gr[2], gr[3], gh[2 * i4 + 1], gl[2 * i4 + 1]);
-                }
-                // P and dS packed over the columns just read (see the header).
-                tmem_st8(cs + 16 * c, ph);
-                tmem_st8(cs + 16 * c + 8, pl);
-                tmem_st8(cp + 16 * c, gh);
-                tmem_st8(cp + 16 * c + 8, gl);
-                // dS^T row for the dQ product: query chunks 4*hf + 2*c, +1.
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const uint32_t off = sw128(row, 4 * hf + 2 * c + u);
-                    *reinterpret_cast<uint4*>(sm.sh[buf] + off) =
-                        make_uint4(gh[4 * u], gh[4 * u + 1], gh[4 * u + 2], gh[4 * u + 3]);
-                    *reinterpret_cast<uint4*>(sm.sl[buf] + off) =
-                        make_uint4(gl[4 * u], gl[4 * u + 1], gl[4 * u + 2], gl[4 * u + 3]);
-                }
-            }
-            tmem_wait_st();
-            fence_async_smem();
-            tc_fence_before();
-            mbar_arrive(&sm.pds[buf]);
-        }
-        if (!failed) {
-            const int lbuf = (n_it - 1) & 1;
-            if (!mbar_wait_warp(&sm.bar_d[lbuf], ((n_it - 1) >> 1) & 1)) {
-                failed = true;
-            } else {
-                tc_fence_after();
-                // dK, dV columns 32*hf..+31 of this key row.  The TMEM loads are
-                // warp-collective and run on every lane; rows past T are not stored.
+            // dK, dV columns 32*hf..+31 of this key row.  The TMEM loads are
+            // warp-collective and run on every lane; rows past T are not stored.
+            {
                 float a[32];
                 const bool store = j < p.T;
-                float* dvr = p.dv + (base + j) * p.ld_d + h * D + 32 * hf;
-                float* dkr = p.dk + (base + j) * p.ld_d + h * D + 32 * hf;
+                const long grow = static_cast<long>(it.b) * p.T + j;
+                float* dvr = p.dv + grow * p.ld_d + it.h * D + 32 * hf;
+                float* dkr = p.dk + grow * p.ld_d + it.h * D + 32 * hf;
                 tmem_ld32(lb + tm + COL_DV + 32 * hf, a);
                 tmem_wait_ld();
                 if (store) {
@@ -458,6 +568,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                             make_float4(a[i] * p.scale, a[i + 1] * p.scale, a[i + 2] * p.scale, a[i + 3] * p.scale);
                 }
             }
+            if (!has_next) break;
+            it = nx;
         }
     }
 
@@ -496,6 +608,9 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     p.causal = a.causal;
     p.n_ktiles = (a.T + BK - 1) / BK;
     p.n_qtiles = (a.T + BQ - 1) / BQ;
+    const long n_work = static_cast<long>(p.n_ktiles) * a.B * a.H;
+    if (n_work <= 0 || n_work > INT32_MAX) return cudaErrorInvalidValue;
+    p.n_work = static_cast<int>(n_work);
     const size_t smem = sizeof(Smem) + 1024;
     int dev = 0;
     e = cudaGetDevice(&dev);
@@ -507,8 +622,9 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
         if (e != cudaSuccess) return e;
         attr_done.fetch_or(bit);
     }
-    const long nblocks = static_cast<long>(p.n_ktiles) * a.B * a.H;
-    e = launch_pdl(attn_bwd_tc64, dim3(static_cast<unsigned>(nblocks)), dim3(NTHREADS), smem, stream, p);
+    // Persistent: one CTA per SM (the shared-memory footprint allows no more).
+    const int grid = static_cast<int>(n_work < num_sms ? n_work : num_sms);
+    e = launch_pdl(attn_bwd_tc64, dim3(static_cast<unsigned>(grid)), dim3(NTHREADS), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

@@ -46,51 +46,68 @@ __device__ __forceinline__ void stage_rows(uint8_t* hi, uint8_t* lo, const float
     }
 }
 
-// Two tiles of the same shape (e.g. Q and dO, or K and V) in one pass: all
-// loads of both are in flight before the first conversion.
+// Two tiles of the same shape (e.g. Q and dO, or K and V) held in registers
+// between their loads and their conversion, so the loads can be issued early
+// and the shared-memory stores made once the destination is free.
 template <int R, int NTH>
-__device__ __forceinline__ void stage_rows2(uint8_t* hi0, uint8_t* lo0, const float* g0, long ld0, uint8_t* hi1,
-                                            uint8_t* lo1, const float* g1, long ld1, int row0, int T, int t) {
+struct Rows2 {
     static_assert((R * 8) % NTH == 0, "tile items must divide evenly");
-    constexpr int ITEMS = R * 8 / NTH;
+    static constexpr int ITEMS = R * 8 / NTH;
     float4 a[2][ITEMS], b[2][ITEMS];
-#pragma unroll
-    for (int it = 0; it < ITEMS; ++it) {
-        const int i = t + it * NTH;
-        const int r = i >> 3;
-        const int ch = i & 7;
-        a[0][it] = make_float4(0.f, 0.f, 0.f, 0.f);
-        b[0][it] = a[0][it];
-        a[1][it] = a[0][it];
-        b[1][it] = a[0][it];
-        if (row0 + r < T) {
-            const float4* s0 = reinterpret_cast<const float4*>(g0 + static_cast<long>(row0 + r) * ld0 + ch * 8);
-            const float4* s1 = reinterpret_cast<const float4*>(g1 + static_cast<long>(row0 + r) * ld1 + ch * 8);
-            a[0][it] = __ldg(s0);
-            b[0][it] = __ldg(s0 + 1);
-            a[1][it] = __ldg(s1);
-            b[1][it] = __ldg(s1 + 1);
-        }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        uint8_t* hi = u ? hi1 : hi0;
-        uint8_t* lo = u ? lo1 : lo0;
+
+    __device__ __forceinline__ void load(const float* g0, long ld0, const float* g1, long ld1, int row0, int T,
+                                         int t) {
 #pragma unroll
         for (int it = 0; it < ITEMS; ++it) {
             const int i = t + it * NTH;
             const int r = i >> 3;
             const int ch = i & 7;
-            uint4 h, l;
-            sm100::split2(a[u][it].x, a[u][it].y, h.x, l.x);
-            sm100::split2(a[u][it].z, a[u][it].w, h.y, l.y);
-            sm100::split2(b[u][it].x, b[u][it].y, h.z, l.z);
-            sm100::split2(b[u][it].z, b[u][it].w, h.w, l.w);
-            const uint32_t off = sm100::sw128(r, ch);
-            *reinterpret_cast<uint4*>(hi + off) = h;
-            *reinterpret_cast<uint4*>(lo + off) = l;
+            a[0][it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            b[0][it] = a[0][it];
+            a[1][it] = a[0][it];
+            b[1][it] = a[0][it];
+            if (row0 + r < T) {
+                const float4* s0 = reinterpret_cast<const float4*>(g0 + static_cast<long>(row0 + r) * ld0 + ch * 8);
+                const float4* s1 = reinterpret_cast<const float4*>(g1 + static_cast<long>(row0 + r) * ld1 + ch * 8);
+                a[0][it] = __ldg(s0);
+                b[0][it] = __ldg(s0 + 1);
+                a[1][it] = __ldg(s1);
+                b[1][it] = __ldg(s1 + 1);
+            }
         }
     }
+
+    __device__ __forceinline__ void store(uint8_t* hi0, uint8_t* lo0, uint8_t* hi1, uint8_t* lo1, int t) const {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            uint8_t* hi = u ? hi1 : hi0;
+            uint8_t* lo = u ? lo1 : lo0;
+#pragma unroll
+            for (int it = 0; it < ITEMS; ++it) {
+                const int i = t + it * NTH;
+                const int r = i >> 3;
+                const int ch = i & 7;
+                uint4 h, l;
+                sm100::split2(a[u][it].x, a[u][it].y, h.x, l.x);
+                sm100::split2(a[u][it].z, a[u][it].w, h.y, l.y);
+                sm100::split2(b[u][it].x, b[u][it].y, h.z, l.z);
+                sm100::split2(b[u][it].z, b[u][it].w, h.w, l.w);
+                const uint32_t off = sm100::sw128(r, ch);
+                *reinterpret_cast<uint4*>(hi + off) = h;
+                *reinterpret_cast<uint4*>(lo + off) = l;
+            }
+        }
+    }
+};
+
+// Two tiles of the same shape in one pass: all loads of both are in flight
+// before the first conversion.
+template <int R, int NTH>
+__device__ __forceinline__ void stage_rows2(uint8_t* hi0, uint8_t* lo0, const float* g0, long ld0, uint8_t* hi1,
+                                            uint8_t* lo1, const float* g1, long ld1, int row0, int T, int t) {
+    Rows2<R, NTH> x;
+    x.load(g0, ld0, g1, ld1, row0, T, t);
+    x.store(hi0, lo0, hi1, lo1, t);
 }
 
 }  // namespace tc
