@@ -93,6 +93,8 @@ struct alignas(1024) Smem {
     uint64_t pds[2];      // P / dS of the tile in buffer b written
     uint64_t bar_d[2];    // gradient products of the tile in buffer b done
     uint64_t dq_free[2];  // dQ accumulator b read out by the loaders
+    uint64_t stg_full;    // dK / dV staging written (phase r: item r)
+    uint64_t stg_done;    // dK / dV staging stored to global
     uint32_t tmem_slot;
 };
 
@@ -283,6 +285,52 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
     }
 }
 
+// dK, dV of the CTA's item r -> global, by the elementwise warps.  Warp
+// (qd, hf) reads its 32 key rows x 32 columns of each accumulator (TMEM loads
+// are warp-collective and run on every lane) into the idle dS^T buffers, laid
+// out [row][16 float4] with the float4 index XOR-swizzled by row; then the 256
+// threads store whole 256-byte rows, two per warp instruction.  Rows past T
+// are not stored.  The dS^T buffers are free: the item's last dQ product has
+// completed and the next item's tiles are written by these same warps after
+// the second barrier.  The barriers are mbarriers with bounded waits, so a
+// warp that gave up earlier cannot leave the others blocked.
+__device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm, const Item& it, uint32_t lb,
+                                          int row, int hf, int tid, int r) {
+    float4* stg_v = reinterpret_cast<float4*>(sm.sh[0]);  // 128 rows x 256 B = 32 KB (sh[0], sh[1])
+    float4* stg_k = reinterpret_cast<float4*>(sm.sl[0]);
+    float a[32];
+    tmem_ld32(lb + tm + COL_DV + 32 * hf, a);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        stg_v[row * 16 + ((8 * hf + i) ^ (row & 15))] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
+    tmem_ld32(lb + tm + COL_DK + 32 * hf, a);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        stg_k[row * 16 + ((8 * hf + i) ^ (row & 15))] =
+            make_float4(a[4 * i] * p.scale, a[4 * i + 1] * p.scale, a[4 * i + 2] * p.scale, a[4 * i + 3] * p.scale);
+    mbar_arrive(&sm.stg_full);
+    if (!mbar_wait_warp(&sm.stg_full, r & 1)) return false;
+    const long row0 = static_cast<long>(it.b) * p.T + it.k0;
+    float* dvg = p.dv + row0 * p.ld_d + it.h * D;
+    float* dkg = p.dk + row0 * p.ld_d + it.h * D;
+#pragma unroll
+    for (int k = 0; k < BK * 16 / NELEM; ++k) {
+        const int i = tid + k * NELEM;
+        const int r = i >> 4;
+        const int c4 = i & 15;
+        if (it.k0 + r < p.T) {
+            const float4 v = stg_v[r * 16 + (c4 ^ (r & 15))];
+            const float4 g = stg_k[r * 16 + (c4 ^ (r & 15))];
+            *reinterpret_cast<float4*>(dvg + r * p.ld_d + c4 * 4) = v;
+            *reinterpret_cast<float4*>(dkg + r * p.ld_d + c4 * 4) = g;
+        }
+    }
+    mbar_arrive(&sm.stg_done);  // staging reads done before the next tile's dS^T writes
+    return mbar_wait_warp(&sm.stg_done, r & 1);
+}
+
 __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     pdl_enter();
     extern __shared__ uint8_t smem_raw[];
@@ -312,6 +360,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         }
         mbar_init(&sm.pds[0], NELEM);
         mbar_init(&sm.pds[1], NELEM);
+        mbar_init(&sm.stg_full, NELEM);
+        mbar_init(&sm.stg_done, NELEM);
     }
     tc_fence_before();
     __syncthreads();
@@ -544,29 +594,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 break;
             }
             tc_fence_after();
-            // dK, dV columns 32*hf..+31 of this key row.  The TMEM loads are
-            // warp-collective and run on every lane; rows past T are not stored.
-            {
-                float a[32];
-                const bool store = j < p.T;
-                const long grow = static_cast<long>(it.b) * p.T + j;
-                float* dvr = p.dv + grow * p.ld_d + it.h * D + 32 * hf;
-                float* dkr = p.dk + grow * p.ld_d + it.h * D + 32 * hf;
-                tmem_ld32(lb + tm + COL_DV + 32 * hf, a);
-                tmem_wait_ld();
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(dvr + i) = make_float4(a[i], a[i + 1], a[i + 2], a[i + 3]);
-                }
-                tmem_ld32(lb + tm + COL_DK + 32 * hf, a);
-                tmem_wait_ld();
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(dkr + i) =
-                            make_float4(a[i] * p.scale, a[i + 1] * p.scale, a[i + 2] * p.scale, a[i + 3] * p.scale);
-                }
+            if (!store_dkv(p, sm, tm, it, lb, row, hf, tid, r)) {
+                failed = true;
+                break;
             }
             if (!has_next) break;
             it = nx;
