@@ -264,24 +264,24 @@ __device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, in
 }
 
 // A dQ tile (M=64 accumulator: query row 16*qd + l sits in lane 32*qd + l,
-// l < 16), scaled and added into dq by the loader warp of lane quadrant qd.
+// l < 16), scaled and added into dq by the loader warp of lane quadrant qd,
+// 32 columns at a time.
 __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int lane, int q0,
                                             float* dqg) {
-    float v0[32], v1[32];
     const uint32_t ta = (static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b);
-    tmem_ld32(ta, v0);
-    tmem_ld32(ta + 32, v1);
-    tmem_wait_ld();
     const int r = q0 + qd * 16 + lane;
-    if (lane < 16 && r < p.T) {
-        float* dst = dqg + static_cast<long>(r) * p.ld_d;
+    float* dst = dqg + static_cast<long>(r) * p.ld_d;
 #pragma unroll
-        for (int c = 0; c < 32; c += 4)
-            red_add_v4(dst + c, v0[c] * p.scale, v0[c + 1] * p.scale, v0[c + 2] * p.scale, v0[c + 3] * p.scale);
+    for (int h = 0; h < 2; ++h) {
+        float v[32];
+        tmem_ld32(ta + 32 * h, v);
+        tmem_wait_ld();
+        if (lane < 16 && r < p.T) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 4)
-            red_add_v4(dst + 32 + c, v1[c] * p.scale, v1[c + 1] * p.scale, v1[c + 2] * p.scale,
-                       v1[c + 3] * p.scale);
+            for (int c = 0; c < 32; c += 4)
+                red_add_v4(dst + 32 * h + c, v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale,
+                           v[c + 3] * p.scale);
+        }
     }
 }
 
@@ -371,34 +371,47 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
 
     if (warp >= NELEM / 32 && warp < MMA_WARP) {
         // ------------------------------------------------------------ loaders
-        // Step n stages the CTA's query tile n, then adds tile n-2's dQ into
-        // dq (gradient products finish in tile order, and loading runs ahead).
+        // Step n writes the CTA's query tile n into its ring stage from
+        // registers, issues the global loads of tile n+1 into registers, then
+        // adds tile n-2's dQ into dq (gradient products finish in tile
+        // order): the loads are in flight while the step waits for that dQ.
         const int t = tid - NELEM;
         const int qd = warp & 3;
         Cursor cl, cq;  // tile to load, tile whose dQ is added
         cl.start(p, c, G);
         cq.start(p, c, G);
+        tc::Rows2<BQ, NLOAD> x;
+        float lse_t = 0.f, ds_t = 0.f;
+        auto prefetch = [&]() {
+            const Item it = make_item(p, cl.w);
+            const long base = static_cast<long>(it.b) * p.T;
+            const int q0 = (cl.it0 + cl.n) * BQ;
+            x.load(p.q + base * p.ld_qkv + it.h * D, p.ld_qkv, p.dout + base * p.ld_o + it.h * D, p.ld_o, q0, p.T,
+                   t);
+            if (t < BQ) {
+                const long bh = (static_cast<long>(it.b) * p.H + it.h) * p.T;
+                const bool ok = q0 + t < p.T;
+                lse_t = ok ? p.lse[bh + q0 + t] * kLog2e : INFINITY;
+                ds_t = ok ? p.dsum[bh + q0 + t] : 0.f;
+            }
+        };
+        if (cl.valid()) prefetch();
         for (int n = 0; !failed; ++n) {
             if (cl.valid()) {
-                const Item it = make_item(p, cl.w);
-                const long base = static_cast<long>(it.b) * p.T;
                 const int s = n % STAGES;
-                const int q0 = (cl.it0 + cl.n) * BQ;
                 if (n >= STAGES && !mbar_wait_warp(&sm.empty[s], ((n - STAGES) / STAGES) & 1)) {
                     failed = true;  // warp-uniform: the dQ epilogue below is warp-collective
                     break;
                 }
                 if (t < BQ) {
-                    const long bh = (static_cast<long>(it.b) * p.H + it.h) * p.T;
-                    const bool ok = q0 + t < p.T;
-                    sm.lse2[s][t] = ok ? p.lse[bh + q0 + t] * kLog2e : INFINITY;
-                    sm.dsum[s][t] = ok ? p.dsum[bh + q0 + t] : 0.f;
+                    sm.lse2[s][t] = lse_t;
+                    sm.dsum[s][t] = ds_t;
                 }
-                tc::stage_rows2<BQ, NLOAD>(sm.qh[s], sm.ql[s], p.q + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.gh[s],
-                                           sm.gl[s], p.dout + base * p.ld_o + it.h * D, p.ld_o, q0, p.T, t);
+                x.store(sm.qh[s], sm.ql[s], sm.gh[s], sm.gl[s], t);
                 fence_async_smem();
                 mbar_arrive(&sm.full[s]);
                 cl.next(p, c, G);
+                if (cl.valid()) prefetch();
             }
             if (n >= 2) {
                 if (!cq.valid()) break;
