@@ -448,11 +448,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 bool progressed = false;
                 if (cs.valid() && ns < ng + 2) {
                     bool kv_ok = kv_round >= cs.r;
-                    if (!kv_ok && mbar_try_wait(&sm.kv_full, cs.r & 1)) {
+                    if (!kv_ok && mbar_test_wait(&sm.kv_full, cs.r & 1)) {
                         kv_round = cs.r;
                         kv_ok = true;
                     }
-                    if (kv_ok && mbar_try_wait(&sm.full[ns % STAGES], (ns / STAGES) & 1)) {
+                    if (kv_ok && mbar_test_wait(&sm.full[ns % STAGES], (ns / STAGES) & 1)) {
                         tc_fence_after();
                         issue_sdp(d, tm, ns % STAGES, ns & 1);
                         mma_commit(&sm.bar_s[ns & 1]);
@@ -461,8 +461,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                         progressed = true;
                     }
                 }
-                if (ng < ns && mbar_try_wait(&sm.pds[ng & 1], (ng >> 1) & 1) &&
-                    (ng < 2 || mbar_try_wait(&sm.dq_free[ng & 1], ((ng - 2) >> 1) & 1))) {
+                if (ng < ns && mbar_test_wait(&sm.pds[ng & 1], (ng >> 1) & 1) &&
+                    (ng < 2 || mbar_test_wait(&sm.dq_free[ng & 1], ((ng - 2) >> 1) & 1))) {
                     tc_fence_after();
                     issue_dq(d, tm, ng & 1);
                     if (cg.n == cg.n_it - 1) mma_commit(&sm.kv_free);
