@@ -336,12 +336,13 @@ static BwdParams make_params(const BwdArgs& a) {
 }
 
 template <int D>
-static cudaError_t launch_prep_d(const BwdParams& p, int num_sms, cudaStream_t stream, int* launches) {
+static cudaError_t launch_prep_d(const BwdParams& p, int /*num_sms*/, cudaStream_t stream, int* launches) {
+    // One row per (warp, lane group): every load is issued at once rather
+    // than in grid-stride rounds (the kernel is bound by memory latency).
     const long nrows = static_cast<long>(p.B) * p.T * p.H;
     const long rows_per_block = (256 / 32) * (32 / (D / 4));
     long blocks = (nrows + rows_per_block - 1) / rows_per_block;
-    const long cap = static_cast<long>(num_sms > 0 ? num_sms : 148) * 8;
-    if (blocks > cap) blocks = cap;
+    if (blocks > 0x7fffffffL) blocks = 0x7fffffffL;
     cudaError_t e = launch_pdl(attn_bwd_rowdot<D>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
