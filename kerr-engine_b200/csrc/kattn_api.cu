@@ -147,7 +147,7 @@ int ok_with_launches(int n) {
 // Forward launch on the kernel family the context selects.
 cudaError_t dispatch_fwd(kattn_ctx* ctx, const kattn::FwdArgs& a, cudaStream_t s, int* launches) {
     const int path = ctx->path.load(std::memory_order_relaxed);
-    if (path != KATTN_PATH_FFMA && kattn::fwd_tc_supported(a)) return kattn::launch_fwd_tc(a, ctx->d_status, s, launches);
+    if (path != KATTN_PATH_FFMA && kattn::fwd_tc_supported(a)) return kattn::launch_fwd_tc(a, ctx->num_sms, ctx->d_status, s, launches);
     return kattn::launch_fwd(a, ctx->num_sms, s, launches);
 }
 

@@ -6,16 +6,20 @@
 // f32 accumulation in tensor memory (relative error ~1e-5, inside the 1e-4
 // forward tolerance; a single bf16 or tf32 product is not).
 //
-// CTA = 128 query rows of one (batch, head) slab, 128 threads; thread t owns
+// Work item = 128 query rows of one (batch, head) slab.  The kernel is
+// persistent: two CTAs of 128 threads per SM, CTA c taking items c, 2G-1-c,
+// 2G+c, ... of the list ordered longest first (a snake order: at the 768-dim
+// shape 192 CTAs run one long item, 88 run two short ones).  Thread t owns
 // query row t (TMEM lane t).  Per 64-row key tile j:
-//   S_j = Q K_j^T        tcgen05.mma SS, M=128 N=64, 3 x 4 k-steps -> TMEM buffer j&1
+//   S_j = Q K_j^T        tcgen05.mma SS, M=128 N=64, 3 x 4 k-steps -> TMEM buffer g&1
 //   softmax (online, log2 domain) in registers; P_j hi/lo written over S_j
-//   O_j = P_j V_j        tcgen05.mma TS (P from TMEM), V MN-major  -> TMEM buffer j&1
+//   O_j = P_j V_j        tcgen05.mma TS (P from TMEM), V MN-major  -> TMEM buffer g&1
 //   O <- O * alpha + O_j in registers, one tile later
 // PV_j and S_{j+1} are issued together; while they run the threads fold in
 // O_{j-1} and stage K_{j+2} and V_{j+1} (K and V tiles have separate
-// lifetimes: K_j is free once S_j is done, V_j once PV_j is).  ~99 KB of
-// shared memory and 256 TMEM columns per CTA: two CTAs share an SM.
+// lifetimes: K_j is free once S_j is done, V_j once PV_j is).  g counts the
+// CTA's tiles across its items (buffers, stages and barrier phases).  ~99 KB
+// of shared memory and 256 TMEM columns per CTA: two CTAs share an SM.
 #include <atomic>
 
 #include "kattn_common.cuh"
@@ -66,6 +70,7 @@ struct Params {
     int causal;
     int n_qtiles;
     int n_ktiles;
+    int n_work;  // items: n_qtiles * B * H
 };
 
 // Shared-memory descriptors of the Q tile and of K / V stage 0 (stage 1 is
@@ -121,20 +126,10 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
     const int nslab = p.B * p.H;
-    const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x / nslab);  // longest rows first
-    const int slab = static_cast<int>(blockIdx.x % nslab);
-    const int b = slab / p.H;
-    const int h = slab % p.H;
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
-    const int q0 = qt * BM;
-    const int row = q0 + tid;
-    const int n_kv = p.causal ? min(p.n_ktiles, (q0 + BM + BN - 1) / BN) : p.n_ktiles;
-
-    const long base = static_cast<long>(b) * p.T;
-    const float* qg = p.q + base * p.ld_qkv + h * D;
-    const float* kg = p.k + base * p.ld_qkv + h * D;
-    const float* vg = p.v + base * p.ld_qkv + h * D;
+    const int cta = static_cast<int>(blockIdx.x);
+    const int G = static_cast<int>(gridDim.x);
 
     if (warp == 0) {
         tmem_alloc(&sm.tmem_slot, TMEM_COLS);
@@ -146,29 +141,54 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
             mbar_init(&sm.bar_o[i], 1);
         }
     }
-    tc::stage_rows2<BN, NT>(sm.kh[0], sm.kl[0], kg, p.ld_qkv, sm.vh[0], sm.vl[0], vg, p.ld_qkv, 0, p.T, tid);
-    tc::stage_rows<BM, NT>(sm.qh, sm.ql, qg, p.ld_qkv, q0, p.T, p.scale_log2, tid);
-    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = sm.tmem_slot;
     Descs dsc;
-    if (tid == 0) {
-        dsc = make_descs(sm);
-        issue_s(dsc, tm, 0, 0);
-        mma_commit(&sm.bar_s[0]);
-    }
-    if (n_kv > 1) tc::stage_rows<BN, NT>(sm.kh[1], sm.kl[1], kg, p.ld_qkv, BN, p.T, 1.f, tid);
-    fence_async_smem();
+    if (tid == 0) dsc = make_descs(sm);
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    bool failed = false;
+    int g = 0;  // the CTA's tile sequence number: TMEM buffer and K / V stage g&1, barrier phases
+
+    for (int r = 0; !failed; ++r) {
+    // Item r of this CTA in the snake order over the items (longest first).
+    const int w = r * G + ((r & 1) ? G - 1 - cta : cta);
+    if (w >= p.n_work) break;
+    const int qt = p.n_qtiles - 1 - w / nslab;
+    const int slab = w % nslab;
+    const int b = slab / p.H;
+    const int h = slab % p.H;
+    const int q0 = qt * BM;
+    const int row = q0 + tid;
+    const int n_kv = p.causal ? min(p.n_ktiles, (q0 + BM + BN - 1) / BN) : p.n_ktiles;
+
+    const long base = static_cast<long>(b) * p.T;
+    const float* qg = p.q + base * p.ld_qkv + h * D;
+    const float* kg = p.k + base * p.ld_qkv + h * D;
+    const float* vg = p.v + base * p.ld_qkv + h * D;
+    const int g0 = g;
+
+    // Every stage and buffer is free: the previous item's last P V is done.
+    tc::stage_rows2<BN, NT>(sm.kh[g0 & 1], sm.kl[g0 & 1], kg, p.ld_qkv, sm.vh[g0 & 1], sm.vl[g0 & 1], vg, p.ld_qkv, 0,
+                            p.T, tid);
+    tc::stage_rows<BM, NT>(sm.qh, sm.ql, qg, p.ld_qkv, q0, p.T, p.scale_log2, tid);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+        issue_s(dsc, tm, g0 & 1, g0 & 1);
+        mma_commit(&sm.bar_s[g0 & 1]);
+    }
+    if (n_kv > 1) tc::stage_rows<BN, NT>(sm.kh[(g0 + 1) & 1], sm.kl[(g0 + 1) & 1], kg, p.ld_qkv, BN, p.T, 1.f, tid);
+    fence_async_smem();
 
     float o[D];
 #pragma unroll
     for (int c = 0; c < D; ++c) o[c] = 0.f;
     float m = -INFINITY, l = 0.f;
     float alpha_prev = 1.f;  // rescale factor of the tile whose P V is still pending
-    bool failed = false;
 
     // O <- O * alpha + (P V tile in buffer b).
     auto fold = [&](int b, float alpha) {
@@ -182,10 +202,10 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         }
     };
 
-    for (int j = 0; j < n_kv; ++j) {
-        const int bf = j & 1;  // TMEM buffer / smem stage of tile j
+    for (int j = 0; j < n_kv; ++j, ++g) {
+        const int bf = g & 1;  // TMEM buffer / smem stage of tile j
         const int k0 = j * BN;
-        const bool ok_s = mbar_wait(&sm.bar_s[bf], (j >> 1) & 1);
+        const bool ok_s = mbar_wait(&sm.bar_s[bf], (g >> 1) & 1);
         if (__syncthreads_or(!ok_s)) {
             failed = true;
             break;
@@ -251,7 +271,7 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         }
         if (j >= 1) {
             // Fold in the previous tile's P V (its buffer is the other one).
-            const bool ok_o = mbar_wait(&sm.bar_o[bf ^ 1], ((j - 1) >> 1) & 1);
+            const bool ok_o = mbar_wait(&sm.bar_o[bf ^ 1], ((g - 1) >> 1) & 1);
             if (__syncthreads_or(!ok_o)) {
                 failed = true;
                 break;
@@ -266,30 +286,25 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         const bool kn = j + 2 < n_kv, vn = j + 1 < n_kv && j >= 1;
         if (kn) tc::stage_rows<BN, NT>(sm.kh[bf], sm.kl[bf], kg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
         if (vn) tc::stage_rows<BN, NT>(sm.vh[bf ^ 1], sm.vl[bf ^ 1], vg, p.ld_qkv, (j + 1) * BN, p.T, 1.f, tid);
-        if (j == 0 && n_kv > 1) tc::stage_rows<BN, NT>(sm.vh[1], sm.vl[1], vg, p.ld_qkv, BN, p.T, 1.f, tid);
+        if (j == 0 && n_kv > 1) tc::stage_rows<BN, NT>(sm.vh[bf ^ 1], sm.vl[bf ^ 1], vg, p.ld_qkv, BN, p.T, 1.f, tid);
         if (kn || vn || j == 0) fence_async_smem();
     }
 
     if (!failed) {
-        const int jl = n_kv - 1;
-        const bool ok_o = mbar_wait(&sm.bar_o[jl & 1], (jl >> 1) & 1);
+        const int gl = g - 1;
+        const bool ok_o = mbar_wait(&sm.bar_o[gl & 1], (gl >> 1) & 1);
         if (__syncthreads_or(!ok_o)) {
             failed = true;
         } else {
             tc_fence_after();
-            fold(jl & 1, alpha_prev);
+            fold(gl & 1, alpha_prev);
         }
     }
 
-    if (failed) {
-        if (tid == 0) atomicOr(p.status, 1);
-        // Let any MMA still in flight drain (bounded) before the columns are freed.
-        if (tid == 0) mma_commit(&sm.bar_s[0]);
-        mbar_wait(&sm.bar_s[0], 0, 10000000ull);
-        mbar_wait(&sm.bar_s[0], 1, 10000000ull);
-    } else {
-        // Normalise and stage O through shared memory (reusing the Q tiles,
-        // float4 chunks XOR-swizzled by row) for coalesced global stores.
+    if (failed) break;
+    // Normalise and stage O through shared memory (reusing the Q tiles,
+    // float4 chunks XOR-swizzled by row) for coalesced global stores.
+    {
         const float inv = 1.f / l;
         float4* stg = reinterpret_cast<float4*>(sm.qh);  // 128 rows x 16 float4 = 32 KB (qh + ql)
         __syncthreads();
@@ -303,12 +318,26 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
 #pragma unroll
         for (int it = 0; it < 16; ++it) {
             const int i = tid + it * NT;
-            const int r = i >> 4;
+            const int rr = i >> 4;
             const int c4 = i & 15;
-            if (q0 + r < p.T)
-                *reinterpret_cast<float4*>(og + static_cast<long>(q0 + r) * p.ld_o + c4 * 4) =
-                    stg[r * 16 + (c4 ^ (r & 15))];
+            if (q0 + rr < p.T)
+                *reinterpret_cast<float4*>(og + static_cast<long>(q0 + rr) * p.ld_o + c4 * 4) =
+                    stg[rr * 16 + (c4 ^ (rr & 15))];
         }
+    }
+    // The next item stages its Q over the rows just read, and its MMAs reuse
+    // the TMEM buffers this item's threads have read.
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    }
+
+    if (failed) {
+        if (tid == 0) atomicOr(p.status, 1);
+        // Let any MMA still in flight drain (bounded) before the columns are freed.
+        if (tid == 0) mma_commit(&sm.bar_s[0]);
+        mbar_wait(&sm.bar_s[0], 0, 10000000ull);
+        mbar_wait(&sm.bar_s[0], 1, 10000000ull);
     }
     tc_fence_before();
     __syncthreads();
@@ -319,7 +348,7 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
 
 bool fwd_tc_supported(const FwdArgs& a) { return a.d == 64; }
 
-cudaError_t launch_fwd_tc(const FwdArgs& a, int* status, cudaStream_t stream, int* launches) {
+cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches) {
     Params p;
     p.q = a.q;
     p.k = a.k;
@@ -336,6 +365,9 @@ cudaError_t launch_fwd_tc(const FwdArgs& a, int* status, cudaStream_t stream, in
     p.causal = a.causal;
     p.n_qtiles = (a.T + BM - 1) / BM;
     p.n_ktiles = (a.T + BN - 1) / BN;
+    const long n_work = static_cast<long>(p.n_qtiles) * a.B * a.H;
+    if (n_work <= 0 || n_work > INT32_MAX) return cudaErrorInvalidValue;
+    p.n_work = static_cast<int>(n_work);
     const size_t smem = sizeof(Smem) + 1024;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -347,8 +379,11 @@ cudaError_t launch_fwd_tc(const FwdArgs& a, int* status, cudaStream_t stream, in
         if (e != cudaSuccess) return e;
         attr_done.fetch_or(bit);
     }
-    const long nblocks = static_cast<long>(p.n_qtiles) * a.B * a.H;
-    e = launch_pdl(attn_fwd_tc64, dim3(static_cast<unsigned>(nblocks)), dim3(NT), smem, stream, p);
+    // Persistent: two CTAs per SM (shared memory and TMEM allow two), each
+    // walking its items in the snake order.
+    const long slots = 2L * (num_sms > 0 ? num_sms : 148);
+    const int grid = static_cast<int>(n_work < slots ? n_work : slots);
+    e = launch_pdl(attn_fwd_tc64, dim3(static_cast<unsigned>(grid)), dim3(NT), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

@@ -64,7 +64,7 @@ cudaError_t launch_bwd(const BwdArgs& a, int num_sms, cudaStream_t stream, int* 
 // Tensor-core (tcgen05) kernels.  `status` is a device word the kernels set
 // (bit 0) when a bounded wait on the tensor core gives up.
 bool fwd_tc_supported(const FwdArgs& a);
-cudaError_t launch_fwd_tc(const FwdArgs& a, int* status, cudaStream_t stream, int* launches);
+cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches);
 bool bwd_tc_supported(const BwdArgs& a);
 cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches);
 
