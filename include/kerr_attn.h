@@ -149,8 +149,35 @@ int kattn_bwd_host(kattn_ctx* ctx,
                    int B, int T, int H, int d, float scale, int causal);
 
 /* Number of kernel launches the last kattn_fwd / kattn_bwd call on this
- * thread enqueued (0 for an empty problem or an error). */
+ * thread enqueued (0 for an empty problem or an error).  For the
+ * kattn_linear_* calls: this library's kernels, not the cuBLAS GEMMs. */
 int kattn_last_launch_count(void);
+
+/* ---- Attention projections c_attn / c_proj (dense layers) -----------------
+ * Replace CpuBackend::linear_batch (src/backend.rs:296-298, :508-520),
+ * linear_backward_dx_batch (src/backend.rs:316-318 -> src/backward.rs:48-60)
+ * and outer_product_accum (src/backend.rs:320-342) at src/pipeline.rs:289,
+ * :353 and :695-737.  Rows are positions (M = B*T); weights keep the
+ * reference's [out][in] layout (src/model.rs:184-185): w is [N][K]
+ * contiguous.  Device pointers, 16-byte aligned; every row stride and K, N
+ * a multiple of 4 floats.  Each product is formed in bf16 hi/lo pairs
+ * (hi*hi + hi*lo + lo*hi, f32 accumulation; ~1e-5 relative) by three cuBLAS
+ * GEMMs over operands this library splits.  Workspace comes from the
+ * device's stream-ordered pool; nothing synchronises the host. */
+
+/* y[m][n] = b[n] + sum_k w[n][k] x[m][k];  b may be NULL (no bias). */
+int kattn_linear_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, const float* b,
+                     float* y, long ld_y, int M, int N, int K, void* stream);
+
+/* dx[m][k] = sum_n dy[m][n] w[n][k]  (dx fully overwritten). */
+int kattn_linear_bwd_dx(kattn_ctx* ctx, const float* dy, long ld_dy, const float* w,
+                        float* dx, long ld_dx, int M, int N, int K, void* stream);
+
+/* dw[n][k] (+)= sum_m dy[m][n] x[m][k] and db[n] (+)= sum_m dy[m][n]: added
+ * to dw / db when accumulate != 0 (the += of src/pipeline.rs:701-704,
+ * :733-736), written otherwise.  dw is [N][K] contiguous; db may be NULL. */
+int kattn_linear_bwd_dw(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
+                        float* dw, float* db, int M, int N, int K, int accumulate, void* stream);
 
 #ifdef __cplusplus
 }

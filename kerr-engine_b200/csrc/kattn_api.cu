@@ -1,5 +1,6 @@
 // C ABI of the attention path (include/kerr_attn.h): argument checking,
 // device contexts, workspace handling and the host-buffer entry points.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <climits>
@@ -24,6 +25,8 @@ struct kattn_ctx {
     char* arena = nullptr;          // device staging for the host-buffer entry points
     size_t arena_bytes = 0;
     float* noalloc_ws = nullptr;    // device address of g_noalloc_ws on this device
+    void* cublas = nullptr;         // cublasHandle_t of the projection GEMMs, created on first use
+    std::mutex proj_mu;             // binds the handle to a stream and enqueues a call as one step
 };
 
 // Fixed backward workspace of kattn_bwd_noalloc: [B][H][T] floats, shared by
@@ -165,6 +168,46 @@ int path_check(const kattn_ctx* ctx, int d) {
     return KATTN_OK;
 }
 
+// Checks of a row-major f32 operand of the projection calls: rows x cols at
+// row stride ld, 16-byte aligned, ld and cols multiples of 4 floats.
+int check_matrix(const char* name, const void* p, long ld, long rows, long cols) {
+    if (rows > 0 && cols > 0 && !p) return fail(KATTN_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+    if (ld < cols) return fail(KATTN_ERR_INVALID_ARGUMENT, "%s row stride %ld < %ld columns", name, ld, cols);
+    if (p && reinterpret_cast<uintptr_t>(p) % 16 != 0)
+        return fail(KATTN_ERR_MISALIGNED, "%s is not 16-byte aligned", name);
+    if (ld % 4 != 0 || cols % 4 != 0)
+        return fail(KATTN_ERR_MISALIGNED, "%s row stride %ld / width %ld not a multiple of 4", name, ld, cols);
+    return KATTN_OK;
+}
+
+int check_dims(int M, int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return fail(KATTN_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d K=%d)", M, N, K);
+    if (static_cast<long>(M) * N > INT_MAX || static_cast<long>(M) * K > INT_MAX || static_cast<long>(N) * K > INT_MAX)
+        return fail(KATTN_ERR_INVALID_ARGUMENT, "problem too large (M=%d N=%d K=%d)", M, N, K);
+    return KATTN_OK;
+}
+
+// The context's cuBLAS handle bound to `stream` (created on first use; the
+// caller holds proj_mu and has the context's device current).
+int proj_handle(kattn_ctx* ctx, cudaStream_t stream, void** out) {
+    if (!ctx->cublas) {
+        cublasHandle_t h = nullptr;
+        const cublasStatus_t st = cublasCreate(&h);
+        if (st != CUBLAS_STATUS_SUCCESS) return fail(KATTN_ERR_CUDA, "cublasCreate: status %d", static_cast<int>(st));
+        ctx->cublas = h;
+    }
+    const cublasStatus_t st = cublasSetStream(static_cast<cublasHandle_t>(ctx->cublas), stream);
+    if (st != CUBLAS_STATUS_SUCCESS) return fail(KATTN_ERR_CUDA, "cublasSetStream: status %d", static_cast<int>(st));
+    *out = ctx->cublas;
+    return KATTN_OK;
+}
+
+int proj_result(const kattn::ProjStatus& st, int launches) {
+    if (st.cuda != cudaSuccess) return cuda_fail(st.cuda, st.what);
+    if (st.cublas != 0) return fail(KATTN_ERR_CUDA, "%s: cuBLAS status %d", st.what, st.cublas);
+    return ok_with_launches(launches);
+}
+
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 int ensure_arena(kattn_ctx* ctx, size_t bytes) {
@@ -286,6 +329,7 @@ int kattn_destroy(kattn_ctx* ctx) {
         }
         if (ctx->arena) cudaFree(ctx->arena);
         if (ctx->d_status) cudaFree(ctx->d_status);
+        if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
     }
     delete ctx;
     return status;
@@ -470,6 +514,71 @@ int kattn_bwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* 
     e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
     return ok_with_launches(launches);
+}
+
+int kattn_linear_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, const float* b, float* y, long ld_y,
+                     int M, int N, int K, void* stream) {
+    g_last_launches = 0;
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    KATTN_TRY(check_dims(M, N, K));
+    KATTN_TRY(check_matrix("x", x, ld_x, M, K));
+    KATTN_TRY(check_matrix("w", w, K, N, K));
+    KATTN_TRY(check_matrix("y", y, ld_y, M, N));
+    if (b && reinterpret_cast<uintptr_t>(b) % 4 != 0) return fail(KATTN_ERR_MISALIGNED, "b is not 4-byte aligned");
+    if (M == 0 || N == 0) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    std::lock_guard<std::mutex> lock(ctx->proj_mu);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* h = nullptr;
+    KATTN_TRY(proj_handle(ctx, s, &h));
+    int launches = 0, gemms = 0;
+    const kattn::ProjStatus st =
+        kattn::proj_forward(h, ctx->num_sms, s, x, ld_x, w, b, y, ld_y, M, N, K, &launches, &gemms);
+    return proj_result(st, launches);
+}
+
+int kattn_linear_bwd_dx(kattn_ctx* ctx, const float* dy, long ld_dy, const float* w, float* dx, long ld_dx, int M,
+                        int N, int K, void* stream) {
+    g_last_launches = 0;
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    KATTN_TRY(check_dims(M, N, K));
+    KATTN_TRY(check_matrix("dy", dy, ld_dy, M, N));
+    KATTN_TRY(check_matrix("w", w, K, N, K));
+    KATTN_TRY(check_matrix("dx", dx, ld_dx, M, K));
+    if (M == 0 || K == 0) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    std::lock_guard<std::mutex> lock(ctx->proj_mu);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* h = nullptr;
+    KATTN_TRY(proj_handle(ctx, s, &h));
+    int launches = 0, gemms = 0;
+    const kattn::ProjStatus st =
+        kattn::proj_backward_dx(h, ctx->num_sms, s, dy, ld_dy, w, dx, ld_dx, M, N, K, &launches, &gemms);
+    return proj_result(st, launches);
+}
+
+int kattn_linear_bwd_dw(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x, float* dw, float* db,
+                        int M, int N, int K, int accumulate, void* stream) {
+    g_last_launches = 0;
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    KATTN_TRY(check_dims(M, N, K));
+    KATTN_TRY(check_matrix("dy", dy, ld_dy, M, N));
+    KATTN_TRY(check_matrix("x", x, ld_x, M, K));
+    KATTN_TRY(check_matrix("dw", dw, K, N, K));
+    if (db && reinterpret_cast<uintptr_t>(db) % 4 != 0) return fail(KATTN_ERR_MISALIGNED, "db is not 4-byte aligned");
+    if (N == 0 || (K == 0 && !db)) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    std::lock_guard<std::mutex> lock(ctx->proj_mu);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* h = nullptr;
+    KATTN_TRY(proj_handle(ctx, s, &h));
+    int launches = 0, gemms = 0;
+    const kattn::ProjStatus st = kattn::proj_backward_dw(h, ctx->num_sms, s, dy, ld_dy, x, ld_x, dw, db, M, N, K,
+                                                         accumulate, &launches, &gemms);
+    return proj_result(st, launches);
 }
 
 #pragma GCC visibility pop

@@ -71,4 +71,24 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
 // D = rowsum(dout * o) into a.dsum and dq = 0 (first kernel of every backward).
 cudaError_t launch_bwd_prep(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches);
 
+// Projection GEMMs (kproj.cu).  The outcome of a call: a CUDA error, or a
+// cuBLAS status (cublasStatus_t as int), with the step that failed.
+struct ProjStatus {
+    cudaError_t cuda = cudaSuccess;
+    int cublas = 0;
+    const char* what = nullptr;
+    bool ok() const { return cuda == cudaSuccess && cublas == 0; }
+};
+
+// `handle` is a cublasHandle_t already bound to `stream`.  Arrays are
+// row-major f32; w is [N][K] contiguous, dw [N][K] contiguous.  *launches
+// counts this library's kernels, *gemms the cuBLAS GEMM calls.
+ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t stream, const float* x, long ld_x, const float* w,
+                        const float* b, float* y, long ld_y, int M, int N, int K, int* launches, int* gemms);
+ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t stream, const float* dy, long ld_dy,
+                            const float* w, float* dx, long ld_dx, int M, int N, int K, int* launches, int* gemms);
+ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t stream, const float* dy, long ld_dy,
+                            const float* x, long ld_x, float* dw, float* db, int M, int N, int K, int accumulate,
+                            int* launches, int* gemms);
+
 }  // namespace kattn

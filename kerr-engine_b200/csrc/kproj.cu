@@ -1,0 +1,246 @@
+// The attention projections c_attn and c_proj as dense GEMMs (sm_100a):
+// forward y = x W^T + b, and the backward dx = dy W, dW (+)= dy^T x,
+// db (+)= colsum(dy).  Replaces CpuBackend::linear_batch (src/backend.rs:296-298,
+// :508-520), linear_backward_dx_batch (src/backend.rs:316-318 ->
+// src/backward.rs:48-60) and outer_product_accum (src/backend.rs:320-342) at
+// the call sites src/pipeline.rs:289, :353, :695-737.
+//
+// Numerics: each f32 operand is split by the kernels below into bf16 hi and
+// lo = bf16(x - hi) (the same split as the attention kernels), and every
+// product is formed as hi*hi + hi*lo + lo*hi by three cuBLAS bf16 GEMMs with
+// f32 accumulation into the same output: relative error ~1e-5, where a single
+// bf16 or tf32 GEMM would give ~1e-3.  These are plain GEMMs, so the library
+// runs them; the split, bias and column-sum kernels are this library's.
+//
+// Row-major f32 [rows][ld] arrays map onto cuBLAS's column-major view as
+// their transposes:
+//   forward: y^T (N x M)  = W (T of the K x N view of w) * x^T (K x M)
+//   dx     : dx^T (K x M) = w^T (K x N view of w)        * dy^T (N x M)
+//   dW     : dW^T (K x N) = x^T (K x M)                 * dy (T of the N x M view)
+#include <cublas_v2.h>
+#include <cuda_bf16.h>
+
+#include "kattn_common.cuh"
+#include "kattn_launch.h"
+#include "sm100.cuh"
+
+namespace kattn {
+
+namespace {
+
+// src [rows][ld] f32 -> hi, lo [rows][cols] bf16 (cols % 4 == 0, ld % 4 == 0).
+__global__ void __launch_bounds__(256) proj_split_bf16(const float* __restrict__ src, long ld, int rows, int cols,
+                                                       uint2* __restrict__ hi, uint2* __restrict__ lo) {
+    pdl_enter();
+    const int c4 = cols / 4;
+    const long n = static_cast<long>(rows) * c4;
+    for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const long r = i / c4;
+        const int c = static_cast<int>(i - r * c4);
+        const float4 v = *reinterpret_cast<const float4*>(src + r * ld + 4 * c);
+        uint2 h, l;
+        sm100::split2(v.x, v.y, h.x, l.x);
+        sm100::split2(v.z, v.w, h.y, l.y);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+// y[m][n] = b[n] (the GEMMs then accumulate onto it).
+__global__ void __launch_bounds__(256) proj_fill_bias(float* __restrict__ y, long ld, int rows, int cols,
+                                                      const float* __restrict__ b) {
+    pdl_enter();
+    const long n = static_cast<long>(rows) * cols;
+    for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const long r = i / cols;
+        const int c = static_cast<int>(i - r * cols);
+        y[r * ld + c] = b[c];
+    }
+}
+
+// part[p][n] = sum of dy[m][n] over rows [p*R, min(M, (p+1)*R)), rows in order.
+__global__ void __launch_bounds__(256) proj_colsum_part(const float* __restrict__ dy, long ld, int M, int N, int R,
+                                                        float* __restrict__ part) {
+    pdl_enter();
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int p = blockIdx.y;
+    if (n >= N) return;
+    const int m0 = p * R;
+    const int m1 = min(M, m0 + R);
+    float s = 0.f;
+    for (int m = m0; m < m1; ++m) s += dy[static_cast<long>(m) * ld + n];
+    part[static_cast<long>(p) * N + n] = s;
+}
+
+// db[n] (+)= sum over p of part[p][n], p in order: deterministic.
+__global__ void __launch_bounds__(256) proj_colsum_final(const float* __restrict__ part, int P, int N,
+                                                         float* __restrict__ db, int accumulate) {
+    pdl_enter();
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    float s = 0.f;
+    for (int p = 0; p < P; ++p) s += part[static_cast<long>(p) * N + n];
+    db[n] = accumulate ? db[n] + s : s;
+}
+
+unsigned grid_for(long items, int num_sms) {
+    long g = (items + 255) / 256;
+    const long cap = static_cast<long>(num_sms > 0 ? num_sms : 148) * 16;
+    if (g > cap) g = cap;
+    return static_cast<unsigned>(g < 1 ? 1 : g);
+}
+
+struct Split {
+    uint2* hi;
+    uint2* lo;
+};
+
+ProjStatus launch_split(const float* src, long ld, int rows, int cols, Split out, int num_sms, cudaStream_t s,
+                        int* launches) {
+    const long n = static_cast<long>(rows) * (cols / 4);
+    if (n == 0) return {};
+    const cudaError_t e = launch_pdl(proj_split_bf16, dim3(grid_for(n, num_sms)), dim3(256), 0, s, src, ld, rows,
+                                     cols, out.hi, out.lo);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "operand split"};
+    ++*launches;
+    return {};
+}
+
+// C (column-major m x n, ldc) = beta0 * C + A*B over the bf16 hi / lo pairs:
+// hi*hi, then + hi*lo, + lo*hi.
+ProjStatus gemm3(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k, Split a, int lda,
+                 Split b, int ldb, float beta0, float* c, long ldc, int* gemms) {
+    const float one = 1.f;
+    const void* A[3] = {a.hi, a.hi, a.lo};
+    const void* B[3] = {b.hi, b.lo, b.hi};
+    for (int i = 0; i < 3; ++i) {
+        const float beta = i == 0 ? beta0 : 1.f;
+        const cublasStatus_t st =
+            cublasGemmEx(h, ta, tb, m, n, k, &one, A[i], CUDA_R_16BF, lda, B[i], CUDA_R_16BF, ldb, &beta, c,
+                         CUDA_R_32F, static_cast<int>(ldc), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+        if (st != CUBLAS_STATUS_SUCCESS) return {cudaSuccess, st, "cublasGemmEx"};
+        ++*gemms;
+    }
+    return {};
+}
+
+// Stream-ordered workspace for the split copies of the operands (bytes of
+// one f32 array each: hi + lo at 2 bytes apiece).
+struct Workspace {
+    char* base = nullptr;
+    cudaStream_t s = nullptr;
+    ~Workspace() {
+        if (base) cudaFreeAsync(base, s);
+    }
+};
+
+Split carve(char*& p, long elems) {
+    Split sp;
+    sp.hi = reinterpret_cast<uint2*>(p);
+    p += ((elems * 2 + 255) / 256) * 256;
+    sp.lo = reinterpret_cast<uint2*>(p);
+    p += ((elems * 2 + 255) / 256) * 256;
+    return sp;
+}
+
+long split_bytes(long elems) { return 2 * ((elems * 2 + 255) / 256) * 256; }
+
+}  // namespace
+
+ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t s, const float* x, long ld_x, const float* w,
+                        const float* b, float* y, long ld_y, int M, int N, int K, int* launches, int* gemms) {
+    if (M == 0 || N == 0) return {};
+    cublasHandle_t h = static_cast<cublasHandle_t>(handle);
+    Workspace ws;
+    ws.s = s;
+    const long ex = static_cast<long>(M) * K, ew = static_cast<long>(N) * K;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), split_bytes(ex) + split_bytes(ew), s);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
+    char* p = ws.base;
+    const Split xs = carve(p, ex), wsp = carve(p, ew);
+    ProjStatus st = launch_split(x, ld_x, M, K, xs, num_sms, s, launches);
+    if (!st.ok()) return st;
+    st = launch_split(w, K, N, K, wsp, num_sms, s, launches);
+    if (!st.ok()) return st;
+    float beta0 = 0.f;
+    if (!b && K == 0) {
+        e = cudaMemset2DAsync(y, ld_y * 4, 0, static_cast<size_t>(N) * 4, M, s);
+        return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, CUBLAS_STATUS_SUCCESS, "cudaMemset2DAsync"};
+    }
+    if (b) {
+        e = launch_pdl(proj_fill_bias, dim3(grid_for(static_cast<long>(M) * N, num_sms)), dim3(256), 0, s, y, ld_y, M,
+                       N, b);
+        if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "bias fill"};
+        ++*launches;
+        beta0 = 1.f;
+    }
+    if (K == 0) return {};
+    return gemm3(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, wsp, K, xs, K, beta0, y, ld_y, gemms);
+}
+
+ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, const float* dy, long ld_dy, const float* w,
+                            float* dx, long ld_dx, int M, int N, int K, int* launches, int* gemms) {
+    if (M == 0 || K == 0) return {};
+    cublasHandle_t h = static_cast<cublasHandle_t>(handle);
+    if (N == 0) {
+        const cudaError_t e = cudaMemset2DAsync(dx, ld_dx * 4, 0, static_cast<size_t>(K) * 4, M, s);
+        return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, CUBLAS_STATUS_SUCCESS, "cudaMemset2DAsync"};
+    }
+    Workspace ws;
+    ws.s = s;
+    const long ed = static_cast<long>(M) * N, ew = static_cast<long>(N) * K;
+    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), split_bytes(ed) + split_bytes(ew), s);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
+    char* p = ws.base;
+    const Split ds = carve(p, ed), wsp = carve(p, ew);
+    ProjStatus st = launch_split(dy, ld_dy, M, N, ds, num_sms, s, launches);
+    if (!st.ok()) return st;
+    st = launch_split(w, K, N, K, wsp, num_sms, s, launches);
+    if (!st.ok()) return st;
+    return gemm3(h, CUBLAS_OP_N, CUBLAS_OP_N, K, M, N, wsp, K, ds, N, 0.f, dx, ld_dx, gemms);
+}
+
+ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, const float* dy, long ld_dy, const float* x,
+                            long ld_x, float* dw, float* db, int M, int N, int K, int accumulate, int* launches,
+                            int* gemms) {
+    if (N == 0) return {};
+    cublasHandle_t h = static_cast<cublasHandle_t>(handle);
+    Workspace ws;
+    ws.s = s;
+    const long ed = static_cast<long>(M) * N, ex = static_cast<long>(M) * K;
+    const int R = 64;  // rows per column-sum partial
+    const int P = M > 0 ? (M + R - 1) / R : 1;
+    const long part_bytes = ((static_cast<long>(P) * N * 4 + 255) / 256) * 256;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base),
+                                    split_bytes(ed) + split_bytes(ex) + (db ? part_bytes : 0), s);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
+    char* p = ws.base;
+    const Split ds = carve(p, ed), xs = carve(p, ex);
+    float* part = reinterpret_cast<float*>(p);
+    if (db) {
+        if (M > 0) {
+            e = launch_pdl(proj_colsum_part, dim3((N + 255) / 256, P), dim3(256), 0, s, dy, ld_dy, M, N, R, part);
+            if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "column sums"};
+            ++*launches;
+        }
+        e = launch_pdl(proj_colsum_final, dim3((N + 255) / 256), dim3(256), 0, s, static_cast<const float*>(part),
+                       M > 0 ? P : 0, N, db, accumulate);
+        if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "column sums"};
+        ++*launches;
+    }
+    if (K == 0) return {};
+    if (M == 0) {
+        if (accumulate) return {};
+        e = cudaMemsetAsync(dw, 0, static_cast<size_t>(N) * K * 4, s);
+        return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, CUBLAS_STATUS_SUCCESS, "cudaMemsetAsync"};
+    }
+    ProjStatus st = launch_split(dy, ld_dy, M, N, ds, num_sms, s, launches);
+    if (!st.ok()) return st;
+    st = launch_split(x, ld_x, M, K, xs, num_sms, s, launches);
+    if (!st.ok()) return st;
+    return gemm3(h, CUBLAS_OP_N, CUBLAS_OP_T, K, N, M, xs, K, ds, N, accumulate ? 1.f : 0.f, dw, K, gemms);
+}
+
+}  // namespace kattn

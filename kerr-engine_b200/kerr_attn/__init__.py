@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "kattn_set_path", "kattn_check_device",
     "kattn_fwd", "kattn_bwd", "kattn_fwd_host", "kattn_bwd_host", "kattn_last_launch_count",
     "kattn_bwd_noalloc",
+    "kattn_linear_fwd", "kattn_linear_bwd_dx", "kattn_linear_bwd_dw",
 )
 
 # Largest B*H*T that kattn_bwd_noalloc accepts (KATTN_NOALLOC_MAX_ROWS).
@@ -98,6 +99,12 @@ def lib():
     L.kattn_fwd_host.restype = _i
     L.kattn_bwd_host.argtypes = bwd_args
     L.kattn_bwd_host.restype = _i
+    L.kattn_linear_fwd.argtypes = [_p, _p, _l, _p, _p, _p, _l, _i, _i, _i, _p]
+    L.kattn_linear_fwd.restype = _i
+    L.kattn_linear_bwd_dx.argtypes = [_p, _p, _l, _p, _p, _l, _i, _i, _i, _p]
+    L.kattn_linear_bwd_dx.restype = _i
+    L.kattn_linear_bwd_dw.argtypes = [_p, _p, _l, _p, _l, _p, _p, _i, _i, _i, _i, _p]
+    L.kattn_linear_bwd_dw.restype = _i
     _lib = L
     return L
 
@@ -288,3 +295,67 @@ def bwd_host(ctx: Context, q, k, v, o, dout, lse, dq, dk, dv, n_head: int, causa
 def split_qkv(qkv, n_embd: int):
     """q, k, v column-block views of a [B, T, 3C] buffer (src/pipeline.rs:296-302)."""
     return qkv[..., :n_embd], qkv[..., n_embd:2 * n_embd], qkv[..., 2 * n_embd:]
+
+
+# ---------------------------------------------------------------- projections
+# c_attn / c_proj as dense layers (include/kerr_attn.h, kattn_linear_*).  Rows
+# are positions: x / y / dy / dx are [..., features] float32 CUDA views whose
+# leading dimensions flatten to M rows with one row stride; w is [out, in]
+# contiguous (the reference's layout), b / db [out] contiguous.
+
+def _mat(t, name):
+    """(pointer, row stride, rows, cols) of a float32 CUDA view whose rows
+    (all leading dimensions) share one stride and have unit inner stride."""
+    import torch
+
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32")
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must have unit inner stride")
+    cols = t.shape[-1]
+    rows = t.numel() // cols if cols else 0
+    if t.dim() == 1:
+        return ctypes.c_void_p(t.data_ptr()), cols, 1, cols
+    ld = t.stride(-2)
+    expect = ld
+    for dim in range(t.dim() - 2, 0, -1):
+        expect *= t.shape[dim]
+        if t.shape[dim - 1] > 1 and t.stride(dim - 1) != expect:
+            raise ValueError(f"{name} rows must be evenly strided over the leading dimensions")
+    return ctypes.c_void_p(t.data_ptr()), ld, rows, cols
+
+
+def linear_fwd(ctx: Context, x, w, b, y, stream=None) -> int:
+    """y = x w^T + b (b may be None).  Returns this library's kernels launched."""
+    px, ldx, M, K = _mat(x, "x")
+    py, ldy, My, N = _mat(y, "y")
+    if My != M or tuple(w.shape) != (N, K):
+        raise ValueError("shapes: x [M, K], w [N, K], y [M, N]")
+    st = lib().kattn_linear_fwd(ctx.handle, px, ldx, _vec(w, "w"), None if b is None else _vec(b, "b"), py, ldy,
+                                M, N, K, _stream_ptr(stream, x.device))
+    _check(st, "kattn_linear_fwd")
+    return last_launch_count()
+
+
+def linear_bwd_dx(ctx: Context, dy, w, dx, stream=None) -> int:
+    """dx = dy w."""
+    pd, ldd, M, N = _mat(dy, "dy")
+    px, ldx, Mx, K = _mat(dx, "dx")
+    if Mx != M or tuple(w.shape) != (N, K):
+        raise ValueError("shapes: dy [M, N], w [N, K], dx [M, K]")
+    st = lib().kattn_linear_bwd_dx(ctx.handle, pd, ldd, _vec(w, "w"), px, ldx, M, N, K,
+                                   _stream_ptr(stream, dy.device))
+    _check(st, "kattn_linear_bwd_dx")
+    return last_launch_count()
+
+
+def linear_bwd_dw(ctx: Context, dy, x, dw, db, accumulate: bool = True, stream=None) -> int:
+    """dw (+)= dy^T x and db (+)= colsum(dy) (db may be None)."""
+    pd, ldd, M, N = _mat(dy, "dy")
+    px, ldx, Mx, K = _mat(x, "x")
+    if Mx != M or tuple(dw.shape) != (N, K):
+        raise ValueError("shapes: dy [M, N], x [M, K], dw [N, K]")
+    st = lib().kattn_linear_bwd_dw(ctx.handle, pd, ldd, px, ldx, _vec(dw, "dw"), None if db is None else _vec(db, "db"),
+                                   M, N, K, int(accumulate), _stream_ptr(stream, dy.device))
+    _check(st, "kattn_linear_bwd_dw")
+    return last_launch_count()

@@ -62,6 +62,19 @@ void kattn_oracle_backward_batch(int B, int T, int C, int H,
 /* Threads the batched drivers use for nthreads <= 0. */
 int kattn_oracle_default_threads(int B);
 
+/* Linear layers of the attention projections (kproj_oracle.c): rows are
+ * positions, weights [N out][K in] row-major.
+ *   forward    : y[m][n] = b[n] + sum_k w[n][k] x[m][k]   (b may be NULL)
+ *   backward_dx: dx[m][k] = sum_n dy[m][n] w[n][k]
+ *   backward_dw: dw[n][k] += sum_m dy[m][n] x[m][k];  db[n] += sum_m dy[m][n]
+ *                (db may be NULL; pass zeroed arrays for fresh gradients) */
+void kproj_oracle_forward(int M, int N, int K, const float* x, long ld_x, const float* w, const float* b,
+                          float* y, long ld_y, int nthreads);
+void kproj_oracle_backward_dx(int M, int N, int K, const float* dy, long ld_dy, const float* w, float* dx,
+                              long ld_dx, int nthreads);
+void kproj_oracle_backward_dw(int M, int N, int K, const float* dy, long ld_dy, const float* x, long ld_x,
+                              float* dw, float* db, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

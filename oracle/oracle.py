@@ -49,6 +49,15 @@ def lib():
         L.kattn_oracle_backward_batch.restype = None
         L.kattn_oracle_default_threads.argtypes = [ctypes.c_int]
         L.kattn_oracle_default_threads.restype = ctypes.c_int
+        L.kproj_oracle_forward.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f, _f,
+                                           _f, ctypes.c_long, ctypes.c_int]
+        L.kproj_oracle_forward.restype = None
+        L.kproj_oracle_backward_dx.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f,
+                                               _f, ctypes.c_long, ctypes.c_int]
+        L.kproj_oracle_backward_dx.restype = None
+        L.kproj_oracle_backward_dw.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f,
+                                               ctypes.c_long, _f, _f, ctypes.c_int]
+        L.kproj_oracle_backward_dw.restype = None
         _lib = L
     return _lib
 
@@ -106,3 +115,44 @@ def backward(d_out, q, k, v, att, n_head: int, threads: int = 0):
     lib().kattn_oracle_backward_batch(B, T, C, n_head, _ptr(d_out), C, _addr(q), _addr(k), _addr(v),
                                       ld, _ptr(att), _ptr(dq), _ptr(dk), _ptr(dv), C, threads)
     return dq, dk, dv
+
+
+# ---------------------------------------------------------------- linear layers
+# The attention projections (c_attn, c_proj): src/backend.rs:240-247, :508-520
+# (forward), src/backward.rs:48-60 (dx), src/backend.rs:320-342 (dw, db).
+# x / dy are [M, in] / [M, out] float32 rows (positions); w is [out, in].
+
+def linear_forward(x, w, b=None, threads=0):
+    """y[m, n] = b[n] + sum_k w[n, k] x[m, k]."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    assert w.shape == (N, K)
+    y = np.empty((M, N), np.float32)
+    bb = None if b is None else np.ascontiguousarray(b, np.float32)
+    lib().kproj_oracle_forward(M, N, K, _ptr(x), K, _ptr(w), _ptr(bb), _ptr(y), N, threads)
+    return y
+
+
+def linear_backward_dx(dy, w, threads=0):
+    """dx[m, k] = sum_n dy[m, n] w[n, k]."""
+    dy = np.ascontiguousarray(dy, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    M, N = dy.shape
+    K = w.shape[1]
+    dx = np.empty((M, K), np.float32)
+    lib().kproj_oracle_backward_dx(M, N, K, _ptr(dy), N, _ptr(w), _ptr(dx), K, threads)
+    return dx
+
+
+def linear_backward_dw(dy, x, threads=0):
+    """(dw, db): dw[n, k] = sum_m dy[m, n] x[m, k], db[n] = sum_m dy[m, n]."""
+    dy = np.ascontiguousarray(dy, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    M, N = dy.shape
+    K = x.shape[1]
+    dw = np.zeros((N, K), np.float32)
+    db = np.zeros(N, np.float32)
+    lib().kproj_oracle_backward_dw(M, N, K, _ptr(dy), N, _ptr(x), K, _ptr(dw), _ptr(db), threads)
+    return dw, db

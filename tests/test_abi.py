@@ -99,6 +99,31 @@ def test_bwd_validation(L):
     assert L.kattn_bwd(*bad, 1, 8, 4, 32, 0.17, 1, None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
 
 
+def test_linear_validation(L):
+    # The projection entry points reject bad arguments before touching a device.
+    ctx = _fake_ctx()
+    P = ctypes.c_void_p
+    x, w, b, y = P(0x10000), P(0x20000), P(0x30000), P(0x40000)
+
+    def fwd(c=ctx, x=x, ldx=128, w=w, b=b, y=y, ldy=384, M=256, N=384, K=128):
+        return L.kattn_linear_fwd(c, x, ldx, w, b, y, ldy, M, N, K, None)
+
+    assert fwd(c=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(M=-1) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(x=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(ldx=64) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT      # ld < K
+    assert fwd(x=P(0x10008)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert fwd(ldy=386) == kerr_attn.KATTN_ERR_MISALIGNED           # stride not a multiple of 4
+    assert fwd(K=126, ldx=128) == kerr_attn.KATTN_ERR_MISALIGNED    # width not a multiple of 4
+    assert fwd(b=P(0x30002)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert fwd(M=0, x=None, y=None) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+    assert L.kattn_linear_bwd_dx(ctx, y, 384, w, P(0x50004), 128, 256, 384, 128, None) == \
+        kerr_attn.KATTN_ERR_MISALIGNED
+    assert L.kattn_linear_bwd_dw(ctx, y, 384, x, 128, None, b, 256, 384, 128, 1, None) == \
+        kerr_attn.KATTN_ERR_INVALID_ARGUMENT                         # dw is NULL
+    assert L.kattn_linear_bwd_dw(ctx, y, 384, x, 128, P(0x60000), b, 256, 0, 128, 1, None) == kerr_attn.KATTN_OK
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device error path")
 def test_create_without_device_fails_cleanly(L):
     with pytest.raises(kerr_attn.KattnError) as e:

@@ -135,3 +135,23 @@ def test_oracle_reproduces_golden(oracle_lib, name):
     assert np.array_equal(lse, z["lse"])
     dq, dk, dv = oracle_lib.backward(z["dout"], q, k, v, att, H)
     assert np.array_equal(dq, z["dq"]) and np.array_equal(dk, z["dk"]) and np.array_equal(dv, z["dv"])
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4, 4), (37, 29, 41), (64, 384, 128)])
+def test_linear_oracle_against_float64(M, N, K):
+    # The projection layers' restatement (oracle/kproj_oracle.c) against float64.
+    from oracle import oracle
+
+    rng = np.random.default_rng(M * 31 + N)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    dy = rng.standard_normal((M, N)).astype(np.float32)
+    x64, w64, dy64 = x.astype(np.float64), w.astype(np.float64), dy.astype(np.float64)
+    y = oracle.linear_forward(x, w, b)
+    assert np.abs(y - (x64 @ w64.T + b)).max() < 1e-5 * max(1.0, np.abs(y).max())
+    dx = oracle.linear_backward_dx(dy, w)
+    assert np.abs(dx - dy64 @ w64).max() < 1e-5 * max(1.0, np.abs(dx).max())
+    dw, db = oracle.linear_backward_dw(dy, x)
+    assert np.abs(dw - dy64.T @ x64).max() < 1e-5 * max(1.0, np.abs(dw).max()) * np.sqrt(M)
+    assert np.abs(db - dy64.sum(0)).max() < 1e-5 * max(1.0, np.abs(db).max()) * np.sqrt(M)
