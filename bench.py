@@ -393,6 +393,165 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+LAYER_METRIC = ("attention layer (c_attn + causal attention + c_proj) fwd+bwd tokens/s per GPU at 768-dim T=256, "
+                "projection gradients all-reduced over the ranks")
+
+
+def layer_cpu_sample(n_seq: int, T: int, H: int, d: int, threads: int, seed: int = 11):
+    """One block of the layer through the oracle (linear layers + attention,
+    forward and backward) over n_seq sequences, every call on `threads`
+    host threads."""
+    import numpy as np
+
+    from oracle import oracle
+
+    C = H * d
+    rng = np.random.default_rng(seed)
+    M = n_seq * T
+    x = rng.standard_normal((M, C)).astype(np.float32)
+    wa = rng.uniform(-1, 1, (3 * C, C)).astype(np.float32) / np.sqrt(C)
+    wp = rng.uniform(-1, 1, (C, C)).astype(np.float32) / np.sqrt(C)
+    ba = np.zeros(3 * C, np.float32)
+    bp = np.zeros(C, np.float32)
+    dy = rng.standard_normal((M, C)).astype(np.float32)
+    t0 = time.perf_counter()
+    qkv = oracle.linear_forward(x, wa, ba, threads=threads).reshape(n_seq, T, 3 * C)
+    q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+    o, att, _ = oracle.forward(q, k, v, H, threads=threads)
+    oracle.linear_forward(o.reshape(M, C), wp, bp, threads=threads)
+    d_o = oracle.linear_backward_dx(dy, wp, threads=threads)
+    oracle.linear_backward_dw(dy, o.reshape(M, C), threads=threads)
+    dq, dk, dv = oracle.backward(d_o.reshape(n_seq, T, C), q, k, v, att, H, threads=threads)
+    dqkv = np.concatenate([dq, dk, dv], axis=-1).reshape(M, 3 * C)
+    oracle.linear_backward_dx(dqkv, wa, threads=threads)
+    oracle.linear_backward_dw(dqkv, x, threads=threads)
+    return time.perf_counter() - t0
+
+
+def run_layer(args):
+    """The whole attention layer of the 768-dim model per block: c_attn,
+    attention, c_proj forward; their backward in reverse block order; each
+    block's projection gradients all-reduced across the ranks (NCCL) as soon as
+    its backward is enqueued, overlapping the blocks below (the data-parallel
+    exchange of the step)."""
+    import torch
+    import torch.distributed as dist
+
+    import kerr_attn
+    from kerr_attn.dist import ProjGradBuckets
+    from kerr_attn.dist import max_over_ranks as _max_over_ranks
+    from kerr_attn.dist import sync as _sync
+    from kerr_attn.dist import world as _world
+
+    rank, local, world = _world()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    W = WORKLOAD
+    B, T, H, d, NB = W["batch_per_gpu"], W["seq_len"], W["n_head"], W["head_dim"], W["blocks"]
+    C = H * d
+    M = B * T
+    ctx = kerr_attn.Context(local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + rank)
+    blocks = []
+    for _ in range(NB):
+        # Linear init U(+-1/sqrt(fan_in)), bias 0 (src/init.rs:54-181).
+        blk = {"x": torch.randn(B, T, C, device=dev, generator=g),
+               "wa": (torch.rand(3 * C, C, device=dev, generator=g) * 2 - 1) / math.sqrt(C),
+               "ba": torch.zeros(3 * C, device=dev),
+               "wp": (torch.rand(C, C, device=dev, generator=g) * 2 - 1) / math.sqrt(C),
+               "bp": torch.zeros(C, device=dev),
+               "qkv": torch.empty(B, T, 3 * C, device=dev), "o": torch.empty(B, T, C, device=dev),
+               "lse": torch.empty(B, H, T, device=dev), "y": torch.empty(B, T, C, device=dev),
+               "dy": torch.randn(B, T, C, device=dev, generator=g), "d_o": torch.empty(B, T, C, device=dev),
+               "dqkv": torch.empty(B, T, 3 * C, device=dev), "dx": torch.empty(B, T, C, device=dev)}
+        blk["q"], blk["k"], blk["v"] = kerr_attn.split_qkv(blk["qkv"], C)
+        blk["dq"], blk["dk"], blk["dv"] = kerr_attn.split_qkv(blk["dqkv"], C)
+        blocks.append(blk)
+    buckets = ProjGradBuckets(NB, C, B, device=dev)
+
+    def step():
+        n = 0
+        for b in blocks:
+            n += kerr_attn.linear_fwd(ctx, b["x"], b["wa"], b["ba"], b["qkv"])
+            n += kerr_attn.fwd(ctx, b["q"], b["k"], b["v"], b["o"], b["lse"], H)
+            n += kerr_attn.linear_fwd(ctx, b["o"], b["wp"], b["bp"], b["y"])
+        for i in reversed(range(NB)):
+            b = blocks[i]
+            aw, ab, pw, pb = buckets.views(i)
+            n += kerr_attn.linear_bwd_dx(ctx, b["dy"], b["wp"], b["d_o"])
+            n += kerr_attn.linear_bwd_dw(ctx, b["dy"], b["o"], pw, pb, accumulate=False)
+            n += kerr_attn.bwd(ctx, b["q"], b["k"], b["v"], b["o"], b["d_o"], b["lse"], b["dq"], b["dk"], b["dv"], H)
+            n += kerr_attn.linear_bwd_dx(ctx, b["dqkv"], b["wa"], b["dx"])
+            n += kerr_attn.linear_bwd_dw(ctx, b["dqkv"], b["x"], aw, ab, accumulate=False)
+            buckets.launch(i)
+        buckets.finish()
+        return n
+
+    for _ in range(args.warmup):
+        step()
+    _sync(dev)
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = mk(), mk()
+    _sync(dev)
+    t0.record()
+    launches = 0
+    for _ in range(args.steps):
+        launches += step()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    _sync(dev)
+    ms_step = _max_over_ranks(t0.elapsed_time(t1), dev) / args.steps
+    tokens = B * T * world
+    work = algorithmic(B, T, H, d)
+    gemm_flops = 24.0 * M * C * C  # c_attn and c_proj: forward, dx and dW (2 flops per MAC)
+    attn_flops = work["fwd_flops"] + work["bwd_flops"]
+    flops_step = NB * (gemm_flops + attn_flops)
+    achieved = flops_step / (ms_step / 1e3) / 1e12
+    peaks, peak_src = measured_peaks()
+    bf16 = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+    ctx.check_device()
+    line = {"metric": LAYER_METRIC, "value": tokens / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded x, dy ~ N(0,1); linear init U(+-1/sqrt(fan_in)), bias 0)",
+            "config": dict(W, workload="kerr-engine 768-dim attention layer fwd+bwd (c_attn, attention, c_proj), "
+                                       "4 blocks per step", global_batch=B * world,
+                           parallelism=f"dp{world}, projection gradients all-reduced per block"),
+            "gpu_launches": launches,
+            "cublas_gemms_per_step": NB * 6,
+            "allreduce": {"buckets_per_step": NB, "floats_per_bucket": buckets.numel,
+                          "bytes_per_step": NB * buckets.numel * 4, "backend": "nccl" if world > 1 else "none"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "unit": "TFLOP/s",
+                         "algorithmic_flops_per_step": flops_step,
+                         "executed_tflops": 3 * achieved, "peak": bf16,
+                         "frac": (3 * achieved / bf16) if bf16 else None,
+                         "peak_source": f"{peak_src} dense bf16 (sustained)",
+                         "note": "every product runs as 3 bf16 MMAs (hi/lo split): executed = 3 x algorithmic"},
+            "clocks": clocks.summary()}
+    if world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        n_seq = min(4, B)
+        layer_cpu_sample(n_seq, T, H, d, cores)
+        t = layer_cpu_sample(n_seq, T, H, d, cores)
+        line["cpu_baseline"] = {"value": n_seq * T / (NB * t), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": f"1 of 4 blocks, {n_seq} of {B} sequences, every oracle call on "
+                                          f"{cores} host threads; scaled to the 4-block step"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -403,11 +562,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", choices=("auto", "ffma", "tensor"), default="auto",
                     help="kernel family (auto: tensor cores where supported)")
+    ap.add_argument("--workload", choices=("attention", "layer"), default="attention",
+                    help="attention: the headline (attention fwd+bwd); layer: c_attn + attention + c_proj with "
+                         "the projection-gradient all-reduce")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "layer":
+        run_layer(args)
     else:
         run_ours(args)
 

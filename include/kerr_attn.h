@@ -161,8 +161,9 @@ int kattn_last_launch_count(void);
  * reference's [out][in] layout (src/model.rs:184-185): w is [N][K]
  * contiguous.  Device pointers, 16-byte aligned; every row stride and K, N
  * a multiple of 4 floats.  Each product is formed in bf16 hi/lo pairs
- * (hi*hi + hi*lo + lo*hi, f32 accumulation; ~1e-5 relative) by three cuBLAS
- * GEMMs over operands this library splits.  Workspace comes from the
+ * (hi*hi + hi*lo + lo*hi, f32 accumulation; ~1e-5 relative) by one cuBLAS
+ * GEMM over a threefold contraction of operands this library splits and
+ * concatenates.  Workspace comes from the
  * device's stream-ordered pool; nothing synchronises the host. */
 
 /* y[m][n] = b[n] + sum_k w[n][k] x[m][k];  b may be NULL (no bias). */

@@ -7,10 +7,14 @@
 //
 // Numerics: each f32 operand is split by the kernels below into bf16 hi and
 // lo = bf16(x - hi) (the same split as the attention kernels), and every
-// product is formed as hi*hi + hi*lo + lo*hi by three cuBLAS bf16 GEMMs with
-// f32 accumulation into the same output: relative error ~1e-5, where a single
-// bf16 or tf32 GEMM would give ~1e-3.  These are plain GEMMs, so the library
-// runs them; the split, bias and column-sum kernels are this library's.
+// product is formed as hi*hi + hi*lo + lo*hi with f32 accumulation: relative
+// error ~1e-5, where a single bf16 or tf32 GEMM would give ~1e-3.  The three
+// products run as ONE cuBLAS bf16 GEMM over a contraction three times as long:
+// the split writes each operand three times along its contraction dimension,
+// e.g. x' = [x_hi | x_hi | x_lo] against w' = [w_hi | w_lo | w_hi], so the f32
+// output is written once instead of read and rewritten by three GEMMs.  These
+// are plain GEMMs, so the library runs them; the split, bias and column-sum
+// kernels are this library's.
 //
 // Row-major f32 [rows][ld] arrays map onto cuBLAS's column-major view as
 // their transposes:
@@ -28,9 +32,12 @@ namespace kattn {
 
 namespace {
 
-// src [rows][ld] f32 -> hi, lo [rows][cols] bf16 (cols % 4 == 0, ld % 4 == 0).
-__global__ void __launch_bounds__(256) proj_split_bf16(const float* __restrict__ src, long ld, int rows, int cols,
-                                                       uint2* __restrict__ hi, uint2* __restrict__ lo) {
+// src [rows][ld] f32 -> three bf16 copies of it (each either hi or lo:
+// segment g is lo when bit g of `lo_mask` is set), concatenated along the
+// columns (dst [rows][3*cols]) or along the rows (dst [3*rows][cols]).
+// cols % 4 == 0, ld % 4 == 0.
+__global__ void __launch_bounds__(256) proj_split3(const float* __restrict__ src, long ld, int rows, int cols,
+                                                   uint2* __restrict__ dst, int along_rows, int lo_mask) {
     pdl_enter();
     const int c4 = cols / 4;
     const long n = static_cast<long>(rows) * c4;
@@ -42,8 +49,11 @@ __global__ void __launch_bounds__(256) proj_split_bf16(const float* __restrict__
         uint2 h, l;
         sm100::split2(v.x, v.y, h.x, l.x);
         sm100::split2(v.z, v.w, h.y, l.y);
-        hi[i] = h;
-        lo[i] = l;
+#pragma unroll
+        for (int g = 0; g < 3; ++g) {
+            const long o = along_rows ? (static_cast<long>(g) * rows + r) * c4 + c : r * 3 * c4 + g * c4 + c;
+            dst[o] = (lo_mask >> g) & 1 ? l : h;
+        }
     }
 }
 
@@ -92,42 +102,37 @@ unsigned grid_for(long items, int num_sms) {
     return static_cast<unsigned>(g < 1 ? 1 : g);
 }
 
-struct Split {
-    uint2* hi;
-    uint2* lo;
+// One operand as three bf16 copies along its contraction (see proj_split3).
+struct Cat3 {
+    uint2* p;
+    int along_rows;
+    int lo_mask;
 };
 
-ProjStatus launch_split(const float* src, long ld, int rows, int cols, Split out, int num_sms, cudaStream_t s,
-                        int* launches) {
+ProjStatus launch_split3(const float* src, long ld, int rows, int cols, Cat3 out, int num_sms, cudaStream_t s,
+                         int* launches) {
     const long n = static_cast<long>(rows) * (cols / 4);
     if (n == 0) return {};
-    const cudaError_t e = launch_pdl(proj_split_bf16, dim3(grid_for(n, num_sms)), dim3(256), 0, s, src, ld, rows,
-                                     cols, out.hi, out.lo);
+    const cudaError_t e = launch_pdl(proj_split3, dim3(grid_for(n, num_sms)), dim3(256), 0, s, src, ld, rows, cols,
+                                     out.p, out.along_rows, out.lo_mask);
     if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "operand split"};
     ++*launches;
     return {};
 }
 
-// C (column-major m x n, ldc) = beta0 * C + A*B over the bf16 hi / lo pairs:
-// hi*hi, then + hi*lo, + lo*hi.
-ProjStatus gemm3(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k, Split a, int lda,
-                 Split b, int ldb, float beta0, float* c, long ldc, int* gemms) {
+// C (column-major m x n, ldc) = beta * C + A * B, bf16 operands, f32 accumulation.
+ProjStatus gemm(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k, const void* a,
+                int lda, const void* b, int ldb, float beta, float* c, long ldc, int* gemms) {
     const float one = 1.f;
-    const void* A[3] = {a.hi, a.hi, a.lo};
-    const void* B[3] = {b.hi, b.lo, b.hi};
-    for (int i = 0; i < 3; ++i) {
-        const float beta = i == 0 ? beta0 : 1.f;
-        const cublasStatus_t st =
-            cublasGemmEx(h, ta, tb, m, n, k, &one, A[i], CUDA_R_16BF, lda, B[i], CUDA_R_16BF, ldb, &beta, c,
-                         CUDA_R_32F, static_cast<int>(ldc), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-        if (st != CUBLAS_STATUS_SUCCESS) return {cudaSuccess, st, "cublasGemmEx"};
-        ++*gemms;
-    }
+    const cublasStatus_t st = cublasGemmEx(h, ta, tb, m, n, k, &one, a, CUDA_R_16BF, lda, b, CUDA_R_16BF, ldb, &beta,
+                                           c, CUDA_R_32F, static_cast<int>(ldc), CUBLAS_COMPUTE_32F,
+                                           CUBLAS_GEMM_DEFAULT);
+    if (st != CUBLAS_STATUS_SUCCESS) return {cudaSuccess, st, "cublasGemmEx"};
+    ++*gemms;
     return {};
 }
 
-// Stream-ordered workspace for the split copies of the operands (bytes of
-// one f32 array each: hi + lo at 2 bytes apiece).
+// Stream-ordered workspace for the split copies of the operands.
 struct Workspace {
     char* base = nullptr;
     cudaStream_t s = nullptr;
@@ -136,16 +141,19 @@ struct Workspace {
     }
 };
 
-Split carve(char*& p, long elems) {
-    Split sp;
-    sp.hi = reinterpret_cast<uint2*>(p);
-    p += ((elems * 2 + 255) / 256) * 256;
-    sp.lo = reinterpret_cast<uint2*>(p);
-    p += ((elems * 2 + 255) / 256) * 256;
-    return sp;
+// Bytes of a three-copy bf16 operand of `elems` f32 elements, rounded to 256.
+long cat3_bytes(long elems) { return ((elems * 6 + 255) / 256) * 256; }
+
+Cat3 carve(char*& p, long elems, int along_rows, int lo_mask) {
+    Cat3 c{reinterpret_cast<uint2*>(p), along_rows, lo_mask};
+    p += cat3_bytes(elems);
+    return c;
 }
 
-long split_bytes(long elems) { return 2 * ((elems * 2 + 255) / 256) * 256; }
+// Segment patterns (bit g set: lo in segment g) so that the three products
+// are hi*hi + lo*hi + hi*lo.
+constexpr int PAT_HHL = 0b100;  // hi, hi, lo
+constexpr int PAT_HLH = 0b010;  // hi, lo, hi
 
 }  // namespace
 
@@ -153,31 +161,33 @@ ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t s, const float* 
                         const float* b, float* y, long ld_y, int M, int N, int K, int* launches, int* gemms) {
     if (M == 0 || N == 0) return {};
     cublasHandle_t h = static_cast<cublasHandle_t>(handle);
-    Workspace ws;
-    ws.s = s;
-    const long ex = static_cast<long>(M) * K, ew = static_cast<long>(N) * K;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), split_bytes(ex) + split_bytes(ew), s);
-    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
-    char* p = ws.base;
-    const Split xs = carve(p, ex), wsp = carve(p, ew);
-    ProjStatus st = launch_split(x, ld_x, M, K, xs, num_sms, s, launches);
-    if (!st.ok()) return st;
-    st = launch_split(w, K, N, K, wsp, num_sms, s, launches);
-    if (!st.ok()) return st;
-    float beta0 = 0.f;
-    if (!b && K == 0) {
+    cudaError_t e;
+    if (K == 0 && !b) {
         e = cudaMemset2DAsync(y, ld_y * 4, 0, static_cast<size_t>(N) * 4, M, s);
         return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, CUBLAS_STATUS_SUCCESS, "cudaMemset2DAsync"};
     }
+    float beta = 0.f;
     if (b) {
         e = launch_pdl(proj_fill_bias, dim3(grid_for(static_cast<long>(M) * N, num_sms)), dim3(256), 0, s, y, ld_y, M,
                        N, b);
         if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "bias fill"};
         ++*launches;
-        beta0 = 1.f;
+        beta = 1.f;
     }
     if (K == 0) return {};
-    return gemm3(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, wsp, K, xs, K, beta0, y, ld_y, gemms);
+    Workspace ws;
+    ws.s = s;
+    const long ex = static_cast<long>(M) * K, ew = static_cast<long>(N) * K;
+    e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), cat3_bytes(ex) + cat3_bytes(ew), s);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
+    char* p = ws.base;
+    // x' [M][3K] = [x_hi | x_hi | x_lo], w' [N][3K] = [w_hi | w_lo | w_hi].
+    const Cat3 xc = carve(p, ex, 0, PAT_HHL), wc = carve(p, ew, 0, PAT_HLH);
+    ProjStatus st = launch_split3(x, ld_x, M, K, xc, num_sms, s, launches);
+    if (!st.ok()) return st;
+    st = launch_split3(w, K, N, K, wc, num_sms, s, launches);
+    if (!st.ok()) return st;
+    return gemm(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, 3 * K, wc.p, 3 * K, xc.p, 3 * K, beta, y, ld_y, gemms);
 }
 
 ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, const float* dy, long ld_dy, const float* w,
@@ -191,15 +201,16 @@ ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, const flo
     Workspace ws;
     ws.s = s;
     const long ed = static_cast<long>(M) * N, ew = static_cast<long>(N) * K;
-    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), split_bytes(ed) + split_bytes(ew), s);
+    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), cat3_bytes(ed) + cat3_bytes(ew), s);
     if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
     char* p = ws.base;
-    const Split ds = carve(p, ed), wsp = carve(p, ew);
-    ProjStatus st = launch_split(dy, ld_dy, M, N, ds, num_sms, s, launches);
+    // dy' [M][3N] = [dy_hi | dy_hi | dy_lo], w' [3N][K] = [w_hi; w_lo; w_hi].
+    const Cat3 dc = carve(p, ed, 0, PAT_HHL), wc = carve(p, ew, 1, PAT_HLH);
+    ProjStatus st = launch_split3(dy, ld_dy, M, N, dc, num_sms, s, launches);
     if (!st.ok()) return st;
-    st = launch_split(w, K, N, K, wsp, num_sms, s, launches);
+    st = launch_split3(w, K, N, K, wc, num_sms, s, launches);
     if (!st.ok()) return st;
-    return gemm3(h, CUBLAS_OP_N, CUBLAS_OP_N, K, M, N, wsp, K, ds, N, 0.f, dx, ld_dx, gemms);
+    return gemm(h, CUBLAS_OP_N, CUBLAS_OP_N, K, M, 3 * N, wc.p, K, dc.p, 3 * N, 0.f, dx, ld_dx, gemms);
 }
 
 ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, const float* dy, long ld_dy, const float* x,
@@ -214,10 +225,11 @@ ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, const flo
     const int P = M > 0 ? (M + R - 1) / R : 1;
     const long part_bytes = ((static_cast<long>(P) * N * 4 + 255) / 256) * 256;
     cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base),
-                                    split_bytes(ed) + split_bytes(ex) + (db ? part_bytes : 0), s);
+                                    cat3_bytes(ed) + cat3_bytes(ex) + (db ? part_bytes : 0), s);
     if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
     char* p = ws.base;
-    const Split ds = carve(p, ed), xs = carve(p, ex);
+    // x' [3M][K] = [x_hi; x_hi; x_lo], dy' [3M][N] = [dy_hi; dy_lo; dy_hi].
+    const Cat3 xc = carve(p, ex, 1, PAT_HHL), dc = carve(p, ed, 1, PAT_HLH);
     float* part = reinterpret_cast<float*>(p);
     if (db) {
         if (M > 0) {
@@ -236,11 +248,11 @@ ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, const flo
         e = cudaMemsetAsync(dw, 0, static_cast<size_t>(N) * K * 4, s);
         return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, CUBLAS_STATUS_SUCCESS, "cudaMemsetAsync"};
     }
-    ProjStatus st = launch_split(dy, ld_dy, M, N, ds, num_sms, s, launches);
+    ProjStatus st = launch_split3(dy, ld_dy, M, N, dc, num_sms, s, launches);
     if (!st.ok()) return st;
-    st = launch_split(x, ld_x, M, K, xs, num_sms, s, launches);
+    st = launch_split3(x, ld_x, M, K, xc, num_sms, s, launches);
     if (!st.ok()) return st;
-    return gemm3(h, CUBLAS_OP_N, CUBLAS_OP_T, K, N, M, xs, K, ds, N, accumulate ? 1.f : 0.f, dw, K, gemms);
+    return gemm(h, CUBLAS_OP_N, CUBLAS_OP_T, K, N, 3 * M, xc.p, K, dc.p, N, accumulate ? 1.f : 0.f, dw, K, gemms);
 }
 
 }  // namespace kattn

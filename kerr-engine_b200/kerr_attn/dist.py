@@ -56,3 +56,58 @@ def sync(device=None) -> None:
         dist.barrier()
     if cuda:
         torch.cuda.synchronize(device)
+
+
+class ProjGradBuckets:
+    """Gradients of the attention projections, one flat bucket per block, all-
+    reduced (sum) across the data-parallel ranks.
+
+    Bucket i holds block i's c_attn weight [3C][C] and bias [3C], then c_proj's
+    weight [C][C] and bias [C] (4C^2 + 4C floats, the reference's
+    attn_c_attn_w / _b, attn_c_proj_w / _b).  ``launch(i)`` starts block i's
+    all-reduce as soon as its backward has been enqueued, so it overlaps the
+    backward of the blocks below it; ``finish()`` waits for every bucket and
+    divides by world * batch_per_rank: the reference sums per-sequence
+    gradients over the batch and divides by batch_size (src/train.rs:257-269),
+    and over ranks the batch is world * batch_per_rank sequences.
+    """
+
+    def __init__(self, n_blocks: int, n_embd: int, batch_per_rank: int, device=None):
+        import torch
+
+        self.C = n_embd
+        self.n_blocks = n_blocks
+        self.batch_per_rank = batch_per_rank
+        self.numel = 4 * n_embd * n_embd + 4 * n_embd
+        self.flat = torch.zeros(n_blocks, self.numel, device=device)
+        self._work = []
+
+    def views(self, i: int):
+        """(c_attn_w [3C, C], c_attn_b [3C], c_proj_w [C, C], c_proj_b [C]) of block i."""
+        C = self.C
+        f = self.flat[i]
+        a = 3 * C * C
+        return (f[:a].view(3 * C, C), f[a:a + 3 * C], f[a + 3 * C:a + 3 * C + C * C].view(C, C),
+                f[a + 3 * C + C * C:])
+
+    def zero_(self):
+        self.flat.zero_()
+
+    def launch(self, i: int):
+        """Start block i's all-reduce (no-op without a process group of >1 ranks)."""
+        import torch.distributed as dist
+
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            self._work.append(dist.all_reduce(self.flat[i], op=dist.ReduceOp.SUM, async_op=True))
+
+    def finish(self) -> int:
+        """Wait for every launched all-reduce, then scale to the batch mean.
+        Returns the world size the gradients were reduced over."""
+        import torch.distributed as dist
+
+        for w in self._work:
+            w.wait()
+        self._work.clear()
+        world = dist.get_world_size() if (dist.is_available() and dist.is_initialized()) else 1
+        self.flat.mul_(1.0 / (world * self.batch_per_rank))
+        return world

@@ -7,7 +7,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from kerr_attn.dist import max_over_ranks, shard_batch, sync
+from kerr_attn.dist import ProjGradBuckets, max_over_ranks, shard_batch, sync
 
 
 @pytest.mark.parametrize("batch,world", [(16, 1), (16, 2), (8, 8), (10, 4), (3, 4), (0, 2)])
@@ -61,3 +61,52 @@ def test_max_over_ranks_and_shards_with_gloo():
 
 def test_max_over_ranks_without_group_is_identity():
     assert max_over_ranks(3.25) == 3.25
+
+
+def _bucket_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        C, blocks, batch = 8, 3, 4
+        g = ProjGradBuckets(blocks, C, batch)
+        for i in reversed(range(blocks)):  # the backward walks the blocks top-down
+            aw, ab, pw, pb = g.views(i)
+            aw.fill_(rank + 1.0 + i)
+            ab.fill_(10.0 * (rank + 1))
+            pw.fill_(-1.0 * (rank + 1))
+            pb.fill_(float(i))
+            g.launch(i)
+        out[rank] = (g.finish(), g.flat.clone())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_projection_gradient_allreduce_with_gloo():
+    # Each block's bucket is summed over the ranks and scaled by
+    # 1 / (world * batch): the batch mean over every rank's sequences.
+    world, C, blocks, batch = 2, 8, 3, 4
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_bucket_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn",
+                       join=True)
+    scale = 1.0 / (world * batch)
+    ref = ProjGradBuckets(blocks, C, batch)
+    for i in range(blocks):
+        aw, ab, pw, pb = ref.views(i)
+        aw.fill_(sum(r + 1.0 + i for r in range(world)) * scale)
+        ab.fill_(sum(10.0 * (r + 1) for r in range(world)) * scale)
+        pw.fill_(sum(-1.0 * (r + 1) for r in range(world)) * scale)
+        pb.fill_(world * float(i) * scale)
+    for rank in range(world):
+        w, flat = out[rank]
+        assert w == world
+        assert torch.allclose(flat, ref.flat)
+    assert ref.numel == 4 * C * C + 4 * C
+
+
+def test_projection_buckets_single_process():
+    g = ProjGradBuckets(2, 4, 8)
+    g.views(1)[0].fill_(8.0)
+    g.launch(1)
+    assert g.finish() == 1
+    assert float(g.views(1)[0].max()) == 1.0 and float(g.views(0)[0].abs().max()) == 0.0
