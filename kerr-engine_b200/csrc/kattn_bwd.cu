@@ -45,37 +45,55 @@ struct BwdParams {
 };
 
 // D[b,h,t] = dout[b,t,h,:] . o[b,t,h,:];  dq[b,t,h,:] = 0.
-// D/4 lanes per (b, t, h) row, one float4 each.
+// D/4 lanes per (b, t, h) row, one float4 each; a warp takes RPW*U
+// consecutive rows (consecutive heads of a token are contiguous in memory)
+// and issues all U rounds of loads before it reduces any, so each thread has
+// 2*U float4 loads in flight.  The grid covers every row in one wave.
+constexpr int ROWDOT_U = 4;
+
 template <int D>
 __global__ void __launch_bounds__(256) attn_bwd_rowdot(const BwdParams p) {
     pdl_enter();
     constexpr int LPR = D / 4;
     constexpr int RPW = 32 / LPR;
+    constexpr int U = ROWDOT_U;
     const long nrows = static_cast<long>(p.B) * p.T * p.H;
     const int lane = threadIdx.x & 31;
     const int sub = lane / LPR;
     const int c = (lane % LPR) * 4;
     const long warp = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long nwarps = (static_cast<long>(gridDim.x) * blockDim.x) >> 5;
-    for (long base = warp * RPW; base < nrows; base += nwarps * RPW) {
-        const long row = base + sub;
-        float acc = 0.f;
-        long bt = 0;
-        int h = 0;
-        if (row < nrows) {
-            bt = row / p.H;
-            h = static_cast<int>(row % p.H);
-            const float4 g = *reinterpret_cast<const float4*>(p.dout + bt * p.ld_o + h * D + c);
-            const float4 o = *reinterpret_cast<const float4*>(p.o + bt * p.ld_o + h * D + c);
-            acc = g.x * o.x + g.y * o.y + g.z * o.z + g.w * o.w;
-            *reinterpret_cast<float4*>(p.dq + bt * p.ld_d + h * D + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long base = warp * RPW * U; base < nrows; base += nwarps * RPW * U) {
+        float4 g[U], o[U];
+        long bt[U];
+        int h[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const long row = base + u * RPW + sub;
+            bt[u] = row / p.H;
+            h[u] = static_cast<int>(row - bt[u] * p.H);
+            if (row < nrows) {
+                g[u] = *reinterpret_cast<const float4*>(p.dout + bt[u] * p.ld_o + h[u] * D + c);
+                o[u] = *reinterpret_cast<const float4*>(p.o + bt[u] * p.ld_o + h[u] * D + c);
+            } else {
+                g[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                o[u] = g[u];
+            }
         }
 #pragma unroll
-        for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        if (row < nrows && (lane % LPR) == 0) {
-            const long b = bt / p.T;
-            const long t = bt % p.T;
-            p.dsum[(b * p.H + h) * p.T + t] = acc;
+        for (int u = 0; u < U; ++u) {
+            const long row = base + u * RPW + sub;
+            float acc = g[u].x * o[u].x + g[u].y * o[u].y + g[u].z * o[u].z + g[u].w * o[u].w;
+#pragma unroll
+            for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            if (row < nrows) {
+                *reinterpret_cast<float4*>(p.dq + bt[u] * p.ld_d + h[u] * D + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                if ((lane % LPR) == 0) {
+                    const long b = bt[u] / p.T;
+                    const long t = bt[u] - b * p.T;
+                    p.dsum[(b * p.H + h[u]) * p.T + t] = acc;
+                }
+            }
         }
     }
 }
@@ -336,13 +354,14 @@ static BwdParams make_params(const BwdArgs& a) {
 }
 
 template <int D>
-static cudaError_t launch_prep_d(const BwdParams& p, int /*num_sms*/, cudaStream_t stream, int* launches) {
-    // One row per (warp, lane group): every load is issued at once rather
-    // than in grid-stride rounds (the kernel is bound by memory latency).
+static cudaError_t launch_prep_d(const BwdParams& p, int num_sms, cudaStream_t stream, int* launches) {
+    // One wave when it fits (8 blocks of 256 threads per SM), every load
+    // issued at once; larger problems take grid-stride rounds.
     const long nrows = static_cast<long>(p.B) * p.T * p.H;
-    const long rows_per_block = (256 / 32) * (32 / (D / 4));
+    const long rows_per_block = (256 / 32) * (32 / (D / 4)) * ROWDOT_U;
     long blocks = (nrows + rows_per_block - 1) / rows_per_block;
-    if (blocks > 0x7fffffffL) blocks = 0x7fffffffL;
+    const long cap = 8L * (num_sms > 0 ? num_sms : 148);
+    if (blocks > cap) blocks = cap;
     cudaError_t e = launch_pdl(attn_bwd_rowdot<D>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;

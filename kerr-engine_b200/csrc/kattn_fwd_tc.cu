@@ -7,19 +7,40 @@
 // forward tolerance; a single bf16 or tf32 product is not).
 //
 // Work item = 128 query rows of one (batch, head) slab.  The kernel is
-// persistent: two CTAs of 128 threads per SM, CTA c taking items c, 2G-1-c,
-// 2G+c, ... of the list ordered longest first (a snake order: at the 768-dim
-// shape 192 CTAs run one long item, 88 run two short ones).  Thread t owns
-// query row t (TMEM lane t).  Per 64-row key tile j:
-//   S_j = Q K_j^T        tcgen05.mma SS, M=128 N=64, 3 x 4 k-steps -> TMEM buffer g&1
-//   softmax (online, log2 domain) in registers; P_j hi/lo written over S_j
-//   O_j = P_j V_j        tcgen05.mma TS (P from TMEM), V MN-major  -> TMEM buffer g&1
-//   O <- O * alpha + O_j in registers, one tile later
-// PV_j and S_{j+1} are issued together; while they run the threads fold in
-// O_{j-1} and stage K_{j+2} and V_{j+1} (K and V tiles have separate
-// lifetimes: K_j is free once S_j is done, V_j once PV_j is).  g counts the
-// CTA's tiles across its items (buffers, stages and barrier phases).  ~99 KB
-// of shared memory and 256 TMEM columns per CTA: two CTAs share an SM.
+// persistent: two CTAs per SM, CTA c taking items c, 2G-1-c, 2G+c, ... of the
+// list ordered longest first (a snake order: at the 768-dim shape 192 CTAs
+// run one long item, 88 run two short ones).  g numbers the CTA's 64-row key
+// tiles across its items; tile g uses K stage g&1, V stage g&1 and TMEM
+// buffers g&1.
+//
+// Warp roles (320 threads):
+//   warps 0-7  two threads per query row: warp w handles TMEM lanes
+//              32*(w%4).. (rows) and key columns 32*(w/4).. of each tile.
+//              They convert the landed tiles and run the online softmax
+//              (log2 domain), exchanging half-row maxima through shared
+//              memory.
+//   warp 8     one lane issues every tcgen05.mma as soon as its operands are
+//              ready, so that no softmax thread blocks on the MMA queue.
+//   warp 9     one lane issues every TMA copy as soon as its buffer is free
+//              (a copy instruction can wait for the SM's copy engine).
+// Loads are TMA copies of raw f32 tiles (3-D tensor maps over [B][T][columns],
+// so rows past T read zeros) straight into the operand buffers, ahead of use:
+// K_{g+2} once S_g is done, V_{g+2} once PV_g is done, an item's Q once the
+// previous item's Q is in TMEM.  The softmax threads convert each landed K / V
+// tile in place into bf16 hi / lo halves in the 128B-swizzled UMMA layout, and
+// an item's Q into TMEM (hi / lo), where it is the A operand of S.
+// Per key tile g the softmax threads
+//   convert K_{g+1}                  -> S_{g+1} = Q K_{g+1}^T (TS, 12 MMAs)
+//   softmax of S_g, P_g hi/lo over S_g
+//   convert V_g                      -> O += P_g V_g (TS, P from TMEM, 12 MMAs)
+// so S_{g+1} runs during the softmax of S_g.  O accumulates in TMEM; the
+// running row maximum is raised lazily (only when a tile exceeds it by more
+// than 2^8), and only then is O rescaled.  O is staged through the item's last
+// V stage (64 rows at a time) for coalesced stores.  ~99 KB of shared memory
+// and 256 TMEM columns per CTA: two CTAs share an SM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <atomic>
 
 #include "kattn_common.cuh"
@@ -32,35 +53,56 @@ using namespace sm100;
 
 namespace {
 
-constexpr int BM = 128;  // query rows per CTA
+constexpr int BM = 128;  // query rows per item
 constexpr int BN = 64;   // key rows per tile
-constexpr int NT = 128;
+constexpr int NSM = 256;  // softmax / convert threads (warps 0-7), two per query row
+constexpr int MMA_WARP = NSM / 32;
+constexpr int TMA_WARP = MMA_WARP + 1;
+constexpr int NTHREADS = NSM + 64;
+constexpr unsigned IDLE_NS = 64;  // back-off of an idle issuer loop
 constexpr int D = 64;
 
 // TMEM columns.  Buffer b: S at col_s(b) (64 f32 columns; P packed over it:
 // for key columns 32c..32c+31, bf16 hi in columns 32c..32c+15 and lo in
-// 32c+16..32c+31), the P V tile at col_o(b) (64 f32 columns).
+// 32c+16..32c+31); the O accumulator of the current item at COL_O.
 __device__ __forceinline__ uint32_t col_s(int b) { return b ? 64u : 0u; }
-__device__ __forceinline__ uint32_t col_o(int b) { return b ? 192u : 128u; }
+constexpr uint32_t COL_O = 128;
+// Q of the current item as the A operand of S = Q K^T: d pair (2i, 2i+1) of a
+// row packed in column i, hi at Q_HI, lo at Q_LO (32 columns each).
+constexpr uint32_t Q_HI = 192;
+constexpr uint32_t Q_LO = 224;
+// mu may trail the true row maximum by up to this much (log2 units).
+constexpr float RESCALE_LOG2 = 8.f;
 constexpr uint32_t TMEM_COLS = 256;
 
+// A K / V buffer holds a raw f32 tile (rows x 256 bytes) as TMA lands it,
+// then the converted bf16 hi half (rows x 128 bytes) followed by the lo half.
+// The Q buffer holds the raw tile only, as two 128B-swizzled boxes of 32
+// columns (each thread then reads its own row without bank conflicts).
+constexpr uint32_t Q_BYTES = BM * 256;
+constexpr uint32_t Q_BOX_BYTES = BM * 128;
+constexpr uint32_t KV_BYTES = BN * 256;
+
 struct alignas(1024) Smem {
-    uint8_t qh[BM * 128];  // [128 rows][64 bf16], 128B swizzle
-    uint8_t ql[BM * 128];
-    uint8_t kh[2][BN * 128];
-    uint8_t kl[2][BN * 128];
-    uint8_t vh[2][BN * 128];
-    uint8_t vl[2][BN * 128];
-    uint64_t bar_s[2];
-    uint64_t bar_o[2];
+    uint8_t q[Q_BYTES];
+    uint8_t k[2][KV_BYTES];
+    uint8_t v[2][KV_BYTES];
+    uint64_t q_full;       // raw Q of the CTA's item r landed (phase r&1)
+    uint64_t q_ready;      // Q of item r in TMEM; its shared-memory buffer is free (phase r&1)
+    uint64_t k_full[2];    // raw K tile g landed in stage g&1 (phase (g>>1)&1)
+    uint64_t k_ready[2];   // K tile g converted
+    uint64_t v_full[2];    // raw V tile g landed in stage g&1
+    uint64_t pv_ready[2];  // P_g written to TMEM and V_g converted
+    uint64_t bar_s[2];     // S_g done (TMEM buffer g&1, phase (g>>1)&1)
+    uint64_t bar_o[2];     // PV_g done
+    uint64_t stg_free;     // item r's O staging read out of its last V stage (phase r&1)
+    uint64_t drain;        // MMAs drained after a failure
+    float red[2][2][BM];   // row max (per tile, buffer g&1) / row sum of each half-row
     uint32_t tmem_slot;
 };
 
-struct Params {
-    const float* q;
-    const float* k;
-    const float* v;
-    long ld_qkv;
+struct alignas(64) Params {
+    CUtensorMap tq, tk, tv;  // {H*64 columns, T rows, B} f32; boxes {32, BM, 1} (128B swizzle) for q, {64, BN, 1} for k, v
     float* o;
     long ld_o;
     float* lse;
@@ -73,59 +115,111 @@ struct Params {
     int n_work;  // items: n_qtiles * B * H
 };
 
+// Item round r of CTA c: item w = r*G + (r odd ? G-1-c : c) of the list
+// ordered longest first, its slab (b, h), first query row q0 and key-tile
+// count n_kv.
+struct Seq {
+    int r, j, w, b, h, q0, n_kv;
+    __device__ __forceinline__ void set_item(const Params& p, int c, int G) {
+        j = 0;
+        w = r * G + ((r & 1) ? G - 1 - c : c);
+        if (w >= p.n_work) {
+            w = -1;
+            return;
+        }
+        const int nslab = p.B * p.H;
+        const int slab = w % nslab;
+        b = slab / p.H;
+        h = slab - b * p.H;
+        q0 = (p.n_qtiles - 1 - w / nslab) * BM;
+        n_kv = p.causal ? min(p.n_ktiles, (q0 + BM + BN - 1) / BN) : p.n_ktiles;
+    }
+    __device__ __forceinline__ bool valid() const { return w >= 0; }
+};
+
+// Thread 0's next tile to load (item round r, key tile j; w < 0: none
+// left), with only what the walk needs kept in registers.
+struct Ahead {
+    int r, j, w, n_kv;
+    __device__ __forceinline__ void set(const Params& p, int c, int G) {
+        j = 0;
+        w = r * G + ((r & 1) ? G - 1 - c : c);
+        if (w >= p.n_work) {
+            w = -1;
+            return;
+        }
+        const int q0 = (p.n_qtiles - 1 - w / (p.B * p.H)) * BM;
+        n_kv = p.causal ? min(p.n_ktiles, (q0 + BM + BN - 1) / BN) : p.n_ktiles;
+    }
+    __device__ __forceinline__ void next(const Params& p, int c, int G) {
+        if (++j == n_kv) {
+            ++r;
+            set(p, c, G);
+        }
+    }
+    __device__ __forceinline__ bool valid() const { return w >= 0; }
+    __device__ __forceinline__ int slab(const Params& p) const { return w % (p.B * p.H); }
+};
+
 // Shared-memory descriptors of the Q tile and of K / V stage 0 (stage 1 is
-// STAGE_BYTES further), built once by the issuing thread.
-constexpr uint32_t STAGE_BYTES = BN * 128;
+// KV_BYTES further), rebuilt by the issuing thread at each issue (a few
+// integer operations) rather than held in registers by every thread.
 struct Descs {
-    uint64_t qh, ql, kh, kl, vh, vl;
+    uint64_t kh, kl, vh, vl;
 };
 
 __device__ __forceinline__ Descs make_descs(const Smem& sm) {
     Descs d;
-    d.qh = smem_desc(smem_u32(sm.qh), 16, 1024);
-    d.ql = smem_desc(smem_u32(sm.ql), 16, 1024);
-    d.kh = smem_desc(smem_u32(sm.kh[0]), 16, 1024);
-    d.kl = smem_desc(smem_u32(sm.kl[0]), 16, 1024);
-    d.vh = smem_desc(smem_u32(sm.vh[0]), BN * 128, 1024);  // MN-major (P V B operand)
-    d.vl = smem_desc(smem_u32(sm.vl[0]), BN * 128, 1024);
+    d.kh = smem_desc(smem_u32(sm.k[0]), 16, 1024);
+    d.kl = smem_desc(smem_u32(sm.k[0] + BN * 128), 16, 1024);
+    d.vh = smem_desc(smem_u32(sm.v[0]), BN * 128, 1024);  // MN-major (P V B operand)
+    d.vl = smem_desc(smem_u32(sm.v[0] + BN * 128), BN * 128, 1024);
     return d;
 }
 
-// S = Q K^T of the key tile in stage `stage` into TMEM buffer b.
+// S = Q K^T of the key tile in stage `stage` into TMEM buffer b (TS: Q from
+// TMEM, so only K is read from shared memory).
 __device__ __forceinline__ void issue_s(const Descs& d, uint32_t tm, int stage, int b) {
     constexpr uint32_t idesc = idesc_bf16(BM, BN, 0, 0);
-    const uint32_t so = stage * STAGE_BYTES;
+    const uint32_t so = stage * KV_BYTES;
     const uint64_t kh = desc_add(d.kh, so), kl = desc_add(d.kl, so);
 #pragma unroll
     for (int s = 0; s < D / 16; ++s) {
         const uint32_t o = s * 32;
-        mma_ss(tm + col_s(b), desc_add(d.qh, o), desc_add(kh, o), idesc, s > 0);
-        mma_ss(tm + col_s(b), desc_add(d.qh, o), desc_add(kl, o), idesc, 1);
-        mma_ss(tm + col_s(b), desc_add(d.ql, o), desc_add(kh, o), idesc, 1);
+        mma_ts(tm + col_s(b), tm + Q_HI + 8 * s, desc_add(kh, o), idesc, s > 0);
+        mma_ts(tm + col_s(b), tm + Q_HI + 8 * s, desc_add(kl, o), idesc, 1);
+        mma_ts(tm + col_s(b), tm + Q_LO + 8 * s, desc_add(kh, o), idesc, 1);
     }
 }
 
-// O_tile = P V of the key tile in stage `stage`, P packed over S buffer b.
-__device__ __forceinline__ void issue_pv(const Descs& d, uint32_t tm, int stage, int b) {
+// O (+)= P V of the key tile in stage `stage`, P packed over S buffer b;
+// `first`: the item's first tile (O is overwritten).
+__device__ __forceinline__ void issue_pv(const Descs& d, uint32_t tm, int stage, int b, bool first) {
     constexpr uint32_t idesc = idesc_bf16(BM, D, 0, 1);
-    const uint32_t so = stage * STAGE_BYTES;
+    const uint32_t so = stage * KV_BYTES;
     const uint64_t vh = desc_add(d.vh, so), vl = desc_add(d.vl, so);
 #pragma unroll
     for (int s = 0; s < BN / 16; ++s) {
         const uint32_t o = s * 2048;
         const uint32_t ph = tm + col_s(b) + 32 * (s >> 1) + 8 * (s & 1);
-        mma_ts(tm + col_o(b), ph, desc_add(vh, o), idesc, s > 0);
-        mma_ts(tm + col_o(b), ph, desc_add(vl, o), idesc, 1);
-        mma_ts(tm + col_o(b), ph + 16, desc_add(vh, o), idesc, 1);
+        mma_ts(tm + COL_O, ph, desc_add(vh, o), idesc, (first && s == 0) ? 0u : 1u);
+        mma_ts(tm + COL_O, ph, desc_add(vl, o), idesc, 1);
+        mma_ts(tm + COL_O, ph + 16, desc_add(vh, o), idesc, 1);
     }
 }
 
-__global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
+// TMA of one raw tile: `rows` rows of slab (b, h) from row `row0`.
+__device__ __forceinline__ void load_tile(const CUtensorMap& map, void* dst, uint64_t* bar, uint32_t bytes, int h,
+                                          int row0, int b) {
+    mbar_arrive_expect_tx(bar, bytes);
+    tma_load_3d(dst, &map, h * D, row0, b, bar);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_constant__ Params p) {
     pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-    const int nslab = p.B * p.H;
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int cta = static_cast<int>(blockIdx.x);
@@ -139,209 +233,435 @@ __global__ void __launch_bounds__(NT, 2) attn_fwd_tc64(const Params p) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.bar_s[i], 1);
             mbar_init(&sm.bar_o[i], 1);
+            mbar_init(&sm.k_full[i], 1);
+            mbar_init(&sm.v_full[i], 1);
+            mbar_init(&sm.k_ready[i], NSM);
+            mbar_init(&sm.pv_ready[i], NSM);
         }
+        mbar_init(&sm.q_full, 1);
+        mbar_init(&sm.q_ready, NSM);
+        mbar_init(&sm.stg_free, NSM);
+        mbar_init(&sm.drain, 1);
+        fence_barrier_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = sm.tmem_slot;
-    Descs dsc;
-    if (tid == 0) dsc = make_descs(sm);
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     bool failed = false;
-    int g = 0;  // the CTA's tile sequence number: TMEM buffer and K / V stage g&1, barrier phases
 
-    for (int r = 0; !failed; ++r) {
-    // Item r of this CTA in the snake order over the items (longest first).
-    const int w = r * G + ((r & 1) ? G - 1 - cta : cta);
-    if (w >= p.n_work) break;
-    const int qt = p.n_qtiles - 1 - w / nslab;
-    const int slab = w % nslab;
-    const int b = slab / p.H;
-    const int h = slab % p.H;
-    const int q0 = qt * BM;
-    const int row = q0 + tid;
-    const int n_kv = p.causal ? min(p.n_ktiles, (q0 + BM + BN - 1) / BN) : p.n_ktiles;
-
-    const long base = static_cast<long>(b) * p.T;
-    const float* qg = p.q + base * p.ld_qkv + h * D;
-    const float* kg = p.k + base * p.ld_qkv + h * D;
-    const float* vg = p.v + base * p.ld_qkv + h * D;
-    const int g0 = g;
-
-    // Every stage and buffer is free: the previous item's last P V is done.
-    tc::stage_rows2<BN, NT>(sm.kh[g0 & 1], sm.kl[g0 & 1], kg, p.ld_qkv, sm.vh[g0 & 1], sm.vl[g0 & 1], vg, p.ld_qkv, 0,
-                            p.T, tid);
-    tc::stage_rows<BM, NT>(sm.qh, sm.ql, qg, p.ld_qkv, q0, p.T, p.scale_log2, tid);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-        issue_s(dsc, tm, g0 & 1, g0 & 1);
-        mma_commit(&sm.bar_s[g0 & 1]);
-    }
-    if (n_kv > 1) tc::stage_rows<BN, NT>(sm.kh[(g0 + 1) & 1], sm.kl[(g0 + 1) & 1], kg, p.ld_qkv, BN, p.T, 1.f, tid);
-    fence_async_smem();
-
-    float o[D];
-#pragma unroll
-    for (int c = 0; c < D; ++c) o[c] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    float alpha_prev = 1.f;  // rescale factor of the tile whose P V is still pending
-
-    // O <- O * alpha + (P V tile in buffer b).
-    auto fold = [&](int b, float alpha) {
-        float sv[32];
-#pragma unroll
-        for (int c = 0; c < D; c += 32) {
-            tmem_ld32(lane_base + tm + col_o(b) + c, sv);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha, sv[i]);
-        }
-    };
-
-    for (int j = 0; j < n_kv; ++j, ++g) {
-        const int bf = g & 1;  // TMEM buffer / smem stage of tile j
-        const int k0 = j * BN;
-        const bool ok_s = mbar_wait(&sm.bar_s[bf], (g >> 1) & 1);
-        if (__syncthreads_or(!ok_s)) {
-            failed = true;
-            break;
-        }
-        tc_fence_after();
-        const bool need_mask = (p.causal && k0 + BN - 1 > q0) || k0 + BN > p.T;
-
-        // Tile row max over the 64 scores (masked columns to -inf), eight
-        // independent chains.  Columns >= nv of this row are masked.
-        float sv[BN];
-        tmem_ld32(lane_base + tm + col_s(bf), *reinterpret_cast<float(*)[32]>(&sv[0]));
-        tmem_ld32(lane_base + tm + col_s(bf) + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
-        tmem_wait_ld();
-        if (need_mask) {
-            const int nv = min(p.T - k0, p.causal ? row - k0 + 1 : BN);
-#pragma unroll
-            for (int i = 0; i < BN; ++i) sv[i] = (i < nv) ? sv[i] : -INFINITY;
-        }
-        float mx[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mx[u] = fmaxf(sv[u], sv[u + 8]);
-#pragma unroll
-        for (int i = 16; i < BN; i += 8)
-#pragma unroll
-            for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], sv[i + u]);
-        const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-        const float mn = fmaxf(m, tmax);
-        const float ms = (mn == -INFINITY) ? 0.f : mn;
-        const float alpha = ex2(m - ms);
-        m = mn;
-
-        // Probabilities, packed bf16 hi / lo over the S columns just read.
-        float acc8[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc8[u] = 0.f;
-#pragma unroll
-        for (int c = 0; c < BN; c += 32) {
-            uint32_t ph[16], pl[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-                const float e0 = ex2(sv[c + i] - ms), e1 = ex2(sv[c + i + 1] - ms);
-                acc8[(i >> 1) & 7] += e0 + e1;
-                split2(e0, e1, ph[i / 2], pl[i / 2]);
+    if (warp == MMA_WARP) {
+        // ------------------------------------------------------------ MMA issuer
+        // One lane issues every tcgen05.mma, in whichever order the
+        // conditions are met (non-blocking probes of the barriers):
+        //   S_ns   once K_ns is converted (and, for an item's first tile, its
+        //          Q), PV_{ns-2} issued (S_ns overwrites P_{ns-2}; the tensor
+        //          core runs one thread's MMAs in order)
+        //   PV_np  once P_np is written, O rescaled and V_np converted
+        // Each probe is unambiguous: the previous phase of the probed barrier
+        // completed before the MMA that needed it was issued.
+        if ((tid & 31) == 0) {
+            Ahead sq, pq;
+            sq.r = 0;
+            sq.set(p, cta, G);
+            pq = sq;
+            int ns = 0, np = 0;
+            uint64_t t_idle = 0;
+            while (!failed && (sq.valid() || np < ns)) {
+                bool progressed = false;
+                if (np < ns && mbar_test_wait(&sm.pv_ready[np & 1], (np >> 1) & 1)) {
+                    tc_fence_after();
+                    issue_pv(make_descs(sm), tm, np & 1, np & 1, pq.j == 0);
+                    mma_commit(&sm.bar_o[np & 1]);
+                    ++np;
+                    pq.next(p, cta, G);
+                    progressed = true;
+                }
+                if (sq.valid() && np >= ns - 1 && mbar_test_wait(&sm.k_ready[ns & 1], (ns >> 1) & 1) &&
+                    (sq.j != 0 || mbar_test_wait(&sm.q_ready, sq.r & 1))) {
+                    tc_fence_after();
+                    issue_s(make_descs(sm), tm, ns & 1, ns & 1);
+                    mma_commit(&sm.bar_s[ns & 1]);
+                    ++ns;
+                    sq.next(p, cta, G);
+                    progressed = true;
+                }
+                if (progressed) {
+                    t_idle = 0;
+                } else {
+                    // Idle: back off so the poll leaves the sub-partition's
+                    // issue slots to the softmax warps.
+                    const uint64_t now = globaltimer_ns();
+                    if (t_idle == 0) t_idle = now;
+                    else if (now - t_idle > 1000000000ull) failed = true;
+                    __nanosleep(IDLE_NS);
+                }
             }
-            tmem_st16(lane_base + tm + col_s(bf) + c, ph);
-            tmem_st16(lane_base + tm + col_s(bf) + c + 16, pl);
+            if (failed) {
+                // MMAs still in flight complete before the columns are freed.
+                mma_commit(&sm.drain);
+                mbar_wait(&sm.drain, 0, 10000000ull);
+            }
         }
-        const float rs = ((acc8[0] + acc8[1]) + (acc8[2] + acc8[3])) + ((acc8[4] + acc8[5]) + (acc8[6] + acc8[7]));
-        l = l * alpha + rs;
-        tmem_wait_st();
-        tc_fence_before();
-        __syncthreads();
+        __syncwarp();
+    } else if (warp == TMA_WARP) {
+        // ------------------------------------------------------------ TMA issuer
+        // One lane issues every copy as soon as its buffer is free.  A copy
+        // instruction can wait for the SM's copy engine, which is why this
+        // is not the lane that issues the MMAs.
+        //   K_gk -> stage gk&1      once S_{gk-2} is done
+        //   V_gv -> stage gv&1      once PV_{gv-2} is done and, if tile gv-2
+        //                           ended an item, that item's O staging in
+        //                           the stage is read out (stg_free)
+        //   Q of item qr            once item qr-1's Q is in TMEM (q_ready)
+        // Probes are unambiguous by induction: the copy into a buffer one
+        // use earlier waited for the phase before the one probed now.
+        if ((tid & 31) == 0) {
+            prefetch_tensormap(&p.tq);
+            prefetch_tensormap(&p.tk);
+            prefetch_tensormap(&p.tv);
+            Ahead kq, vq, qq;
+            kq.r = 0;
+            kq.set(p, cta, G);
+            vq = kq;
+            qq = kq;
+            int gk = 0, gv = 0;
+            int stg_item[2] = {-1, -1};  // item whose O staging occupies V stage s
+            uint64_t t_idle = 0;
+            while (!failed && (kq.valid() || vq.valid() || qq.valid())) {
+                bool progressed = false;
+                if (kq.valid() && (gk < 2 || mbar_test_wait(&sm.bar_s[gk & 1], ((gk - 2) >> 1) & 1))) {
+                    const int sl = kq.slab(p);
+                    load_tile(p.tk, sm.k[gk & 1], &sm.k_full[gk & 1], KV_BYTES, sl % p.H, kq.j * BN, sl / p.H);
+                    ++gk;
+                    kq.next(p, cta, G);
+                    progressed = true;
+                }
+                if (vq.valid() && (gv < 2 || (mbar_test_wait(&sm.bar_o[gv & 1], ((gv - 2) >> 1) & 1) &&
+                                              (stg_item[gv & 1] < 0 ||
+                                               mbar_test_wait(&sm.stg_free, stg_item[gv & 1] & 1))))) {
+                    stg_item[gv & 1] = -1;
+                    if (vq.j + 1 == vq.n_kv) stg_item[gv & 1] = vq.r;
+                    const int sl = vq.slab(p);
+                    load_tile(p.tv, sm.v[gv & 1], &sm.v_full[gv & 1], KV_BYTES, sl % p.H, vq.j * BN, sl / p.H);
+                    ++gv;
+                    vq.next(p, cta, G);
+                    progressed = true;
+                }
+                if (qq.valid() && (qq.r == 0 || mbar_test_wait(&sm.q_ready, (qq.r - 1) & 1))) {
+                    const int sl = qq.slab(p);
+                    const int q0 = (p.n_qtiles - 1 - qq.w / (p.B * p.H)) * BM;
+                    mbar_arrive_expect_tx(&sm.q_full, Q_BYTES);
+                    tma_load_3d(sm.q, &p.tq, (sl % p.H) * D, q0, sl / p.H, &sm.q_full);
+                    tma_load_3d(sm.q + Q_BOX_BYTES, &p.tq, (sl % p.H) * D + 32, q0, sl / p.H, &sm.q_full);
+                    ++qq.r;
+                    qq.set(p, cta, G);
+                    progressed = true;
+                }
+                if (progressed) {
+                    t_idle = 0;
+                } else {
+                    // Idle: back off so the poll leaves the sub-partition's
+                    // issue slots to the softmax warps.
+                    const uint64_t now = globaltimer_ns();
+                    if (t_idle == 0) t_idle = now;
+                    else if (now - t_idle > 1000000000ull) failed = true;
+                    __nanosleep(IDLE_NS);
+                }
+            }
+            if (failed) {
+                // Copies still landing complete before the CTA's shared memory
+                // is released (bounded waits: 10 ms each).  Earlier copies into
+                // a stage were consumed before the stage was reloaded.
+                for (int t = max(0, gk - 2); t < gk; ++t) mbar_wait(&sm.k_full[t & 1], (t >> 1) & 1, 10000000ull);
+                for (int t = max(0, gv - 2); t < gv; ++t) mbar_wait(&sm.v_full[t & 1], (t >> 1) & 1, 10000000ull);
+                if (qq.r > 0) mbar_wait(&sm.q_full, (qq.r - 1) & 1, 10000000ull);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ softmax
+        // Two threads per query row: warp w handles TMEM lanes 32*(w%4).. (rows)
+        // and key columns 32*hf..32*hf+31 of each tile, hf = w/4 (the other
+        // half of the row is warp w^4).  The halves exchange their row max
+        // through shared memory once per tile and their row sums once per
+        // item.  Waits are bounded; a failed one is reported at the next
+        // barrier of the eight warps (named barrier 1), after which all of
+        // them stop together.
+        //
+        // O accumulates in TMEM across an item's tiles (PV_g adds onto it).
+        // The probabilities are exp2(s - mu) with mu a running row maximum
+        // that is raised only when a tile's maximum exceeds it by more than
+        // RESCALE_LOG2 (then O and l are scaled by exp2(mu_old - mu_new)
+        // before PV_g), so P <= 2^RESCALE_LOG2 and O is rarely touched.
+        const int hf = warp >> 2;
+        const int rl = (warp & 3) * 32 + (tid & 31);  // row in the item's tile, TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        bool bad = false;
+        // Columns 32*hf.. of row rl of item rq's Q (scaled by scale*log2(e)),
+        // from swizzled box hf into TMEM lane rl.  Every S of the item before
+        // has completed (the caller waited for the last one).
+        auto load_q = [&](int rq) {
+            bad |= !mbar_wait(&sm.q_full, rq & 1);
+            const uint8_t* box = sm.q + hf * Q_BOX_BYTES + rl * 128;
+            uint32_t qh[16], ql[16];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float4 x = *reinterpret_cast<const float4*>(box + ((c ^ (rl & 7)) << 4));
+                split2(x.x * p.scale_log2, x.y * p.scale_log2, qh[2 * c], ql[2 * c]);
+                split2(x.z * p.scale_log2, x.w * p.scale_log2, qh[2 * c + 1], ql[2 * c + 1]);
+            }
+            tmem_st16(lane_base + tm + Q_HI + 16 * hf, qh);
+            tmem_st16(lane_base + tm + Q_LO + 16 * hf, ql);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&sm.q_ready);
+        };
+        int g = 0;  // the CTA's tile sequence number
+        Seq it;
+        it.r = 0;
+        it.set_item(p, cta, G);
+        for (int r = 0; it.valid(); ++r) {
+            const int n_kv = it.n_kv;
+            const int row = it.q0 + rl;
+            Seq nx = it;
+            ++nx.r;
+            nx.set_item(p, cta, G);
+            const bool has_next = nx.valid();
 
-        if (tid == 0) {
+            // Item start (the CTA's first item only): convert K_0 and move
+            // Q into TMEM.  Later items' K_0 and Q are converted during the
+            // previous item's last tile, so their first S runs meanwhile.
+            if (g == 0) {
+                tc::RawTile<BN, NSM> kr;
+                bad |= !mbar_wait(&sm.k_full[0], 0);
+                kr.read(sm.k[0], tid);
+                if (named_sync_or(1, NSM, bad)) {
+                    failed = true;
+                    break;
+                }
+                kr.write(sm.k[0], 1.f, tid);
+                fence_async_smem();
+                mbar_arrive(&sm.k_ready[0]);
+                load_q(0);
+            }
+
+            float mu = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+            for (int j = 0; j < n_kv; ++j, ++g) {
+                const int bf = g & 1;  // TMEM S buffer and K / V stages of tile g
+                const int k0 = j * BN;
+
+                // (1) Convert K_{g+1} (this item's next tile or the next
+                // item's first), so S_{g+1} can run during this softmax.
+                if (j + 1 < n_kv || has_next) {
+                    const int gn = g + 1;
+                    tc::RawTile<BN, NSM> kr;
+                    bad |= !mbar_wait(&sm.k_full[gn & 1], (gn >> 1) & 1);
+                    kr.read(sm.k[gn & 1], tid);
+                    if (named_sync_or(1, NSM, bad)) {
+                        failed = true;
+                        break;
+                    }
+                    kr.write(sm.k[gn & 1], 1.f, tid);
+                    fence_async_smem();
+                    mbar_arrive(&sm.k_ready[gn & 1]);
+                }
+
+                // (2) Softmax of this half of S_g: row max (masked columns to
+                // -inf, eight independent chains), combined with the other
+                // half's; then the probabilities, packed bf16 hi / lo over the
+                // 32 S columns just read (hi in the first 16, lo in the next).
+                bad |= !mbar_wait(&sm.bar_s[bf], (g >> 1) & 1);
+                tc_fence_after();
+                // The item's last S is done, so its Q columns are free: move
+                // the next item's Q in now (its first S then runs during this
+                // softmax and the epilogue).
+                if (j + 1 == n_kv && has_next) load_q(r + 1);
+                const int kb = k0 + 32 * hf;  // first key of this half
+                const bool need_mask = (p.causal && kb + 31 > it.q0) || kb + 32 > p.T;
+                const uint32_t cs = lane_base + tm + col_s(bf) + 32 * hf;
+                float sv[32];
+                tmem_ld32(cs, sv);
+                tmem_wait_ld();
+                if (need_mask) {
+                    const int nv = min(p.T - kb, p.causal ? row - kb + 1 : 32);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) sv[i] = (i < nv) ? sv[i] : -INFINITY;
+                }
+                float mx[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) mx[u] = fmaxf(sv[u], sv[u + 8]);
+#pragma unroll
+                for (int i = 16; i < 32; i += 8)
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], sv[i + u]);
+                sm.red[bf][hf][rl] = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                if (named_sync_or(1, NSM, bad)) {
+                    failed = true;
+                    break;
+                }
+                const float tmax = fmaxf(sm.red[bf][0][rl], sm.red[bf][1][rl]);
+                // Raise mu on the item's first tile, or when this tile's max is
+                // more than 2^RESCALE_LOG2 above it (both halves decide alike).
+                float alpha = 1.f;
+                if (j == 0 || tmax > mu + RESCALE_LOG2) {
+                    const float mn = fmaxf(mu, tmax);
+                    alpha = (j == 0 || mu == -INFINITY) ? 0.f : ex2(mu - mn);
+                    mu = mn;
+                }
+                const float ms = (mu == -INFINITY) ? 0.f : mu;
+                float acc8[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc8[u] = 0.f;
+                {
+                    uint32_t ph[16], pl[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const float e0 = ex2(sv[i] - ms), e1 = ex2(sv[i + 1] - ms);
+                        acc8[(i >> 1) & 7] += e0 + e1;
+                        split2(e0, e1, ph[i / 2], pl[i / 2]);
+                    }
+                    tmem_st16(cs, ph);
+                    tmem_st16(cs + 16, pl);
+                }
+                const float rs =
+                    ((acc8[0] + acc8[1]) + (acc8[2] + acc8[3])) + ((acc8[4] + acc8[5]) + (acc8[6] + acc8[7]));
+                l = (j == 0) ? rs : l * alpha + rs;
+
+                // (3) Rescale this half of O if a row of this warp raised mu
+                // (after PV_{g-1} has added onto it); convert V_g; then P_g, O
+                // and V_g are ready for PV_g.
+                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                    const int gp = g - 1;
+                    bad |= !mbar_wait(&sm.bar_o[gp & 1], (gp >> 1) & 1);
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < 32; c += 16) {
+                        float ov[16];
+                        uint32_t ow[16];
+                        tmem_ld16(lane_base + tm + COL_O + 32 * hf + c, ov);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) ow[i] = __float_as_uint(ov[i] * alpha);
+                        tmem_st16(lane_base + tm + COL_O + 32 * hf + c, ow);
+                    }
+                }
+                tmem_wait_st();
+                {
+                    tc::RawTile<BN, NSM> vr;
+                    bad |= !mbar_wait(&sm.v_full[bf], (g >> 1) & 1);
+                    vr.read(sm.v[bf], tid);
+                    if (named_sync_or(1, NSM, bad)) {
+                        failed = true;
+                        break;
+                    }
+                    vr.write(sm.v[bf], 1.f, tid);
+                }
+                fence_async_smem();
+                tc_fence_before();
+                mbar_arrive(&sm.pv_ready[bf]);
+            }
+            if (failed) break;
+
+            // The item's last P V; the row sum of both halves; normalise and
+            // store O, staged through the last tile's V stage (its P V is
+            // done; the producer reloads the stage only after stg_free), 64
+            // rows at a time, float4 chunks XOR-swizzled by row, so that the
+            // global stores are whole 256-byte rows.
+            const int gl = g - 1;
+            bad |= !mbar_wait(&sm.bar_o[gl & 1], (gl >> 1) & 1);
             tc_fence_after();
-            issue_pv(dsc, tm, bf, bf);
-            mma_commit(&sm.bar_o[bf]);
-            if (j + 1 < n_kv) {
-                issue_s(dsc, tm, bf ^ 1, bf ^ 1);
-                mma_commit(&sm.bar_s[bf ^ 1]);
-            }
-        }
-        if (j >= 1) {
-            // Fold in the previous tile's P V (its buffer is the other one).
-            const bool ok_o = mbar_wait(&sm.bar_o[bf ^ 1], ((g - 1) >> 1) & 1);
-            if (__syncthreads_or(!ok_o)) {
+            sm.red[0][hf][rl] = l;
+            if (named_sync_or(1, NSM, bad)) {
                 failed = true;
                 break;
             }
-            tc_fence_after();
-            fold(bf ^ 1, alpha_prev);
-        }
-        alpha_prev = alpha;
-        // K_{j+2} into this tile's K stage (S_j is done); V_{j+1} into the
-        // other V stage (PV_{j-1} is done).  Both become visible to the tensor
-        // core at the next iteration's barrier.
-        const bool kn = j + 2 < n_kv, vn = j + 1 < n_kv && j >= 1;
-        if (kn) tc::stage_rows<BN, NT>(sm.kh[bf], sm.kl[bf], kg, p.ld_qkv, (j + 2) * BN, p.T, 1.f, tid);
-        if (vn) tc::stage_rows<BN, NT>(sm.vh[bf ^ 1], sm.vl[bf ^ 1], vg, p.ld_qkv, (j + 1) * BN, p.T, 1.f, tid);
-        if (j == 0 && n_kv > 1) tc::stage_rows<BN, NT>(sm.vh[bf ^ 1], sm.vl[bf ^ 1], vg, p.ld_qkv, BN, p.T, 1.f, tid);
-        if (kn || vn || j == 0) fence_async_smem();
-    }
-
-    if (!failed) {
-        const int gl = g - 1;
-        const bool ok_o = mbar_wait(&sm.bar_o[gl & 1], (gl >> 1) & 1);
-        if (__syncthreads_or(!ok_o)) {
-            failed = true;
-        } else {
-            tc_fence_after();
-            fold(gl & 1, alpha_prev);
-        }
-    }
-
-    if (failed) break;
-    // Normalise and stage O through shared memory (reusing the Q tiles,
-    // float4 chunks XOR-swizzled by row) for coalesced global stores.
-    {
-        const float inv = 1.f / l;
-        float4* stg = reinterpret_cast<float4*>(sm.qh);  // 128 rows x 16 float4 = 32 KB (qh + ql)
-        __syncthreads();
+            const float lt = sm.red[0][0][rl] + sm.red[0][1][rl];
+            const float inv = 1.f / lt;
+            if (hf == 0 && row < p.T) p.lse[(static_cast<long>(it.b) * p.H + it.h) * p.T + row] = (mu + log2f(lt)) * kLn2;
+            float4* stg = reinterpret_cast<float4*>(sm.v[gl & 1]);  // 64 rows x 16 float4 = 16 KB
+            float* og = p.o + static_cast<long>(it.b) * p.T * p.ld_o + it.h * D;
 #pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4)
-            stg[tid * 16 + (c4 ^ (tid & 15))] =
-                make_float4(o[4 * c4] * inv, o[4 * c4 + 1] * inv, o[4 * c4 + 2] * inv, o[4 * c4 + 3] * inv);
-        if (row < p.T) p.lse[(static_cast<long>(b) * p.H + h) * p.T + row] = (m + log2f(l)) * kLn2;
-        __syncthreads();
-        float* og = p.o + base * p.ld_o + h * D;
+            for (int half = 0; half < 2; ++half) {
+                // TMEM loads are warp-collective: every warp loads, the warps
+                // of the rows in this round stage.
+                {
+                    float ov[32];
+                    tmem_ld32(lane_base + tm + COL_O + 32 * hf, ov);
+                    tmem_wait_ld();
+                    if ((rl >> 6) == half) {
+                        const int rr = rl & 63;
 #pragma unroll
-        for (int it = 0; it < 16; ++it) {
-            const int i = tid + it * NT;
-            const int rr = i >> 4;
-            const int c4 = i & 15;
-            if (q0 + rr < p.T)
-                *reinterpret_cast<float4*>(og + static_cast<long>(q0 + rr) * p.ld_o + c4 * 4) =
-                    stg[rr * 16 + (c4 ^ (rr & 15))];
+                        for (int i = 0; i < 8; ++i) {
+                            const int c4 = 8 * hf + i;
+                            stg[rr * 16 + (c4 ^ (rr & 15))] =
+                                make_float4(ov[4 * i] * inv, ov[4 * i + 1] * inv, ov[4 * i + 2] * inv, ov[4 * i + 3] * inv);
+                        }
+                    }
+                }
+                named_sync(1, NSM);
+#pragma unroll
+                for (int k = 0; k < 64 * 16 / NSM; ++k) {
+                    const int i = tid + k * NSM;
+                    const int rr = i >> 4;
+                    const int c4 = i & 15;
+                    const int qrow = it.q0 + 64 * half + rr;
+                    if (qrow < p.T)
+                        *reinterpret_cast<float4*>(og + static_cast<long>(qrow) * p.ld_o + c4 * 4) =
+                            stg[rr * 16 + (c4 ^ (rr & 15))];
+                }
+                named_sync(1, NSM);
+            }
+            fence_async_smem();
+            tc_fence_before();  // the next item's first P V overwrites the O columns just read
+            mbar_arrive(&sm.stg_free);
+            it = nx;
         }
     }
-    // The next item stages its Q over the rows just read, and its MMAs reuse
-    // the TMEM buffers this item's threads have read.
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    }
 
-    if (failed) {
-        if (tid == 0) atomicOr(p.status, 1);
-        // Let any MMA still in flight drain (bounded) before the columns are freed.
-        if (tid == 0) mma_commit(&sm.bar_s[0]);
-        mbar_wait(&sm.bar_s[0], 0, 10000000ull);
-        mbar_wait(&sm.bar_s[0], 1, 10000000ull);
-    }
+    if (__syncthreads_or(failed) && tid == 0) atomicOr(p.status, 1);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tm, TMEM_COLS);
+}
+
+}  // namespace
+
+namespace {
+
+using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (no link-time dependency on the driver library).
+EncodeTiled encode_tiled() {
+    static const EncodeTiled fn = []() -> EncodeTiled {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<EncodeTiled>(f);
+    }();
+    return fn;
+}
+
+// The first H*64 columns of a [B*T][ld] f32 buffer as a 3-D tensor
+// {columns, T rows, B}, boxes of `box_cols` columns x `box_rows` rows of one batch
+// (rows past T are out of bounds and read as zeros).  `base` is 16-byte
+// aligned and ld a multiple of 4 (checked at the C ABI).
+bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int H, int box_cols, int box_rows,
+                 CUtensorMapSwizzle swizzle) {
+    const EncodeTiled fn = encode_tiled();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(H) * D, static_cast<cuuint64_t>(T),
+                                static_cast<cuuint64_t>(B)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(ld) * 4 * T};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -350,10 +670,10 @@ bool fwd_tc_supported(const FwdArgs& a) { return a.d == 64; }
 
 cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches) {
     Params p;
-    p.q = a.q;
-    p.k = a.k;
-    p.v = a.v;
-    p.ld_qkv = a.ld_qkv;
+    if (!encode_rows(&p.tq, a.q, a.ld_qkv, a.B, a.T, a.H, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_rows(&p.tk, a.k, a.ld_qkv, a.B, a.T, a.H, D, BN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_rows(&p.tv, a.v, a.ld_qkv, a.B, a.T, a.H, D, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
     p.o = a.o;
     p.ld_o = a.ld_o;
     p.lse = a.lse;
@@ -383,7 +703,7 @@ cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream
     // walking its items in the snake order.
     const long slots = 2L * (num_sms > 0 ? num_sms : 148);
     const int grid = static_cast<int>(n_work < slots ? n_work : slots);
-    e = launch_pdl(attn_fwd_tc64, dim3(static_cast<unsigned>(grid)), dim3(NT), smem, stream, p);
+    e = launch_pdl(attn_fwd_tc64, dim3(static_cast<unsigned>(grid)), dim3(NTHREADS), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

@@ -57,6 +57,39 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Arrive once and add `bytes` to the phase's expected transaction count (the
+// producer side of a TMA load that signals this barrier).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Makes barrier initialisation visible to the async proxy (TMA) before the
+// first copy that signals one of them.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- TMA
+// Tiled 3-D load of one box of `map` at coordinates (c0, c1, c2) into this
+// CTA's shared memory at `dst`, completing `bytes` of transactions on `bar`.
+// `map` is the address of a __grid_constant__ kernel parameter.  No
+// multicast: the box lands in the issuing CTA only.  Coordinates past the
+// tensor's extent read zeros.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Brings a tensor map (address of a __grid_constant__ parameter) into the
+// TMA unit's descriptor cache ahead of its first copy.
+__device__ __forceinline__ void prefetch_tensormap(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -85,6 +118,26 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
 
 // ---------------------------------------------------------------- fences
 // Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
+// Named barrier over `nthreads` threads (whole warps), id 1..15: for a subset
+// of a CTA's warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also returns whether `pred` held on any participating thread.
+__device__ __forceinline__ bool named_sync_or(uint32_t id, uint32_t nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

@@ -110,5 +110,39 @@ __device__ __forceinline__ void stage_rows2(uint8_t* hi0, uint8_t* lo0, const fl
     x.store(hi0, lo0, hi1, lo1, t);
 }
 
+// A raw f32 tile of R rows x 64 floats as a TMA box lands it (row-major,
+// 256 bytes per row) -> the same bytes rewritten as bf16 hi (first R*128
+// bytes) and lo (next R*128 bytes) in the 128B-swizzled layout, scaled by
+// `mul`.  read() stages the thread's share in registers; the caller makes
+// every thread's read() complete (a barrier over the NTH threads) before any
+// write(), because the tile is converted in place.  Thread `t` of NTH handles
+// float4 f = t, t + NTH, ... (row f/16, columns 4(f%16)..+3), so each group
+// of eight threads reads 128 contiguous bytes and no read conflicts.
+template <int R, int NTH>
+struct RawTile {
+    static_assert((R * 16) % NTH == 0, "tile items must divide evenly");
+    static constexpr int ITEMS = R * 16 / NTH;
+    float4 a[ITEMS];
+
+    __device__ __forceinline__ void read(const uint8_t* tile, int t) {
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) a[it] = reinterpret_cast<const float4*>(tile)[t + it * NTH];
+    }
+
+    __device__ __forceinline__ void write(uint8_t* tile, float mul, int t) const {
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const int f = t + it * NTH;
+            const int r = f >> 4, c4 = f & 15;
+            uint2 h, l;
+            sm100::split2(a[it].x * mul, a[it].y * mul, h.x, l.x);
+            sm100::split2(a[it].z * mul, a[it].w * mul, h.y, l.y);
+            const uint32_t off = sm100::sw128(r, c4 >> 1) + (c4 & 1) * 8;
+            *reinterpret_cast<uint2*>(tile + off) = h;
+            *reinterpret_cast<uint2*>(tile + R * 128 + off) = l;
+        }
+    }
+};
+
 }  // namespace tc
 }  // namespace kattn
