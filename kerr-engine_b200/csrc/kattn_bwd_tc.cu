@@ -332,7 +332,10 @@ __device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
-    pdl_enter();
+    // Launched behind attn_bwd_rowdot, whose outputs (D, the zeroed dq) only
+    // the loader warps touch: they wait for it; the elementwise warps stage
+    // the first item's K / V meanwhile.
+    pdl_launch();
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -375,6 +378,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         // registers, issues the global loads of tile n+1 into registers, then
         // adds tile n-2's dQ into dq (gradient products finish in tile
         // order): the loads are in flight while the step waits for that dQ.
+        pdl_wait();
         const int t = tid - NELEM;
         const int qd = warp & 3;
         Cursor cl, cq;  // tile to load, tile whose dQ is added

@@ -44,6 +44,16 @@ __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// The two halves of pdl_enter, for a kernel whose threads do not all read
+// what the grid before it wrote: pdl_launch lets the next grid start
+// launching; pdl_wait blocks the calling thread until the grid before has
+// finished and its memory is visible.  The grid before that one has finished
+// as soon as this grid is running (that grid waited for it before letting
+// this one launch), so only the immediately preceding grid's outputs need
+// pdl_wait.
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Reductions over the 16 lanes that share a row (lane bits 0..3).
 __device__ __forceinline__ float max16(float x) {
 #pragma unroll
