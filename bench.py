@@ -12,7 +12,9 @@ N(0,1)/8 and dout ~ N(0,1) (no checkpoint or corpus is available).
 
 metric: tokens/s = (sequences x seq_len x ranks) / step time (CUDA events,
 max over ranks).  e2e: the same through the host-buffer C ABI calls
-(kattn_fwd_host / kattn_bwd_host), host<->device copies inside the timed region.
+(kattn_fwd_host_save / kattn_bwd_host_saved, the forward state kept on the
+device as the reference's AttnCache; e2e_plain: kattn_fwd_host /
+kattn_bwd_host), host<->device copies inside the timed region.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -307,22 +309,40 @@ def run_ours(args):
         h["dq"], h["dk"], h["dv"] = kerr_attn.split_qkv(h["dqkv"], C)
         hb.append(h)
 
+    # The saved-state pair (the reference's AttnCache flow): each block's
+    # forward keeps q/k/v, o and lse on the device for its backward, which
+    # then sends only dout up.  The plain pair re-sends everything.
+    saved = [kerr_attn.Saved(ctx) for _ in hb]
+
     def step_host():
+        for h, sv in zip(hb, saved):
+            kerr_attn.fwd_host_save(ctx, sv, h["q"], h["k"], h["v"], h["o"], h["lse"], H)
+        for h, sv in zip(reversed(hb), reversed(saved)):
+            kerr_attn.bwd_host_saved(ctx, sv, h["dout"], h["dq"], h["dk"], h["dv"])
+
+    def step_host_plain():
         for h in hb:
             kerr_attn.fwd_host(ctx, h["q"], h["k"], h["v"], h["o"], h["lse"], H)
         for h in reversed(hb):
             kerr_attn.bwd_host(ctx, h["q"], h["k"], h["v"], h["o"], h["dout"], h["lse"], h["dq"], h["dk"], h["dv"], H)
 
-    step_host()
-    sync_all()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        step_host()
-    sync_all()
-    e2e_s = max_over_ranks(time.perf_counter() - t0) / e2e_steps
+    def time_host(fn):
+        fn()
+        sync_all()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            fn()
+        sync_all()
+        return max_over_ranks(time.perf_counter() - t0) / e2e_steps
+
+    e2e_s = time_host(step_host)
+    e2e_plain_s = time_host(step_host_plain)
+    for sv in saved:
+        sv.close()
     f4 = 4
-    h2d = NB * (B * T * 3 * C * f4 + (B * T * 3 * C + 2 * B * T * C + B * H * T) * f4)
+    h2d = NB * (B * T * 3 * C + B * T * C) * f4
     d2h = NB * ((B * T * C + B * H * T) * f4 + B * T * 3 * C * f4)
+    h2d_plain = NB * (B * T * 3 * C * f4 + (B * T * 3 * C + 2 * B * T * C + B * H * T) * f4)
 
     peaks, peak_src = measured_peaks()
     work = algorithmic(B, T, H, d)
@@ -359,7 +379,11 @@ def run_ours(args):
         "config": dict(WORKLOAD, global_batch=B * world, parallelism=f"dp{world} (batch shards, no exchange)"),
         "e2e": {"value": tokens_per_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "api": "kattn_fwd_host + kattn_bwd_host per block, pinned host buffers"},
+                "api": "kattn_fwd_host_save + kattn_bwd_host_saved per block (forward state kept on the "
+                       "device, as the reference's AttnCache), pinned host buffers"},
+        "e2e_plain": {"value": tokens_per_step / e2e_plain_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d_plain,
+                      "d2h_bytes_per_step": d2h,
+                      "api": "kattn_fwd_host + kattn_bwd_host per block (every input sent up by each call)"},
         "gpu_launches": launches, "kernel_path": args.path,
         "kernel_timing": {"method": "second pass of the same steps with CUDA events around each call",
                           "ms_per_step_with_events": ms_step_ev},

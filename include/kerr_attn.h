@@ -148,6 +148,40 @@ int kattn_bwd_host(kattn_ctx* ctx,
                    float* dq, float* dk, float* dv, long ld_dqkv,
                    int B, int T, int H, int d, float scale, int causal);
 
+/* Host-buffer calls, as above, keep their copies off the critical path: the
+ * sequences are split into up to 8 chunks that move at least ~8 MB each, and one
+ * chunk's results are copied back while the next chunk's kernels run and
+ * the chunk after that is copied in (three streams of the context).  Pinned
+ * host memory lets the copies run at link speed; pageable memory works too. */
+
+/* ---- Saved forward state (the reference's AttnCache) ----------------------
+ * The reference keeps q, k, v and the attention weights of each layer's
+ * forward in an AttnCache (src/pipeline.rs:157-164) and hands them back to
+ * attention_backward (src/pipeline.rs:707-714).  A kattn_saved is that cache
+ * on the device: kattn_fwd_host_save runs kattn_fwd_host and keeps q/k/v, o
+ * and lse resident; kattn_bwd_host_saved then needs only dout from the host,
+ * so a training step moves q/k/v, o and lse across the link once instead of
+ * twice.  A saved state belongs to the context it was created on; it is
+ * reused (and its device memory regrown when a larger forward needs it) by
+ * every later kattn_fwd_host_save into it. */
+typedef struct kattn_saved kattn_saved;
+
+int kattn_saved_create(kattn_ctx* ctx, kattn_saved** out);
+int kattn_saved_destroy(kattn_saved* saved);
+
+/* kattn_fwd_host, keeping the forward's device state in `saved`. */
+int kattn_fwd_host_save(kattn_ctx* ctx, kattn_saved* saved,
+                        const float* q, const float* k, const float* v, long ld_qkv,
+                        float* o, long ld_o, float* lse,
+                        int B, int T, int H, int d, float scale, int causal);
+
+/* kattn_bwd_host for the forward held in `saved` (its shape, scale and
+ * causal flag): dout in, dq / dk / dv out, all host buffers.
+ * KATTN_ERR_INVALID_ARGUMENT when `saved` holds no completed forward. */
+int kattn_bwd_host_saved(kattn_ctx* ctx, const kattn_saved* saved,
+                         const float* dout, long ld_o,
+                         float* dq, float* dk, float* dv, long ld_dqkv);
+
 /* Number of kernel launches the last kattn_fwd / kattn_bwd call on this
  * thread enqueued (0 for an empty problem or an error).  For the
  * kattn_linear_* calls: this library's kernels, not the cuBLAS GEMMs. */

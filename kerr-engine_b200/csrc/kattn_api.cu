@@ -9,8 +9,10 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <vector>
 
 #include "kattn_launch.h"
 #include "kerr_attn.h"
@@ -20,13 +22,31 @@ struct kattn_ctx {
     int num_sms = 0;
     std::atomic<int> path{KATTN_PATH_AUTO};
     int* d_status = nullptr;        // device word set by kernels whose bounded waits give up
-    cudaStream_t stream = nullptr;  // used by the host-buffer entry points
+    cudaStream_t stream = nullptr;  // host-buffer entry points: kernels
+    cudaStream_t h2d = nullptr;     // host-buffer entry points: host-to-device copies
+    cudaStream_t d2h = nullptr;     // host-buffer entry points: device-to-host copies
+    std::vector<cudaEvent_t> events;  // chunk hand-offs between those three streams
     std::mutex host_mu;             // serialises the host-buffer entry points
     char* arena = nullptr;          // device staging for the host-buffer entry points
     size_t arena_bytes = 0;
     float* noalloc_ws = nullptr;    // device address of g_noalloc_ws on this device
     void* cublas = nullptr;         // cublasHandle_t of the projection GEMMs, created on first use
     std::mutex proj_mu;             // binds the handle to a stream and enqueues a call as one step
+};
+
+// Device-resident state of one forward (the reference's AttnCache):
+// q/k/v, o and lse, kept for the backward of the same sequences.
+struct kattn_saved {
+    kattn_ctx* ctx = nullptr;
+    char* buf = nullptr;  // one allocation, grown as needed
+    size_t bytes = 0;
+    float* qkv = nullptr;  // [B*T][3C]
+    float* o = nullptr;    // [B*T][C]
+    float* lse = nullptr;  // [B][H][T]
+    int B = 0, T = 0, H = 0, d = 0;
+    float scale = 0.f;
+    int causal = 0;
+    bool valid = false;  // a forward completed into it
 };
 
 // Fixed backward workspace of kattn_bwd_noalloc: [B][H][T] floats, shared by
@@ -237,6 +257,164 @@ cudaError_t copy_rows(float* dst, long ld_dst, const float* src, long ld_src, in
                              static_cast<size_t>(rows), kind, s);
 }
 
+// Host-buffer calls are pipelined over chunks of whole sequences: chunk c's
+// inputs go up on ctx->h2d, its kernels run on ctx->stream once they have
+// landed, and its outputs come down on ctx->d2h once the kernels are done.
+// So one chunk's download overlaps the next chunk's kernels and the upload
+// of the one after (the link carries both directions at once).  Chunks move
+// at least ~8 MB (inputs plus outputs) and are at most 8; a small problem is
+// one chunk.
+struct Chunks {
+    int n = 1, per = 0;  // chunk count, sequences per chunk
+    Chunks(int B, size_t bytes) {
+        const size_t target = 8u << 20;
+        long want = static_cast<long>(bytes / target);
+        if (want < 1) want = 1;
+        if (want > 8) want = 8;
+        if (want > B) want = B;
+        per = static_cast<int>((B + want - 1) / want);
+        n = (B + per - 1) / per;
+    }
+    int b0(int c) const { return c * per; }
+    int count(int c, int B) const { return std::min(per, B - c * per); }
+};
+
+int ensure_events(kattn_ctx* ctx, size_t n) {
+    while (ctx->events.size() < n) {
+        cudaEvent_t ev;
+        const cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+        ctx->events.push_back(ev);
+    }
+    return KATTN_OK;
+}
+
+// Makes `waiter` wait for the work enqueued so far on `from` (event `ev`).
+cudaError_t hand_off(cudaStream_t from, cudaStream_t waiter, cudaEvent_t ev) {
+    cudaError_t e = cudaEventRecord(ev, from);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(waiter, ev, 0);
+    return e;
+}
+
+// Waits for everything the three host-call streams hold (also after an
+// error, so that no copy into the staging buffers outlives the call).
+cudaError_t drain_host_streams(kattn_ctx* ctx) {
+    cudaError_t e1 = cudaStreamSynchronize(ctx->h2d);
+    cudaError_t e2 = cudaStreamSynchronize(ctx->stream);
+    cudaError_t e3 = cudaStreamSynchronize(ctx->d2h);
+    return e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3);
+}
+
+// Host q/k/v rows [r0, r0+rows) -> the packed device [rows][3C] block at dqkv.
+cudaError_t upload_qkv(float* dqkv, const float* q, const float* k, const float* v, long ld_qkv, int C, long r0,
+                       long rows, cudaStream_t s) {
+    if (k == q + C && v == q + 2 * C && ld_qkv == 3L * C)
+        return cudaMemcpyAsync(dqkv, q + r0 * ld_qkv, sizeof(float) * rows * 3 * C, cudaMemcpyHostToDevice, s);
+    cudaError_t e = copy_rows(dqkv, 3L * C, q + r0 * ld_qkv, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = copy_rows(dqkv + C, 3L * C, k + r0 * ld_qkv, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = copy_rows(dqkv + 2 * C, 3L * C, v + r0 * ld_qkv, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+    return e;
+}
+
+// The packed device [rows][3C] gradient block -> host dq/dk/dv rows [r0, r0+rows).
+cudaError_t download_grads(float* dq, float* dk, float* dv, long ld_d, const float* dgrad, int C, long r0, long rows,
+                           cudaStream_t s) {
+    if (dk == dq + C && dv == dq + 2 * C && ld_d == 3L * C)
+        return cudaMemcpyAsync(dq + r0 * ld_d, dgrad, sizeof(float) * rows * 3 * C, cudaMemcpyDeviceToHost, s);
+    cudaError_t e = copy_rows(dq + r0 * ld_d, ld_d, dgrad, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = copy_rows(dk + r0 * ld_d, ld_d, dgrad + C, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess)
+        e = copy_rows(dv + r0 * ld_d, ld_d, dgrad + 2 * C, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
+    return e;
+}
+
+// Forward from host buffers through the pipelined chunks, into the device
+// buffers dqkv [B*T][3C], d_o [B*T][C], d_lse [B][H][T] (o and lse also come
+// back to the host).  The caller holds host_mu and has the device current.
+int fwd_host_run(kattn_ctx* ctx, float* dqkv, float* d_o, float* d_lse, const float* q, const float* k,
+                 const float* v, long ld_qkv, float* o, long ld_o, float* lse, int B, int T, int H, int d,
+                 float scale, int causal) {
+    const int C = H * d;
+    const Chunks ch(B, sizeof(float) * static_cast<size_t>(B) * T * (4 * C + H));  // q/k/v up; o, lse down
+    KATTN_TRY(ensure_events(ctx, 2 * static_cast<size_t>(ch.n)));
+    int launches = 0;
+    cudaError_t e = cudaSuccess;
+    const char* what = "";
+    for (int c = 0; c < ch.n && e == cudaSuccess; ++c) {
+        const int b0 = ch.b0(c), bc = ch.count(c, B);
+        const long r0 = static_cast<long>(b0) * T, rows = static_cast<long>(bc) * T;
+        const long l0 = static_cast<long>(b0) * H * T;
+        float* cq = dqkv + r0 * 3 * C;
+        what = "host-to-device copy";
+        e = upload_qkv(cq, q, k, v, ld_qkv, C, r0, rows, ctx->h2d);
+        if (e == cudaSuccess) e = hand_off(ctx->h2d, ctx->stream, ctx->events[2 * c]);
+        if (e != cudaSuccess) break;
+        what = "forward launch";
+        const kattn::FwdArgs a{cq, cq + C, cq + 2 * C, 3L * C, d_o + r0 * C, C, d_lse + l0, bc, T, H, d, scale, causal};
+        e = dispatch_fwd(ctx, a, ctx->stream, &launches);
+        if (e == cudaSuccess) e = hand_off(ctx->stream, ctx->d2h, ctx->events[2 * c + 1]);
+        if (e != cudaSuccess) break;
+        what = "device-to-host copy";
+        e = copy_rows(o + r0 * ld_o, ld_o, d_o + r0 * C, C, C, rows, cudaMemcpyDeviceToHost, ctx->d2h);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(lse + l0, d_lse + l0, sizeof(float) * static_cast<size_t>(bc) * H * T,
+                                cudaMemcpyDeviceToHost, ctx->d2h);
+    }
+    const cudaError_t es = drain_host_streams(ctx);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    if (es != cudaSuccess) return cuda_fail(es, "cudaStreamSynchronize");
+    return ok_with_launches(launches);
+}
+
+// Backward from host buffers through the pipelined chunks.  q/k/v, o and lse
+// are uploaded into d_qkv / d_o / d_lse when `upload_saved` is set and are
+// already resident there otherwise; dout goes up to d_do; the gradients come
+// down from d_grad.  d_dsum is the [B][H][T] workspace.
+int bwd_host_run(kattn_ctx* ctx, float* d_qkv, float* d_o, float* d_lse, bool upload_saved, const float* q,
+                 const float* k, const float* v, long ld_qkv, const float* o, const float* lse, const float* dout,
+                 long ld_o, float* dq, float* dk, float* dv, long ld_d, float* d_do, float* d_grad, float* d_dsum,
+                 int B, int T, int H, int d, float scale, int causal) {
+    const int C = H * d;
+    const size_t per_row = (upload_saved ? 5u * C + H : 1u * C) + 3u * C;  // inputs up, gradients down
+    const Chunks ch(B, sizeof(float) * static_cast<size_t>(B) * T * per_row);
+    KATTN_TRY(ensure_events(ctx, 2 * static_cast<size_t>(ch.n)));
+    int launches = 0;
+    cudaError_t e = cudaSuccess;
+    const char* what = "";
+    for (int c = 0; c < ch.n && e == cudaSuccess; ++c) {
+        const int b0 = ch.b0(c), bc = ch.count(c, B);
+        const long r0 = static_cast<long>(b0) * T, rows = static_cast<long>(bc) * T;
+        const long l0 = static_cast<long>(b0) * H * T;
+        float* cq = d_qkv + r0 * 3 * C;
+        float* cg = d_grad + r0 * 3 * C;
+        what = "host-to-device copy";
+        if (upload_saved) {
+            e = upload_qkv(cq, q, k, v, ld_qkv, C, r0, rows, ctx->h2d);
+            if (e == cudaSuccess) e = copy_rows(d_o + r0 * C, C, o + r0 * ld_o, ld_o, C, rows, cudaMemcpyHostToDevice, ctx->h2d);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(d_lse + l0, lse + l0, sizeof(float) * static_cast<size_t>(bc) * H * T,
+                                    cudaMemcpyHostToDevice, ctx->h2d);
+        }
+        if (e == cudaSuccess)
+            e = copy_rows(d_do + r0 * C, C, dout + r0 * ld_o, ld_o, C, rows, cudaMemcpyHostToDevice, ctx->h2d);
+        if (e == cudaSuccess) e = hand_off(ctx->h2d, ctx->stream, ctx->events[2 * c]);
+        if (e != cudaSuccess) break;
+        what = "backward launch";
+        const kattn::BwdArgs a{cq, cq + C, cq + 2 * C, 3L * C, d_o + r0 * C, d_do + r0 * C, C, d_lse + l0,
+                               cg, cg + C, cg + 2 * C, 3L * C, d_dsum + l0, bc, T, H, d, scale, causal};
+        e = dispatch_bwd(ctx, a, ctx->stream, &launches);
+        if (e == cudaSuccess) e = hand_off(ctx->stream, ctx->d2h, ctx->events[2 * c + 1]);
+        if (e != cudaSuccess) break;
+        what = "device-to-host copy";
+        e = download_grads(dq, dk, dv, ld_d, cg, C, r0, rows, ctx->d2h);
+    }
+    const cudaError_t es = drain_host_streams(ctx);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    if (es != cudaSuccess) return cuda_fail(es, "cudaStreamSynchronize");
+    return ok_with_launches(launches);
+}
+
 }  // namespace
 
 extern "C" {
@@ -285,7 +463,11 @@ int kattn_create(int device, kattn_ctx** out) {
     ctx->device = device;
     ctx->num_sms = prop.multiProcessorCount;
     e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->d2h, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
+        if (ctx->stream) cudaStreamDestroy(ctx->stream);
+        if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
         delete ctx;
         return cuda_fail(e, "cudaStreamCreate");
     }
@@ -293,6 +475,8 @@ int kattn_create(int device, kattn_ctx** out) {
     if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int));
     if (e != cudaSuccess) {
         cudaStreamDestroy(ctx->stream);
+        cudaStreamDestroy(ctx->h2d);
+        cudaStreamDestroy(ctx->d2h);
         if (ctx->d_status) cudaFree(ctx->d_status);
         delete ctx;
         return cuda_fail(e, "status word");
@@ -303,6 +487,8 @@ int kattn_create(int device, kattn_ctx** out) {
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ctx->noalloc_ws), g_noalloc_ws);
     if (e != cudaSuccess) {
         cudaStreamDestroy(ctx->stream);
+        cudaStreamDestroy(ctx->h2d);
+        cudaStreamDestroy(ctx->d2h);
         cudaFree(ctx->d_status);
         delete ctx;
         return cuda_fail(e, "cudaGetSymbolAddress(workspace)");
@@ -322,11 +508,13 @@ int kattn_destroy(kattn_ctx* ctx) {
     int status = KATTN_OK;
     {
         DeviceScope scope(ctx->device);
-        if (ctx->stream) {
-            cudaError_t e = cudaStreamSynchronize(ctx->stream);
-            if (e != cudaSuccess) status = cuda_fail(e, "cudaStreamSynchronize");
-            cudaStreamDestroy(ctx->stream);
+        for (cudaStream_t* s : {&ctx->h2d, &ctx->stream, &ctx->d2h}) {
+            if (!*s) continue;
+            cudaError_t e = cudaStreamSynchronize(*s);
+            if (e != cudaSuccess && status == KATTN_OK) status = cuda_fail(e, "cudaStreamSynchronize");
+            cudaStreamDestroy(*s);
         }
+        for (cudaEvent_t ev : ctx->events) cudaEventDestroy(ev);
         if (ctx->arena) cudaFree(ctx->arena);
         if (ctx->d_status) cudaFree(ctx->d_status);
         if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
@@ -427,37 +615,16 @@ int kattn_fwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* 
     std::lock_guard<std::mutex> lock(ctx->host_mu);
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    KATTN_TRY(path_check(ctx, d));
     const int C = H * d;
     const long rows = static_cast<long>(B) * T;
     const size_t qkv_b = align256(sizeof(float) * rows * 3 * C);
     const size_t o_b = align256(sizeof(float) * rows * C);
     const size_t lse_b = align256(sizeof(float) * static_cast<size_t>(B) * H * T);
     KATTN_TRY(ensure_arena(ctx, qkv_b + o_b + lse_b));
-    float* dqkv = reinterpret_cast<float*>(ctx->arena);
-    float* d_o = reinterpret_cast<float*>(ctx->arena + qkv_b);
-    float* d_lse = reinterpret_cast<float*>(ctx->arena + qkv_b + o_b);
-    cudaStream_t s = ctx->stream;
-    cudaError_t e;
-    if (k == q + C && v == q + 2 * C && ld_qkv == 3L * C) {
-        e = cudaMemcpyAsync(dqkv, q, sizeof(float) * rows * 3 * C, cudaMemcpyHostToDevice, s);
-    } else {
-        e = copy_rows(dqkv, 3L * C, q, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
-        if (e == cudaSuccess) e = copy_rows(dqkv + C, 3L * C, k, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
-        if (e == cudaSuccess) e = copy_rows(dqkv + 2 * C, 3L * C, v, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
-    KATTN_TRY(path_check(ctx, d));
-    kattn::FwdArgs a{dqkv, dqkv + C, dqkv + 2 * C, 3L * C, d_o, C, d_lse, B, T, H, d, scale, causal};
-    int launches = 0;
-    e = dispatch_fwd(ctx, a, s, &launches);
-    if (e != cudaSuccess) return cuda_fail(e, "forward launch");
-    e = copy_rows(o, ld_o, d_o, C, C, rows, cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(lse, d_lse, sizeof(float) * static_cast<size_t>(B) * H * T, cudaMemcpyDeviceToHost, s);
-    if (e != cudaSuccess) return cuda_fail(e, "device-to-host copy");
-    e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-    return ok_with_launches(launches);
+    return fwd_host_run(ctx, reinterpret_cast<float*>(ctx->arena), reinterpret_cast<float*>(ctx->arena + qkv_b),
+                        reinterpret_cast<float*>(ctx->arena + qkv_b + o_b), q, k, v, ld_qkv, o, ld_o, lse, B, T, H, d,
+                        scale, causal);
 }
 
 int kattn_bwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* v, long ld_qkv, const float* o,
@@ -470,6 +637,7 @@ int kattn_bwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* 
     std::lock_guard<std::mutex> lock(ctx->host_mu);
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    KATTN_TRY(path_check(ctx, d));
     const int C = H * d;
     const long rows = static_cast<long>(B) * T;
     const size_t qkv_b = align256(sizeof(float) * rows * 3 * C);
@@ -483,37 +651,114 @@ int kattn_bwd_host(kattn_ctx* ctx, const float* q, const float* k, const float* 
     float* d_do = reinterpret_cast<float*>(base + 2 * qkv_b + row_b);
     float* d_lse = reinterpret_cast<float*>(base + 2 * qkv_b + 2 * row_b);
     float* d_dsum = reinterpret_cast<float*>(base + 2 * qkv_b + 2 * row_b + lse_b);
-    cudaStream_t s = ctx->stream;
-    cudaError_t e;
-    if (k == q + C && v == q + 2 * C && ld_qkv == 3L * C) {
-        e = cudaMemcpyAsync(d_qkv, q, sizeof(float) * rows * 3 * C, cudaMemcpyHostToDevice, s);
-    } else {
-        e = copy_rows(d_qkv, 3L * C, q, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
-        if (e == cudaSuccess) e = copy_rows(d_qkv + C, 3L * C, k, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
-        if (e == cudaSuccess) e = copy_rows(d_qkv + 2 * C, 3L * C, v, ld_qkv, C, rows, cudaMemcpyHostToDevice, s);
+    return bwd_host_run(ctx, d_qkv, d_o, d_lse, true, q, k, v, ld_qkv, o, lse, dout, ld_o, dq, dk, dv, ld_dqkv, d_do,
+                        d_grad, d_dsum, B, T, H, d, scale, causal);
+}
+
+int kattn_saved_create(kattn_ctx* ctx, kattn_saved** out) {
+    if (!out) return fail(KATTN_ERR_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    kattn_saved* s = new (std::nothrow) kattn_saved();
+    if (!s) return fail(KATTN_ERR_OUT_OF_MEMORY, "host allocation of the saved state failed");
+    s->ctx = ctx;
+    *out = s;
+    return KATTN_OK;
+}
+
+int kattn_saved_destroy(kattn_saved* saved) {
+    if (!saved) return KATTN_OK;
+    int status = KATTN_OK;
+    if (saved->buf) {
+        kattn_ctx* ctx = saved->ctx;
+        std::lock_guard<std::mutex> lock(ctx->host_mu);
+        DeviceScope scope(ctx->device);
+        const cudaError_t e = cudaFree(saved->buf);
+        if (e != cudaSuccess) status = cuda_fail(e, "cudaFree(saved state)");
     }
-    if (e == cudaSuccess) e = copy_rows(d_o, C, o, ld_o, C, rows, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = copy_rows(d_do, C, dout, ld_o, C, rows, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(d_lse, lse, sizeof(float) * static_cast<size_t>(B) * H * T, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
+    delete saved;
+    return status;
+}
+
+int kattn_fwd_host_save(kattn_ctx* ctx, kattn_saved* saved, const float* q, const float* k, const float* v,
+                        long ld_qkv, float* o, long ld_o, float* lse, int B, int T, int H, int d, float scale,
+                        int causal) {
+    g_last_launches = 0;
+    if (!saved) return fail(KATTN_ERR_INVALID_ARGUMENT, "saved is NULL");
+    if (saved->ctx != ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "saved state belongs to another context");
+    KATTN_TRY(fwd_checks(ctx, q, k, v, ld_qkv, o, ld_o, lse, B, T, H, d, scale, causal, false));
+    std::lock_guard<std::mutex> lock(ctx->host_mu);
+    saved->valid = false;
+    saved->B = B;
+    saved->T = T;
+    saved->H = H;
+    saved->d = d;
+    saved->scale = scale;
+    saved->causal = causal;
+    if (B == 0 || T == 0) {
+        saved->valid = true;
+        return ok_with_launches(0);
+    }
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
     KATTN_TRY(path_check(ctx, d));
-    kattn::BwdArgs a{d_qkv, d_qkv + C, d_qkv + 2 * C, 3L * C, d_o, d_do, C, d_lse,
-                     d_grad, d_grad + C, d_grad + 2 * C, 3L * C, d_dsum, B, T, H, d, scale, causal};
-    int launches = 0;
-    e = dispatch_bwd(ctx, a, s, &launches);
-    if (e != cudaSuccess) return cuda_fail(e, "backward launch");
-    if (dk == dq + C && dv == dq + 2 * C && ld_dqkv == 3L * C) {
-        e = cudaMemcpyAsync(dq, d_grad, sizeof(float) * rows * 3 * C, cudaMemcpyDeviceToHost, s);
-    } else {
-        e = copy_rows(dq, ld_dqkv, d_grad, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
-        if (e == cudaSuccess) e = copy_rows(dk, ld_dqkv, d_grad + C, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
-        if (e == cudaSuccess) e = copy_rows(dv, ld_dqkv, d_grad + 2 * C, 3L * C, C, rows, cudaMemcpyDeviceToHost, s);
+    const int C = H * d;
+    const long rows = static_cast<long>(B) * T;
+    const size_t qkv_b = align256(sizeof(float) * rows * 3 * C);
+    const size_t o_b = align256(sizeof(float) * rows * C);
+    const size_t lse_b = align256(sizeof(float) * static_cast<size_t>(B) * H * T);
+    if (saved->bytes < qkv_b + o_b + lse_b) {
+        if (saved->buf) {
+            const cudaError_t e = cudaFree(saved->buf);
+            saved->buf = nullptr;
+            saved->bytes = 0;
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFree(saved state)");
+        }
+        const cudaError_t e = cudaMalloc(&saved->buf, qkv_b + o_b + lse_b);
+        if (e != cudaSuccess) {
+            saved->buf = nullptr;
+            return cuda_fail(e, "cudaMalloc(saved state)");
+        }
+        saved->bytes = qkv_b + o_b + lse_b;
     }
-    if (e != cudaSuccess) return cuda_fail(e, "device-to-host copy");
-    e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-    return ok_with_launches(launches);
+    saved->qkv = reinterpret_cast<float*>(saved->buf);
+    saved->o = reinterpret_cast<float*>(saved->buf + qkv_b);
+    saved->lse = reinterpret_cast<float*>(saved->buf + qkv_b + o_b);
+    const int st = fwd_host_run(ctx, saved->qkv, saved->o, saved->lse, q, k, v, ld_qkv, o, ld_o, lse, B, T, H, d,
+                                scale, causal);
+    saved->valid = st == KATTN_OK;
+    return st;
+}
+
+int kattn_bwd_host_saved(kattn_ctx* ctx, const kattn_saved* saved, const float* dout, long ld_o, float* dq,
+                         float* dk, float* dv, long ld_dqkv) {
+    g_last_launches = 0;
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    if (!saved) return fail(KATTN_ERR_INVALID_ARGUMENT, "saved is NULL");
+    if (saved->ctx != ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "saved state belongs to another context");
+    if (!saved->valid) return fail(KATTN_ERR_INVALID_ARGUMENT, "saved state holds no completed forward");
+    const int B = saved->B, T = saved->T, H = saved->H, d = saved->d;
+    if (B == 0 || T == 0) return ok_with_launches(0);
+    const int C = H * d;
+    KATTN_TRY(check_tensor("dout", dout, ld_o, C, false));
+    KATTN_TRY(check_tensor("dq", dq, ld_dqkv, C, false));
+    KATTN_TRY(check_tensor("dk", dk, ld_dqkv, C, false));
+    KATTN_TRY(check_tensor("dv", dv, ld_dqkv, C, false));
+    std::lock_guard<std::mutex> lock(ctx->host_mu);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    KATTN_TRY(path_check(ctx, d));
+    const long rows = static_cast<long>(B) * T;
+    const size_t qkv_b = align256(sizeof(float) * rows * 3 * C);
+    const size_t row_b = align256(sizeof(float) * rows * C);
+    const size_t lse_b = align256(sizeof(float) * static_cast<size_t>(B) * H * T);
+    KATTN_TRY(ensure_arena(ctx, qkv_b + row_b + lse_b));
+    float* d_grad = reinterpret_cast<float*>(ctx->arena);
+    float* d_do = reinterpret_cast<float*>(ctx->arena + qkv_b);
+    float* d_dsum = reinterpret_cast<float*>(ctx->arena + qkv_b + row_b);
+    return bwd_host_run(ctx, saved->qkv, saved->o, saved->lse, false, nullptr, nullptr, nullptr, 0, nullptr, nullptr,
+                        dout, ld_o, dq, dk, dv, ld_dqkv, d_do, d_grad, d_dsum, B, T, H, d, saved->scale,
+                        saved->causal);
 }
 
 int kattn_linear_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, const float* b, float* y, long ld_y,

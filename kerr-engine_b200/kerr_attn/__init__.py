@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "kattn_fwd", "kattn_bwd", "kattn_fwd_host", "kattn_bwd_host", "kattn_last_launch_count",
     "kattn_bwd_noalloc",
     "kattn_linear_fwd", "kattn_linear_bwd_dx", "kattn_linear_bwd_dw",
+    "kattn_saved_create", "kattn_saved_destroy", "kattn_fwd_host_save", "kattn_bwd_host_saved",
 )
 
 # Largest B*H*T that kattn_bwd_noalloc accepts (KATTN_NOALLOC_MAX_ROWS).
@@ -99,6 +100,14 @@ def lib():
     L.kattn_fwd_host.restype = _i
     L.kattn_bwd_host.argtypes = bwd_args
     L.kattn_bwd_host.restype = _i
+    L.kattn_saved_create.argtypes = [_p, ctypes.POINTER(_p)]
+    L.kattn_saved_create.restype = _i
+    L.kattn_saved_destroy.argtypes = [_p]
+    L.kattn_saved_destroy.restype = _i
+    L.kattn_fwd_host_save.argtypes = [_p, _p] + fwd_args[1:]
+    L.kattn_fwd_host_save.restype = _i
+    L.kattn_bwd_host_saved.argtypes = [_p, _p, _p, _l, _p, _p, _p, _l]
+    L.kattn_bwd_host_saved.restype = _i
     L.kattn_linear_fwd.argtypes = [_p, _p, _l, _p, _p, _p, _l, _i, _i, _i, _p]
     L.kattn_linear_fwd.restype = _i
     L.kattn_linear_bwd_dx.argtypes = [_p, _p, _l, _p, _p, _l, _i, _i, _i, _p]
@@ -289,6 +298,68 @@ def bwd_host(ctx: Context, q, k, v, o, dout, lse, dq, dk, dv, n_head: int, causa
     st = lib().kattn_bwd_host(ctx.handle, pq, pk, pv, ld, po, pdo, ldo, _vec(lse, "lse"), pdq, pdk, pdv, ldg,
                               B, T, n_head, d, sc, int(causal))
     _check(st, "kattn_bwd_host")
+    return last_launch_count()
+
+
+class Saved:
+    """Device-resident state of one forward (the reference's AttnCache,
+    src/pipeline.rs:157-164): q/k/v, o and lse, for :func:`bwd_host_saved`."""
+
+    def __init__(self, ctx: Context):
+        h = ctypes.c_void_p()
+        _check(lib().kattn_saved_create(ctx.handle, ctypes.byref(h)), "kattn_saved_create")
+        self._h = h
+        self.ctx = ctx
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise RuntimeError("saved state is closed")
+        return self._h
+
+    def close(self):
+        if self._h is not None:
+            st = lib().kattn_saved_destroy(self._h)
+            self._h = None
+            _check(st, "kattn_saved_destroy")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def fwd_host_save(ctx: Context, saved: Saved, q, k, v, o, lse, n_head: int, causal: bool = True,
+                  scale: float | None = None) -> int:
+    """fwd_host, keeping q/k/v, o and lse on the device in `saved`."""
+    B, T, C = q.shape
+    d = C // n_head
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    pq, ld = _rows(q, "q")
+    pk, _ = _rows(k, "k")
+    pv, _ = _rows(v, "v")
+    po, ldo = _rows(o, "o")
+    st = lib().kattn_fwd_host_save(ctx.handle, saved.handle, pq, pk, pv, ld, po, ldo, _vec(lse, "lse"), B, T,
+                                   n_head, d, sc, int(causal))
+    _check(st, "kattn_fwd_host_save")
+    return last_launch_count()
+
+
+def bwd_host_saved(ctx: Context, saved: Saved, dout, dq, dk, dv) -> int:
+    """Backward of the forward held in `saved`, host tensors dout in and dq/dk/dv out."""
+    pdo, ldo = _rows(dout, "dout")
+    pdq, ldg = _rows(dq, "dq")
+    pdk, _ = _rows(dk, "dk")
+    pdv, _ = _rows(dv, "dv")
+    st = lib().kattn_bwd_host_saved(ctx.handle, saved.handle, pdo, ldo, pdq, pdk, pdv, ldg)
+    _check(st, "kattn_bwd_host_saved")
     return last_launch_count()
 
 

@@ -129,3 +129,31 @@ def test_create_without_device_fails_cleanly(L):
     with pytest.raises(kerr_attn.KattnError) as e:
         kerr_attn.Context(0)
     assert e.value.status == kerr_attn.KATTN_ERR_DEVICE
+
+
+def test_saved_state_validation(L):
+    # The saved-state calls reject bad arguments and an empty state before
+    # touching a device; creating and destroying an unused state needs none.
+    ctx, other = _fake_ctx(), ctypes.c_void_p(0x20)  # two distinct handles; neither is dereferenced
+    P = ctypes.c_void_p
+    out = P()
+    assert L.kattn_saved_create(None, ctypes.byref(out)) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert L.kattn_saved_create(ctx, None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert L.kattn_saved_create(ctx, ctypes.byref(out)) == kerr_attn.KATTN_OK and out.value
+    h = P(0x10000)
+    # No forward has run into it yet.
+    assert L.kattn_bwd_host_saved(ctx, out, h, 64, h, h, h, 192) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert "no completed forward" in kerr_attn.last_error()
+    assert L.kattn_bwd_host_saved(ctx, None, h, 64, h, h, h, 192) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert L.kattn_bwd_host_saved(None, out, h, 64, h, h, h, 192) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    # A state belongs to the context that created it.
+    assert L.kattn_bwd_host_saved(other, out, h, 64, h, h, h, 192) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert L.kattn_fwd_host_save(other, out, h, h, h, 192, h, 64, h, 2, 8, 1, 64, 0.125, 1) == \
+        kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert L.kattn_fwd_host_save(ctx, None, h, h, h, 192, h, 64, h, 2, 8, 1, 64, 0.125, 1) == \
+        kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    # The forward's own argument checks apply (head_dim 48 is unsupported).
+    assert L.kattn_fwd_host_save(ctx, out, h, h, h, 144, h, 48, h, 2, 8, 1, 48, 0.125, 1) == \
+        kerr_attn.KATTN_ERR_UNSUPPORTED
+    assert L.kattn_saved_destroy(out) == kerr_attn.KATTN_OK
+    assert L.kattn_saved_destroy(None) == kerr_attn.KATTN_OK

@@ -207,6 +207,59 @@ def test_host_entry_points_match_device(ctx, oracle_lib):
     assert torch.equal(o2, o) and torch.equal(lse2, lse)
 
 
+def _host_fwd_bwd(ctx, qkv, dout, H, saved=None, split_grads=False):
+    """Forward + backward through the host-buffer calls (fwd_host / bwd_host,
+    or fwd_host_save / bwd_host_saved when `saved` is given)."""
+    B, T, C3 = qkv.shape
+    C = C3 // 3
+    qkv_t = torch.from_numpy(qkv).pin_memory()
+    q, k, v = kerr_attn.split_qkv(qkv_t, C)
+    o = torch.empty(B, T, C).pin_memory()
+    lse = torch.empty(B, H, T).pin_memory()
+    dout_t = torch.from_numpy(dout).pin_memory()
+    if split_grads:
+        dq, dk, dv = (torch.empty(B, T, C).pin_memory() for _ in range(3))
+    else:
+        dq, dk, dv = kerr_attn.split_qkv(torch.empty(B, T, 3 * C).pin_memory(), C)
+    if saved is None:
+        kerr_attn.fwd_host(ctx, q, k, v, o, lse, H)
+        kerr_attn.bwd_host(ctx, q, k, v, o, dout_t, lse, dq, dk, dv, H)
+    else:
+        kerr_attn.fwd_host_save(ctx, saved, q, k, v, o, lse, H)
+        kerr_attn.bwd_host_saved(ctx, saved, dout_t, dq, dk, dv)
+    return (o.numpy(), lse.numpy(), dq.numpy(), dk.numpy(), dv.numpy())
+
+
+def test_host_paths_pipelined_and_saved(ctx):
+    # At the 768-dim shape with B=10 the host calls split the batch into
+    # chunks (4/4/2 sequences for the forward and the saved-state backward,
+    # five of 2 for the plain backward), overlapping each chunk's copies with
+    # its neighbours' kernels.  Results must equal the device-pointer path's: the
+    # forward bit for bit, the gradients up to dQ's run-dependent summation
+    # order.  The saved-state pair (kattn_fwd_host_save / kattn_bwd_host_saved,
+    # the reference's AttnCache) must give the same results as the plain pair.
+    B, T, H, d = 10, 256, 12, 64
+    qkv, dout = make_inputs(B, T, H, d, seed=77)
+    ref = gpu_fwd_bwd(ctx, qkv, dout, H)
+
+    def check(got):
+        assert np.array_equal(got[0], ref[0]) and np.array_equal(got[1], ref[1])
+        for g, r in zip(got[2:], ref[2:]):
+            assert rel_err(g, r) < 1e-6
+
+    check(_host_fwd_bwd(ctx, qkv, dout, H))
+    with kerr_attn.Saved(ctx) as saved:
+        check(_host_fwd_bwd(ctx, qkv, dout, H, saved=saved))
+        # Reused for a smaller forward; separate dq / dk / dv host arrays take
+        # the strided download path.
+        qkv2, dout2 = make_inputs(3, 100, H, d, seed=78)
+        ref2 = gpu_fwd_bwd(ctx, qkv2, dout2, H)
+        got2 = _host_fwd_bwd(ctx, qkv2, dout2, H, saved=saved, split_grads=True)
+        assert np.array_equal(got2[0], ref2[0]) and np.array_equal(got2[1], ref2[1])
+        for g, r in zip(got2[2:], ref2[2:]):
+            assert rel_err(g, r) < 1e-6
+
+
 def test_side_stream_and_reuse(ctx, oracle_lib):
     qkv, dout = make_inputs(2, 128, 2, 64, seed=8)
     s = torch.cuda.Stream()
