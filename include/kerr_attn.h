@@ -214,6 +214,29 @@ int kattn_linear_bwd_dx(kattn_ctx* ctx, const float* dy, long ld_dy, const float
 int kattn_linear_bwd_dw(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
                         float* dw, float* db, int M, int N, int K, int accumulate, void* stream);
 
+/* ---- LayerNorm LN1 / LN2 (rows of n_embd) ----------------------------------
+ * Replace layer_norm / layer_norm_batch (src/backend.rs:103, :140-142, CPU
+ * :258-267) and layer_norm_backward / layer_norm_backward_batch
+ * (src/backend.rs:184, :195-206, CPU src/backward.rs:93-128), called at
+ * src/pipeline.rs:236, :250, :678, :743.  eps = 1e-5; the variance is the
+ * mean of squared deviations, as in the reference.  Device pointers, rows
+ * 16-byte aligned, N and every row stride a multiple of 4 floats,
+ * N <= KATTN_LN_MAX_N.  Nothing synchronises the host. */
+#define KATTN_LN_MAX_N 1536
+
+/* y[m][:] = (x[m][:] - mean) / sqrt(var + eps) * w + b for m < M rows of N. */
+int kattn_layernorm_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, const float* b,
+                        float* y, long ld_y, int M, int N, void* stream);
+
+/* dx from dy and x (statistics recomputed from x, as the reference does);
+ * dw[n] (+)= sum_m dy[m][n] * xhat[m][n] and db[n] (+)= sum_m dy[m][n] when
+ * accumulate != 0 (the += of src/pipeline.rs:747-750), written otherwise.
+ * dw or db may be NULL.  The column sums are formed in a fixed order (no
+ * atomics): the same inputs give the same bits. */
+int kattn_layernorm_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
+                        const float* w, float* dx, long ld_dx, float* dw, float* db,
+                        int M, int N, int accumulate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

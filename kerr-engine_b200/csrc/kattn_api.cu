@@ -826,5 +826,45 @@ int kattn_linear_bwd_dw(kattn_ctx* ctx, const float* dy, long ld_dy, const float
     return proj_result(st, launches);
 }
 
+int kattn_layernorm_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, const float* b, float* y,
+                        long ld_y, int M, int N, void* stream) {
+    g_last_launches = 0;
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    if (M < 0 || N < 0) return fail(KATTN_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d)", M, N);
+    if (N > KATTN_LN_MAX_N) return fail(KATTN_ERR_UNSUPPORTED, "N=%d exceeds KATTN_LN_MAX_N=%d", N, KATTN_LN_MAX_N);
+    KATTN_TRY(check_matrix("x", x, ld_x, M, N));
+    KATTN_TRY(check_matrix("y", y, ld_y, M, N));
+    KATTN_TRY(check_matrix("w", w, N, 1, N));
+    KATTN_TRY(check_matrix("b", b, N, 1, N));
+    if (M == 0 || N == 0) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    int launches = 0;
+    const kattn::ProjStatus st =
+        kattn::ln_forward(static_cast<cudaStream_t>(stream), ctx->num_sms, x, ld_x, w, b, y, ld_y, M, N, &launches);
+    return proj_result(st, launches);
+}
+
+int kattn_layernorm_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
+                        float* dx, long ld_dx, float* dw, float* db, int M, int N, int accumulate, void* stream) {
+    g_last_launches = 0;
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    if (M < 0 || N < 0) return fail(KATTN_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d)", M, N);
+    if (N > KATTN_LN_MAX_N) return fail(KATTN_ERR_UNSUPPORTED, "N=%d exceeds KATTN_LN_MAX_N=%d", N, KATTN_LN_MAX_N);
+    KATTN_TRY(check_matrix("dy", dy, ld_dy, M, N));
+    KATTN_TRY(check_matrix("x", x, ld_x, M, N));
+    KATTN_TRY(check_matrix("dx", dx, ld_dx, M, N));
+    KATTN_TRY(check_matrix("w", w, N, 1, N));
+    if (dw) KATTN_TRY(check_matrix("dw", dw, N, 1, N));
+    if (db) KATTN_TRY(check_matrix("db", db, N, 1, N));
+    if (N == 0 || (M == 0 && accumulate)) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    int launches = 0;
+    const kattn::ProjStatus st = kattn::ln_backward(static_cast<cudaStream_t>(stream), dy, ld_dy, x, ld_x, w, dx,
+                                                    ld_dx, dw, db, M, N, accumulate, &launches);
+    return proj_result(st, launches);
+}
+
 #pragma GCC visibility pop
 }  // extern "C"

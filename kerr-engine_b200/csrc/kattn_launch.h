@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include "kerr_attn.h"
+
 namespace kattn {
 
 // Launches `kernel` on `stream` with programmatic stream serialisation, so it
@@ -90,5 +92,16 @@ ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t stream, cons
 ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t stream, const float* dy, long ld_dy,
                             const float* x, long ld_x, float* dw, float* db, int M, int N, int K, int accumulate,
                             int* launches, int* gemms);
+
+// LayerNorm over rows of n floats (kln.cu), eps 1e-5.  n a multiple of 4,
+// at most LN_MAX_N; rows 16-byte aligned.  w, b, dw, db have n floats.
+// Backward: dx written; dw / db (either may be NULL) added to when
+// `accumulate`, written otherwise.  *launches counts the kernels enqueued.
+constexpr int LN_MAX_N = KATTN_LN_MAX_N;
+bool ln_supported(int n);
+ProjStatus ln_forward(cudaStream_t s, int num_sms, const float* x, long ld_x, const float* w, const float* b, float* y,
+                      long ld_y, int M, int n, int* launches);
+ProjStatus ln_backward(cudaStream_t s, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
+                       float* dx, long ld_dx, float* dw, float* db, int M, int n, int accumulate, int* launches);
 
 }  // namespace kattn

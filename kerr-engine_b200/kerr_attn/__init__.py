@@ -42,7 +42,11 @@ EXPORTED_SYMBOLS = (
     "kattn_bwd_noalloc",
     "kattn_linear_fwd", "kattn_linear_bwd_dx", "kattn_linear_bwd_dw",
     "kattn_saved_create", "kattn_saved_destroy", "kattn_fwd_host_save", "kattn_bwd_host_saved",
+    "kattn_layernorm_fwd", "kattn_layernorm_bwd",
 )
+
+# Widest row kattn_layernorm_fwd / _bwd accept (KATTN_LN_MAX_N).
+LN_MAX_N = 1536
 
 # Largest B*H*T that kattn_bwd_noalloc accepts (KATTN_NOALLOC_MAX_ROWS).
 NOALLOC_MAX_ROWS = 1 << 20
@@ -108,6 +112,10 @@ def lib():
     L.kattn_fwd_host_save.restype = _i
     L.kattn_bwd_host_saved.argtypes = [_p, _p, _p, _l, _p, _p, _p, _l]
     L.kattn_bwd_host_saved.restype = _i
+    L.kattn_layernorm_fwd.argtypes = [_p, _p, _l, _p, _p, _p, _l, _i, _i, _p]
+    L.kattn_layernorm_fwd.restype = _i
+    L.kattn_layernorm_bwd.argtypes = [_p, _p, _l, _p, _l, _p, _p, _l, _p, _p, _i, _i, _i, _p]
+    L.kattn_layernorm_bwd.restype = _i
     L.kattn_linear_fwd.argtypes = [_p, _p, _l, _p, _p, _p, _l, _i, _i, _i, _p]
     L.kattn_linear_fwd.restype = _i
     L.kattn_linear_bwd_dx.argtypes = [_p, _p, _l, _p, _p, _l, _i, _i, _i, _p]
@@ -430,3 +438,33 @@ def linear_bwd_dw(ctx: Context, dy, x, dw, db, accumulate: bool = True, stream=N
                                    M, N, K, int(accumulate), _stream_ptr(stream, dy.device))
     _check(st, "kattn_linear_bwd_dw")
     return last_launch_count()
+
+
+# ---------------------------------------------------------------- layer norm
+
+def layernorm_fwd(ctx: Context, x, w, b, y, stream=None) -> int:
+    """y = LayerNorm(x) w + b over the last dimension (eps 1e-5).  Returns kernels launched."""
+    px, ldx, M, N = _mat(x, "x")
+    py, ldy, My, Ny = _mat(y, "y")
+    if (My, Ny) != (M, N) or tuple(w.shape) != (N,) or tuple(b.shape) != (N,):
+        raise ValueError("shapes: x [.., N], y like x, w [N], b [N]")
+    st = lib().kattn_layernorm_fwd(ctx.handle, px, ldx, _vec(w, "w"), _vec(b, "b"), py, ldy, M, N,
+                                   _stream_ptr(stream, x.device))
+    _check(st, "kattn_layernorm_fwd")
+    return last_launch_count()
+
+
+def layernorm_bwd(ctx: Context, dy, x, w, dx, dw, db, accumulate: bool = True, stream=None) -> int:
+    """dx of LayerNorm; dw / db (either may be None) receive the column sums
+    (added when `accumulate`).  Returns kernels launched."""
+    pdy, lddy, M, N = _mat(dy, "dy")
+    px, ldx, Mx, Nx = _mat(x, "x")
+    pdx, lddx, Md, Nd = _mat(dx, "dx")
+    if (Mx, Nx) != (M, N) or (Md, Nd) != (M, N) or tuple(w.shape) != (N,):
+        raise ValueError("shapes: dy, x, dx [.., N], w [N]")
+    st = lib().kattn_layernorm_bwd(ctx.handle, pdy, lddy, px, ldx, _vec(w, "w"), pdx, lddx,
+                                   None if dw is None else _vec(dw, "dw"), None if db is None else _vec(db, "db"),
+                                   M, N, int(accumulate), _stream_ptr(stream, dy.device))
+    _check(st, "kattn_layernorm_bwd")
+    return last_launch_count()
+

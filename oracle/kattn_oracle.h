@@ -62,6 +62,14 @@ void kattn_oracle_backward_batch(int B, int T, int C, int H,
 /* Threads the batched drivers use for nthreads <= 0. */
 int kattn_oracle_default_threads(int B);
 
+/* LayerNorm LN1 / LN2 (kln_oracle.c): rows of N floats, eps 1e-5.  The
+ * backward writes dx and sets (accumulate == 0) or adds to dw / db (either
+ * may be NULL) the column sums over the M rows. */
+void kln_oracle_forward(int M, int N, const float* x, long ld_x, const float* w, const float* b, float* y,
+                        long ld_y);
+void kln_oracle_backward(int M, int N, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
+                         float* dx, long ld_dx, float* dw, float* db, int accumulate);
+
 /* Linear layers of the attention projections (kproj_oracle.c): rows are
  * positions, weights [N out][K in] row-major.
  *   forward    : y[m][n] = b[n] + sum_k w[n][k] x[m][k]   (b may be NULL)

@@ -58,6 +58,11 @@ def lib():
         L.kproj_oracle_backward_dw.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f,
                                                ctypes.c_long, _f, _f, ctypes.c_int]
         L.kproj_oracle_backward_dw.restype = None
+        L.kln_oracle_forward.argtypes = [ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f, _f, _f, ctypes.c_long]
+        L.kln_oracle_forward.restype = None
+        L.kln_oracle_backward.argtypes = [ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f, ctypes.c_long, _f, _f,
+                                          ctypes.c_long, _f, _f, ctypes.c_int]
+        L.kln_oracle_backward.restype = None
         _lib = L
     return _lib
 
@@ -156,3 +161,29 @@ def linear_backward_dw(dy, x, threads=0):
     db = np.zeros(N, np.float32)
     lib().kproj_oracle_backward_dw(M, N, K, _ptr(dy), N, _ptr(x), K, _ptr(dw), _ptr(db), threads)
     return dw, db
+
+
+def layernorm_forward(x, w, b):
+    """LayerNorm of each row of x [M, N] (src/backend.rs:258-267)."""
+    x = np.ascontiguousarray(x, np.float32)
+    M, N = x.shape
+    y = np.empty((M, N), np.float32)
+    lib().kln_oracle_forward(M, N, _ptr(x), N, _ptr(np.ascontiguousarray(w, np.float32)),
+                             _ptr(np.ascontiguousarray(b, np.float32)), _ptr(y), N)
+    return y
+
+
+def layernorm_backward(dy, x, w, dw=None, db=None):
+    """(dx, dw, db) of LayerNorm (src/backward.rs:93-128, src/backend.rs:195-206);
+    dw / db given: the column sums are added to copies of them."""
+    dy = np.ascontiguousarray(dy, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    M, N = x.shape
+    dx = np.empty((M, N), np.float32)
+    acc = dw is not None
+    dw_o = np.array(dw, np.float32) if acc else np.empty(N, np.float32)
+    db_o = np.array(db, np.float32) if db is not None else np.empty(N, np.float32)
+    lib().kln_oracle_backward(M, N, _ptr(dy), N, _ptr(x), N, _ptr(np.ascontiguousarray(w, np.float32)), _ptr(dx), N,
+                              _ptr(dw_o), _ptr(db_o), int(acc))
+    return dx, dw_o, db_o
+

@@ -157,3 +157,31 @@ def test_saved_state_validation(L):
         kerr_attn.KATTN_ERR_UNSUPPORTED
     assert L.kattn_saved_destroy(out) == kerr_attn.KATTN_OK
     assert L.kattn_saved_destroy(None) == kerr_attn.KATTN_OK
+
+
+def test_layernorm_validation(L):
+    # The LayerNorm entry points reject bad arguments before touching a device.
+    ctx = _fake_ctx()
+    P = ctypes.c_void_p
+    x, w, b, y = P(0x10000), P(0x20000), P(0x30000), P(0x40000)
+
+    def fwd(c=ctx, x=x, ldx=768, w=w, b=b, y=y, ldy=768, M=64, N=768):
+        return L.kattn_layernorm_fwd(c, x, ldx, w, b, y, ldy, M, N, None)
+
+    assert fwd(c=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(M=-1) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(N=kerr_attn.LN_MAX_N + 4, ldx=4096, ldy=4096) == kerr_attn.KATTN_ERR_UNSUPPORTED
+    assert fwd(x=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(ldx=764) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT      # ld < N
+    assert fwd(x=P(0x10008)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert fwd(N=766, ldx=768, ldy=768) == kerr_attn.KATTN_ERR_MISALIGNED  # width not a multiple of 4
+    assert fwd(w=P(0x20004)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert fwd(b=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(M=0) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+
+    def bwd(dw=P(0x50000), db=P(0x60000), M=64, acc=1, dx=P(0x70000)):
+        return L.kattn_layernorm_bwd(ctx, y, 768, x, 768, w, dx, 768, dw, db, M, 768, acc, None)
+
+    assert bwd(dx=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert bwd(dw=P(0x50004)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert bwd(M=0, acc=1) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0

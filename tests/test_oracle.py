@@ -155,3 +155,29 @@ def test_linear_oracle_against_float64(M, N, K):
     dw, db = oracle.linear_backward_dw(dy, x)
     assert np.abs(dw - dy64.T @ x64).max() < 1e-5 * max(1.0, np.abs(dw).max()) * np.sqrt(M)
     assert np.abs(db - dy64.sum(0)).max() < 1e-5 * max(1.0, np.abs(db).max()) * np.sqrt(M)
+
+
+def test_layernorm_oracle_against_float64():
+    # The LayerNorm restatement (src/backend.rs:258-267, src/backward.rs:93-128)
+    # against a float64 evaluation of the same formulas, rows of 768 and 100.
+    from oracle import oracle
+
+    rng = np.random.default_rng(5)
+    for M, N in ((37, 768), (9, 100)):
+        x = (rng.standard_normal((M, N)) * 2 + 0.5).astype(np.float32)
+        w = rng.standard_normal(N).astype(np.float32)
+        b = rng.standard_normal(N).astype(np.float32)
+        dy = rng.standard_normal((M, N)).astype(np.float32)
+        xd = x.astype(np.float64)
+        mean = xd.mean(1, keepdims=True)
+        rstd = 1.0 / np.sqrt(((xd - mean) ** 2).mean(1, keepdims=True) + 1e-5)
+        xh = (xd - mean) * rstd
+        y = oracle.layernorm_forward(x, w, b)
+        assert rel_err(y, xh * w + b) < 1e-6
+        g = dy * w
+        dx_ref = rstd / N * (N * g - g.sum(1, keepdims=True) - xh * (g * xh).sum(1, keepdims=True))
+        dw0 = rng.standard_normal(N).astype(np.float32)
+        dx, dw, db = oracle.layernorm_backward(dy, x, w, dw=dw0, db=dw0)
+        assert rel_err(dx, dx_ref) < 1e-6
+        assert rel_err(dw, dw0 + (dy * xh).sum(0)) < 1e-5
+        assert rel_err(db, dw0 + dy.sum(0)) < 1e-5
