@@ -417,14 +417,14 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-LAYER_METRIC = ("attention layer (c_attn + causal attention + c_proj) fwd+bwd tokens/s per GPU at 768-dim T=256, "
-                "projection gradients all-reduced over the ranks")
+LAYER_METRIC = ("attention sublayer (ln_1 + c_attn + causal attention + c_proj) fwd+bwd tokens/s per GPU at "
+                "768-dim T=256, sublayer gradients all-reduced over the ranks")
 
 
 def layer_cpu_sample(n_seq: int, T: int, H: int, d: int, threads: int, seed: int = 11):
-    """One block of the layer through the oracle (linear layers + attention,
-    forward and backward) over n_seq sequences, every call on `threads`
-    host threads."""
+    """One block of the sublayer through the oracle (LayerNorm, linear layers,
+    attention; forward and backward) over n_seq sequences, the linear and
+    attention calls on `threads` host threads."""
     import numpy as np
 
     from oracle import oracle
@@ -432,13 +432,15 @@ def layer_cpu_sample(n_seq: int, T: int, H: int, d: int, threads: int, seed: int
     C = H * d
     rng = np.random.default_rng(seed)
     M = n_seq * T
-    x = rng.standard_normal((M, C)).astype(np.float32)
+    h = rng.standard_normal((M, C)).astype(np.float32)
+    lnw, lnb = np.ones(C, np.float32), np.zeros(C, np.float32)
     wa = rng.uniform(-1, 1, (3 * C, C)).astype(np.float32) / np.sqrt(C)
     wp = rng.uniform(-1, 1, (C, C)).astype(np.float32) / np.sqrt(C)
     ba = np.zeros(3 * C, np.float32)
     bp = np.zeros(C, np.float32)
     dy = rng.standard_normal((M, C)).astype(np.float32)
     t0 = time.perf_counter()
+    x = oracle.layernorm_forward(h, lnw, lnb)
     qkv = oracle.linear_forward(x, wa, ba, threads=threads).reshape(n_seq, T, 3 * C)
     q, k, v = qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
     o, att, _ = oracle.forward(q, k, v, H, threads=threads)
@@ -447,17 +449,19 @@ def layer_cpu_sample(n_seq: int, T: int, H: int, d: int, threads: int, seed: int
     oracle.linear_backward_dw(dy, o.reshape(M, C), threads=threads)
     dq, dk, dv = oracle.backward(d_o.reshape(n_seq, T, C), q, k, v, att, H, threads=threads)
     dqkv = np.concatenate([dq, dk, dv], axis=-1).reshape(M, 3 * C)
-    oracle.linear_backward_dx(dqkv, wa, threads=threads)
+    dx = oracle.linear_backward_dx(dqkv, wa, threads=threads)
     oracle.linear_backward_dw(dqkv, x, threads=threads)
+    oracle.layernorm_backward(dx, h, lnw)
     return time.perf_counter() - t0
 
 
 def run_layer(args):
-    """The whole attention layer of the 768-dim model per block: c_attn,
-    attention, c_proj forward; their backward in reverse block order; each
-    block's projection gradients all-reduced across the ranks (NCCL) as soon as
-    its backward is enqueued, overlapping the blocks below (the data-parallel
-    exchange of the step)."""
+    """The whole attention sublayer of the 768-dim model per block
+    (src/pipeline.rs:236-249): LN1, c_attn, attention, c_proj forward; their
+    backward in reverse block order; each block's parameter gradients (c_attn,
+    c_proj, ln_1) all-reduced across the ranks (NCCL) as soon as its backward
+    is enqueued, overlapping the blocks below (the data-parallel exchange of
+    the step)."""
     import torch
     import torch.distributed as dist
 
@@ -483,8 +487,11 @@ def run_layer(args):
     g.manual_seed(2000 + rank)
     blocks = []
     for _ in range(NB):
-        # Linear init U(+-1/sqrt(fan_in)), bias 0 (src/init.rs:54-181).
-        blk = {"x": torch.randn(B, T, C, device=dev, generator=g),
+        # LayerNorm init weight 1, bias 0; linear init U(+-1/sqrt(fan_in)),
+        # bias 0 (src/init.rs:54-181).
+        blk = {"h": torch.randn(B, T, C, device=dev, generator=g),
+               "lnw": torch.ones(C, device=dev), "lnb": torch.zeros(C, device=dev),
+               "x": torch.empty(B, T, C, device=dev), "dh": torch.empty(B, T, C, device=dev),
                "wa": (torch.rand(3 * C, C, device=dev, generator=g) * 2 - 1) / math.sqrt(C),
                "ba": torch.zeros(3 * C, device=dev),
                "wp": (torch.rand(C, C, device=dev, generator=g) * 2 - 1) / math.sqrt(C),
@@ -501,6 +508,7 @@ def run_layer(args):
     def step():
         n = 0
         for b in blocks:
+            n += kerr_attn.layernorm_fwd(ctx, b["h"], b["lnw"], b["lnb"], b["x"])
             n += kerr_attn.linear_fwd(ctx, b["x"], b["wa"], b["ba"], b["qkv"])
             n += kerr_attn.fwd(ctx, b["q"], b["k"], b["v"], b["o"], b["lse"], H)
             n += kerr_attn.linear_fwd(ctx, b["o"], b["wp"], b["bp"], b["y"])
@@ -512,6 +520,8 @@ def run_layer(args):
             n += kerr_attn.bwd(ctx, b["q"], b["k"], b["v"], b["o"], b["d_o"], b["lse"], b["dq"], b["dk"], b["dv"], H)
             n += kerr_attn.linear_bwd_dx(ctx, b["dqkv"], b["wa"], b["dx"])
             n += kerr_attn.linear_bwd_dw(ctx, b["dqkv"], b["x"], aw, ab, accumulate=False)
+            lw, lb = buckets.ln_views(i)
+            n += kerr_attn.layernorm_bwd(ctx, b["dx"], b["h"], b["lnw"], b["dh"], lw, lb, accumulate=False)
             buckets.launch(i)
         buckets.finish()
         return n
@@ -545,10 +555,11 @@ def run_layer(args):
     line = {"metric": LAYER_METRIC, "value": tokens / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded x, dy ~ N(0,1); linear init U(+-1/sqrt(fan_in)), bias 0)",
-            "config": dict(W, workload="kerr-engine 768-dim attention layer fwd+bwd (c_attn, attention, c_proj), "
-                                       "4 blocks per step", global_batch=B * world,
-                           parallelism=f"dp{world}, projection gradients all-reduced per block"),
+            "data": "synthetic (seeded h, dy ~ N(0,1); LayerNorm init 1 / 0; linear init U(+-1/sqrt(fan_in)), "
+                    "bias 0)",
+            "config": dict(W, workload="kerr-engine 768-dim attention sublayer fwd+bwd (ln_1, c_attn, attention, "
+                                       "c_proj), 4 blocks per step", global_batch=B * world,
+                           parallelism=f"dp{world}, sublayer parameter gradients all-reduced per block"),
             "gpu_launches": launches,
             "cublas_gemms_per_step": NB * 6,
             "allreduce": {"buckets_per_step": NB, "floats_per_bucket": buckets.numel,

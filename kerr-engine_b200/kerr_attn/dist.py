@@ -2,11 +2,12 @@
 
 Every (batch, head) slab of causal attention is independent, so the path
 shards by whole sequences with no exchange on the data path: rank r owns the
-contiguous batch slice shard_batch(B, world, r).  The only collectives are the
-timing barrier and the max-over-ranks reduction of measured times (NCCL over
-NVLink on GPUs, gloo on CPU).  The reference has no multi-process code; its
-only reduction is the host-side gradient sum of src/train.rs:257-269, which
-belongs to the projection layers outside this path.
+contiguous batch slice shard_batch(B, world, r).  The collectives are the
+timing barrier, the max-over-ranks reduction of measured times, and the
+data-parallel sum of the attention sublayer's parameter gradients
+(ProjGradBuckets), NCCL over NVLink on GPUs and gloo on CPU.  The reference
+has no multi-process code; its reduction is the host-side gradient sum over
+the batch of src/train.rs:257-269, which the all-reduce extends over ranks.
 """
 from __future__ import annotations
 
@@ -63,8 +64,9 @@ class ProjGradBuckets:
     reduced (sum) across the data-parallel ranks.
 
     Bucket i holds block i's c_attn weight [3C][C] and bias [3C], then c_proj's
-    weight [C][C] and bias [C] (4C^2 + 4C floats, the reference's
-    attn_c_attn_w / _b, attn_c_proj_w / _b).  ``launch(i)`` starts block i's
+    weight [C][C] and bias [C], then ln_1's weight [C] and bias [C]
+    (4C^2 + 6C floats, the reference's attn_c_attn_w / _b, attn_c_proj_w / _b,
+    ln_1_weight / _bias).  ``launch(i)`` starts block i's
     all-reduce as soon as its backward has been enqueued, so it overlaps the
     backward of the blocks below it; ``finish()`` waits for every bucket and
     divides by world * batch_per_rank: the reference sums per-sequence
@@ -78,7 +80,7 @@ class ProjGradBuckets:
         self.C = n_embd
         self.n_blocks = n_blocks
         self.batch_per_rank = batch_per_rank
-        self.numel = 4 * n_embd * n_embd + 4 * n_embd
+        self.numel = 4 * n_embd * n_embd + 6 * n_embd
         self.flat = torch.zeros(n_blocks, self.numel, device=device)
         self._work = []
 
@@ -88,7 +90,14 @@ class ProjGradBuckets:
         f = self.flat[i]
         a = 3 * C * C
         return (f[:a].view(3 * C, C), f[a:a + 3 * C], f[a + 3 * C:a + 3 * C + C * C].view(C, C),
-                f[a + 3 * C + C * C:])
+                f[a + 3 * C + C * C:a + 4 * C + C * C])
+
+    def ln_views(self, i: int):
+        """(ln_1_w [C], ln_1_b [C]) of block i."""
+        C = self.C
+        e = 4 * C * C + 4 * C
+        f = self.flat[i]
+        return f[e:e + C], f[e + C:e + 2 * C]
 
     def zero_(self):
         self.flat.zero_()

@@ -75,6 +75,9 @@ def _bucket_worker(rank, world, port, out):
             ab.fill_(10.0 * (rank + 1))
             pw.fill_(-1.0 * (rank + 1))
             pb.fill_(float(i))
+            lw, lb = g.ln_views(i)
+            lw.fill_(2.0 * (rank + 1))
+            lb.fill_(-float(i) * (rank + 1))
             g.launch(i)
         out[rank] = (g.finish(), g.flat.clone())
     finally:
@@ -97,11 +100,18 @@ def test_projection_gradient_allreduce_with_gloo():
         ab.fill_(sum(10.0 * (r + 1) for r in range(world)) * scale)
         pw.fill_(sum(-1.0 * (r + 1) for r in range(world)) * scale)
         pb.fill_(world * float(i) * scale)
+        lw, lb = ref.ln_views(i)
+        lw.fill_(sum(2.0 * (r + 1) for r in range(world)) * scale)
+        lb.fill_(sum(-float(i) * (r + 1) for r in range(world)) * scale)
     for rank in range(world):
         w, flat = out[rank]
         assert w == world
         assert torch.allclose(flat, ref.flat)
-    assert ref.numel == 4 * C * C + 4 * C
+    assert ref.numel == 4 * C * C + 6 * C
+    # The views tile each bucket exactly.
+    aw, ab, pw, pb = ref.views(0)
+    lw, lb = ref.ln_views(0)
+    assert sum(t.numel() for t in (aw, ab, pw, pb, lw, lb)) == ref.numel
 
 
 def test_projection_buckets_single_process():
