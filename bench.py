@@ -587,6 +587,300 @@ def run_layer(args):
         dist.destroy_process_group()
 
 
+KERR_METRIC = "Kerr-ODE (FFN ODE core) fwd+bwd tokens/s per GPU at 768-dim T=256, 4 blocks; % of FP32 roofline"
+KERR = {"workload": "kerr-engine 768-dim Kerr-ODE fwd+bwd (rk4_n_steps 8), 4 blocks per step",
+        "batch_per_gpu": 16, "seq_len": 256, "n_embd": 768, "n_bands": 384, "rk4_n_steps": 8, "blocks": 4,
+        "layout": "rows of n_embd floats, bands interleaved (r, s)",
+        "l2": "no flush: 4 blocks x 50 MB of distinct x, y, dy, dx buffers per step exceed the 126 MB L2"}
+
+
+def kerr_algorithmic(M, nb, n_steps):
+    """Floating-point operations of the reference's formulas per launch
+    (src/model.rs:778-843; src/backward.rs:184-379), counted per band and RK4
+    step: forward 90 (4 derivative evaluations of 16, three intermediate
+    states of 4, the weighted combination of 14); backward 300 (the step's
+    forward again, the fourth evaluation's stencil, four adjoint evaluations of
+    29 and their chaining).  Bytes: forward reads x and writes y, backward
+    reads dy and x and writes dx (4 bytes per float, 2 floats per band)."""
+    units = M * nb
+    return {"fwd_flops": 90.0 * n_steps * units, "bwd_flops": 300.0 * n_steps * units,
+            "fwd_bytes": 16.0 * units, "bwd_bytes": 24.0 * units}
+
+
+def run_kerr(args):
+    """Kerr-ODE of the 768-dim model: each block's forward, then the backwards
+    in reverse block order (the FFN's ODE calls of one training step,
+    src/pipeline.rs:1067, :1107).  Weak scaling: every rank runs its own
+    16 sequences; the parameter gradients are per-rank sums (the data-parallel
+    reduction of the FFN parameters is outside this path)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import kerr_attn
+    from kerr_attn.dist import max_over_ranks as _max_over_ranks
+    from kerr_attn.dist import sync as _sync
+    from kerr_attn.dist import world as _world
+
+    rank, local, world = _world()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    K = KERR
+    B, T, nb, n_steps, NB = K["batch_per_gpu"], K["seq_len"], K["n_bands"], K["rk4_n_steps"], K["blocks"]
+    M, n = B * T, 2 * nb
+    ctx = kerr_attn.Context(local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000 + rank)
+    # The reference's initial KerrWeights (src/init.rs:50-61); inputs ~ N(0,1)
+    # as LN2's output (plus the input maestro's small correction) is.
+    gamma_raw = torch.full((nb,), math.log(math.expm1(0.1)), device=dev)
+    omega = (torch.arange(nb, device=dev, dtype=torch.float32) + 1) / nb
+    ab = torch.tensor([0.1, 0.1], device=dev)
+    blocks = [{"x": torch.randn(M, n, device=dev, generator=g), "y": torch.empty(M, n, device=dev),
+               "dy": torch.randn(M, n, device=dev, generator=g), "dx": torch.empty(M, n, device=dev),
+               "dg": torch.zeros(nb, device=dev), "do": torch.zeros(nb, device=dev),
+               "dab": torch.zeros(2, device=dev)} for _ in range(NB)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        c = 0
+        for i, b in enumerate(blocks):
+            if ev is not None:
+                ev["f"][i][0].record(stream)
+            c += kerr_attn.kerr_ode_fwd(ctx, b["x"], gamma_raw, omega, ab, b["y"], n_steps, stream=stream)
+            if ev is not None:
+                ev["f"][i][1].record(stream)
+        for i in reversed(range(NB)):
+            b = blocks[i]
+            if ev is not None:
+                ev["b"][i][0].record(stream)
+            c += kerr_attn.kerr_ode_bwd(ctx, b["dy"], b["x"], gamma_raw, omega, ab, b["dx"], b["dg"], b["do"],
+                                        b["dab"], n_steps, accumulate=False, stream=stream)
+            if ev is not None:
+                ev["b"][i][1].record(stream)
+        return c
+
+    for _ in range(args.warmup):
+        step()
+    _sync(dev)
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = mk(), mk()
+    _sync(dev)
+    t0.record(stream)
+    launches = 0
+    for _ in range(args.steps):
+        launches += step()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    _sync(dev)
+    ms_step = _max_over_ranks(t0.elapsed_time(t1), dev) / args.steps
+    evs = [{"f": [(mk(), mk()) for _ in range(NB)], "b": [(mk(), mk()) for _ in range(NB)]}
+           for _ in range(args.steps)]
+    _sync(dev)
+    for s_ in range(args.steps):
+        step(evs[s_])
+    torch.cuda.synchronize(dev)
+    _sync(dev)
+    fwd_ms = _max_over_ranks(statistics.mean(e["f"][i][0].elapsed_time(e["f"][i][1]) for e in evs
+                                             for i in range(NB)), dev)
+    bwd_ms = _max_over_ranks(statistics.mean(e["b"][i][0].elapsed_time(e["b"][i][1]) for e in evs
+                                             for i in range(NB)), dev)
+    work = kerr_algorithmic(M, nb, n_steps)
+    ck = clocks.summary()
+    peaks, peak_src = measured_peaks()
+    props = torch.cuda.get_device_properties(dev)
+    sm_mhz = ck["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
+    fp32_peak = props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12
+    hbm = peaks.get("hbm_gbs", FALLBACK_HBM_GBS)
+    fwd_tf = work["fwd_flops"] / (fwd_ms / 1e3) / 1e12
+    bwd_tf = work["bwd_flops"] / (bwd_ms / 1e3) / 1e12
+    ctx.check_device()
+
+    # End to end: host x and dy in, host y and dx out per block (pinned), the
+    # parameters resident; copies on the compute stream inside the timed region.
+    hx = [b["x"].cpu().pin_memory() for b in blocks]
+    hdy = [b["dy"].cpu().pin_memory() for b in blocks]
+    hy = [torch.empty(M, n).pin_memory() for _ in blocks]
+    hdx = [torch.empty(M, n).pin_memory() for _ in blocks]
+    hpar = torch.empty(NB, 2 * nb + 2).pin_memory()
+
+    def step_e2e():
+        for i, b in enumerate(blocks):
+            b["x"].copy_(hx[i], non_blocking=True)
+            kerr_attn.kerr_ode_fwd(ctx, b["x"], gamma_raw, omega, ab, b["y"], n_steps, stream=stream)
+            hy[i].copy_(b["y"], non_blocking=True)
+        for i in reversed(range(NB)):
+            b = blocks[i]
+            b["dy"].copy_(hdy[i], non_blocking=True)
+            kerr_attn.kerr_ode_bwd(ctx, b["dy"], b["x"], gamma_raw, omega, ab, b["dx"], b["dg"], b["do"], b["dab"],
+                                   n_steps, accumulate=False, stream=stream)
+            hdx[i].copy_(b["dx"], non_blocking=True)
+            hpar[i, :nb].copy_(b["dg"], non_blocking=True)
+            hpar[i, nb:2 * nb].copy_(b["do"], non_blocking=True)
+            hpar[i, 2 * nb:].copy_(b["dab"], non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    step_e2e()
+    _sync(dev)
+    e0, e1 = mk(), mk()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        step_e2e()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    _sync(dev)
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dev) / e2e_steps
+    tokens = B * T * world
+    line = {"metric": KERR_METRIC, "value": tokens / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded x, dy ~ N(0,1); the reference's initial KerrWeights)",
+            "config": dict(K, global_batch=B * world, parallelism=f"dp{world} (positions sharded, no exchange)"),
+            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": NB * 2 * M * n * 4, "d2h_bytes_per_step": NB * (2 * M * n + 2 * nb + 2) * 4,
+                    "api": "kattn_kerr_ode_fwd / _bwd per block, pinned host x, dy in and y, dx, parameter "
+                           "gradients out, copies on the launching stream"},
+            "gpu_launches": launches,
+            "roofline": {"kernel": "kode_bwd + kode_param_final (one kattn_kerr_ode_bwd call, one block)",
+                         "bound": "fp32", "achieved": bwd_tf, "peak": fp32_peak, "unit": "TFLOP/s",
+                         "frac": bwd_tf / fp32_peak, "launch_ms": bwd_ms,
+                         "algorithmic_flops_per_launch": work["bwd_flops"],
+                         "peak_source": f"nominal FP32 FMA rate (148 SMs x 128 lanes x 2) at the sampled "
+                                        f"{sm_mhz:.0f} MHz; not in MEASURED_PEAKS.json",
+                         "hbm": {"achieved_gbs": work["bwd_bytes"] / (bwd_ms / 1e3) / 1e9, "peak_gbs": hbm,
+                                 "frac": work["bwd_bytes"] / (bwd_ms / 1e3) / 1e9 / hbm,
+                                 "peak_source": peak_src},
+                         "fwd": {"kernel": "kode_fwd", "launch_ms": fwd_ms, "achieved_tflops": fwd_tf,
+                                 "frac": fwd_tf / fp32_peak,
+                                 "achieved_gbs": work["fwd_bytes"] / (fwd_ms / 1e3) / 1e9}},
+            "clocks": ck}
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+
+        oracle.build()
+        cores = os.cpu_count() or 1
+        m = 16 * cores
+        rng = np.random.default_rng(5)
+        x = rng.standard_normal((m, n)).astype(np.float32)
+        dy = rng.standard_normal((m, n)).astype(np.float32)
+        gr, om = gamma_raw.cpu().numpy(), omega.cpu().numpy()
+        t_0 = time.perf_counter()
+        oracle.kerr_ode_forward(x, gr, om, 0.1, 0.1, n_steps, threads=cores)
+        oracle.kerr_ode_backward(dy, x, gr, om, 0.1, 0.1, n_steps, threads=cores)
+        t = time.perf_counter() - t_0
+        line["cpu_baseline"] = {"value": m / (NB * t), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": f"1 of 4 blocks, {m} of {M} positions (fwd + bwd) on {cores} host "
+                                          f"threads; scaled to the 4-block step"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+SWEEP_METRIC = "causal-attn fwd+bwd tokens/s and % of roofline per configuration (one GPU)"
+
+
+def run_sweep(args):
+    """The attention configurations besides the headline, each timed alone on
+    one GPU: the d=32 microbenchmark (B=64, H=4, T=256, q,k,v ~ N(0,1)/sqrt(32))
+    and the long-context sweep (B=8, H=12, d=64, T = 1024, 2048, 4096,
+    q,k,v ~ N(0,1)/8); dout ~ N(0,1).  One line per configuration, with the
+    achieved HBM GB/s and TFLOP/s of the fwd+bwd pair against the measured
+    peaks (the long-context sweep shards 96 slabs across GPUs with no
+    exchange; one GPU runs all of them here)."""
+    import torch
+
+    import kerr_attn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ctx = kerr_attn.Context(0)
+    peaks, peak_src = measured_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_HBM_GBS)
+    bf16 = peaks.get("bf16_tflops")
+    props = torch.cuda.get_device_properties(dev)
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    stream = torch.cuda.current_stream(dev)
+    for name, B, H, T, d, sig in (("attention microbenchmark d=32", 64, 4, 256, 32, 1 / math.sqrt(32)),
+                                  ("long-context T=1024", 8, 12, 1024, 64, 1 / 8),
+                                  ("long-context T=2048", 8, 12, 2048, 64, 1 / 8),
+                                  ("long-context T=4096", 8, 12, 4096, 64, 1 / 8)):
+        C = H * d
+        g = torch.Generator(device=dev)
+        g.manual_seed(B * T + d)
+        nbuf = max(1, math.ceil(256e6 / (4 * B * T * 9 * C)))  # distinct buffers: > L2 per round
+        bufs = []
+        for _ in range(nbuf):
+            qkv = torch.randn(B, T, 3 * C, device=dev, generator=g) * sig
+            b = {"qkv": qkv, "o": torch.empty(B, T, C, device=dev), "lse": torch.empty(B, H, T, device=dev),
+                 "dout": torch.randn(B, T, C, device=dev, generator=g), "dqkv": torch.empty_like(qkv)}
+            b["q"], b["k"], b["v"] = kerr_attn.split_qkv(b["qkv"], C)
+            b["dq"], b["dk"], b["dv"] = kerr_attn.split_qkv(b["dqkv"], C)
+            bufs.append(b)
+
+        def one(b):
+            c = kerr_attn.fwd(ctx, b["q"], b["k"], b["v"], b["o"], b["lse"], H, stream=stream)
+            return c + kerr_attn.bwd(ctx, b["q"], b["k"], b["v"], b["o"], b["dout"], b["lse"], b["dq"], b["dk"],
+                                     b["dv"], H, stream=stream)
+
+        for i in range(max(3, args.warmup)):
+            one(bufs[i % nbuf])
+        torch.cuda.synchronize(dev)
+        reps = max(nbuf, min(args.steps, 40 if T <= 1024 else 10))
+        clocks = ClockSampler(0)
+        clocks.start()
+        t0, t1 = mk(), mk()
+        t0.record(stream)
+        launches = 0
+        for i in range(reps):
+            launches += one(bufs[i % nbuf])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        clocks.stop()
+        ms = t0.elapsed_time(t1) / reps
+        w = algorithmic(B, T, H, d)
+        flops = w["fwd_flops"] + w["bwd_flops"]
+        byts = w["fwd_bytes"] + w["bwd_bytes"]
+        tf = flops / (ms / 1e3) / 1e12
+        gbs = byts / (ms / 1e3) / 1e9
+        ck = clocks.summary()
+        sm_mhz = ck["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
+        tensor = d == 64
+        # Roofline time: HBM bytes at the measured copy rate, or the pipe's
+        # executed flops (3 MMAs per product on the tensor path) at its peak.
+        pipe_tflops = bf16 if tensor else props.multi_processor_count * 256 * sm_mhz * 1e-6
+        executed = (3 if tensor else 1) * flops
+        t_roof = max(byts / (hbm * 1e9), executed / (pipe_tflops * 1e12))
+        line = {"metric": SWEEP_METRIC, "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+                "steps": reps, "ms_per_step": ms, "higher_is_better": True, "dtype": "f32",
+                "data": f"synthetic (seeded q,k,v ~ N(0,1) x {sig:.4f}, dout ~ N(0,1))",
+                "config": {"workload": name, "batch": B, "n_head": H, "seq_len": T, "head_dim": d, "causal": True,
+                           "l2": f"{nbuf} distinct buffer sets rotated" if nbuf > 1 else "inputs exceed L2"},
+                "kernel_path": "tcgen05 bf16x3" if tensor else "fp32 FFMA",
+                "gpu_launches": launches,
+                "roofline": {"achieved_gbs": gbs, "hbm_peak_gbs": hbm, "hbm_frac": gbs / hbm,
+                             "achieved_tflops": tf, "frac_of_roofline": (t_roof * 1e3) / ms,
+                             "roofline_ms": t_roof * 1e3,
+                             "pipe": ("tcgen05 kind::f16, 3 MMAs per product, measured dense bf16 "
+                                      f"{bf16} TF/s ({peak_src})") if tensor else
+                                     f"FP32 FFMA nominal at {sm_mhz:.0f} MHz",
+                             "pipe_frac": (3 if tensor else 1) * tf / pipe_tflops},
+                "clocks": ck}
+        print(json.dumps(line), flush=True)
+        del bufs
+        torch.cuda.empty_cache()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -597,9 +891,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", choices=("auto", "ffma", "tensor"), default="auto",
                     help="kernel family (auto: tensor cores where supported)")
-    ap.add_argument("--workload", choices=("attention", "layer"), default="attention",
+    ap.add_argument("--workload", choices=("attention", "layer", "kerr", "sweep"), default="attention",
                     help="attention: the headline (attention fwd+bwd); layer: c_attn + attention + c_proj with "
-                         "the projection-gradient all-reduce")
+                         "the projection-gradient all-reduce; kerr: the Kerr-ODE fwd+bwd; sweep: the d=32 "
+                         "microbenchmark and the long-context configurations, one line each")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -607,6 +902,10 @@ def main():
         run_reference(args)
     elif args.workload == "layer":
         run_layer(args)
+    elif args.workload == "kerr":
+        run_kerr(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 

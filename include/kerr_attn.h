@@ -237,6 +237,37 @@ int kattn_layernorm_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float
                         const float* w, float* dx, long ld_dx, float* dw, float* db,
                         int M, int N, int accumulate, void* stream);
 
+/* ---- Kerr-ODE, the ODE core of the FFN (KerrMaestroAdd / KerrDualMaestro) --
+ * Replace ComputeBackend::kerr_ode_batch (src/backend.rs:109-111; CPU
+ * kerr_ode_cpu :387-417) and kerr_ode_backward_batch (src/backend.rs:147-176;
+ * CPU kerr_ode_backward, src/backward.rs:382-458), called at
+ * src/pipeline.rs:504, :626, :1003, :1022, :1067, :1107.  A row is one
+ * position: n_embd = 2 n_bands floats, bands interleaved (r_0, s_0, r_1, s_1,
+ * ...) as the reference stores them.  KerrWeights (src/model.rs:199-205) is
+ * passed as device arrays: gamma_raw and omega of n_bands floats, alpha_beta =
+ * {alpha, beta}; rk4_n_steps is n_steps (dt = 1/n_steps).  Rows 16-byte
+ * aligned, row strides multiples of 4 floats; n_bands a multiple of 4, at most
+ * KATTN_KODE_MAX_BANDS.  Outputs may alias their inputs (y = x, dx = dy).
+ * f32 arithmetic (fused multiply-adds; ~1e-7 relative to the reference's
+ * loops).  Nothing synchronises the host. */
+#define KATTN_KODE_MAX_BANDS 1024
+
+/* y[m] = Kerr-ODE(x[m]) for m < M rows. */
+int kattn_kerr_ode_fwd(kattn_ctx* ctx, const float* x, long ld_x, float* y, long ld_y,
+                       const float* gamma_raw, const float* omega, const float* alpha_beta,
+                       int M, int n_bands, int n_steps, void* stream);
+
+/* dx[m] = dL/dx[m] for upstream dy[m]; d_gamma_raw / d_omega (n_bands floats)
+ * and d_alpha_beta (2 floats) receive the parameter gradients summed over the
+ * M rows: added to when accumulate != 0 (the += of src/pipeline.rs:627-632),
+ * written otherwise.  The sums run in a fixed order (no atomics): the same
+ * inputs give the same bits.  Workspace (one row of 2 n_bands + 4 floats per
+ * CTA) comes from the device's stream-ordered pool. */
+int kattn_kerr_ode_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
+                       const float* gamma_raw, const float* omega, const float* alpha_beta,
+                       float* dx, long ld_dx, float* d_gamma_raw, float* d_omega, float* d_alpha_beta,
+                       int M, int n_bands, int n_steps, int accumulate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

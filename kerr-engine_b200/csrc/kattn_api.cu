@@ -866,5 +866,81 @@ int kattn_layernorm_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float
     return proj_result(st, launches);
 }
 
+namespace {
+
+// Checks shared by the Kerr-ODE entry points.
+int kode_checks(const kattn_ctx* ctx, int M, int n_bands, int n_steps, const float* gamma_raw, const float* omega,
+                const float* alpha_beta) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    if (M < 0) return fail(KATTN_ERR_INVALID_ARGUMENT, "negative number of positions (M=%d)", M);
+    if (n_bands <= 0) return fail(KATTN_ERR_INVALID_ARGUMENT, "n_bands must be positive (got %d)", n_bands);
+    if (n_steps < 1) return fail(KATTN_ERR_INVALID_ARGUMENT, "n_steps must be positive (got %d)", n_steps);
+    if (n_bands % 4 != 0)
+        return fail(KATTN_ERR_UNSUPPORTED, "n_bands %d is not a multiple of 4 (n_embd a multiple of 8)", n_bands);
+    if (n_bands > KATTN_KODE_MAX_BANDS)
+        return fail(KATTN_ERR_UNSUPPORTED, "n_bands %d exceeds KATTN_KODE_MAX_BANDS=%d", n_bands,
+                    KATTN_KODE_MAX_BANDS);
+    if (!kattn::kode_supported(n_bands, n_steps))
+        return fail(KATTN_ERR_UNSUPPORTED, "n_steps %d x n_bands %d: the backward's saved states exceed shared memory",
+                    n_steps, n_bands);
+    KATTN_TRY(check_vec("gamma_raw", gamma_raw, true));
+    KATTN_TRY(check_vec("omega", omega, true));
+    KATTN_TRY(check_vec("alpha_beta", alpha_beta, true));
+    return KATTN_OK;
+}
+
+}  // namespace
+
+int kattn_kerr_ode_fwd(kattn_ctx* ctx, const float* x, long ld_x, float* y, long ld_y, const float* gamma_raw,
+                       const float* omega, const float* alpha_beta, int M, int n_bands, int n_steps, void* stream) {
+    g_last_launches = 0;
+    KATTN_TRY(kode_checks(ctx, M, n_bands, n_steps, gamma_raw, omega, alpha_beta));
+    KATTN_TRY(check_matrix("x", x, ld_x, M, 2L * n_bands));
+    KATTN_TRY(check_matrix("y", y, ld_y, M, 2L * n_bands));
+    if (M == 0) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    int launches = 0;
+    const kattn::ProjStatus st = kattn::kode_forward(static_cast<cudaStream_t>(stream), ctx->num_sms, x, ld_x, y, ld_y,
+                                                     gamma_raw, omega, alpha_beta, M, n_bands, n_steps, &launches);
+    return proj_result(st, launches);
+}
+
+int kattn_kerr_ode_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
+                       const float* gamma_raw, const float* omega, const float* alpha_beta, float* dx, long ld_dx,
+                       float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int M, int n_bands, int n_steps,
+                       int accumulate, void* stream) {
+    g_last_launches = 0;
+    KATTN_TRY(kode_checks(ctx, M, n_bands, n_steps, gamma_raw, omega, alpha_beta));
+    KATTN_TRY(check_matrix("dy", dy, ld_dy, M, 2L * n_bands));
+    KATTN_TRY(check_matrix("x", x, ld_x, M, 2L * n_bands));
+    KATTN_TRY(check_matrix("dx", dx, ld_dx, M, 2L * n_bands));
+    KATTN_TRY(check_vec("d_gamma_raw", d_gamma_raw, true));
+    KATTN_TRY(check_vec("d_omega", d_omega, true));
+    KATTN_TRY(check_vec("d_alpha_beta", d_alpha_beta, true));
+    if (M == 0 && accumulate) return ok_with_launches(0);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int rows = 0;
+    cudaError_t e = kattn::kode_backward_grid(ctx->num_sms, M, n_bands, n_steps, &rows);
+    if (e != cudaSuccess) return cuda_fail(e, "Kerr-ODE backward occupancy");
+    float* part = nullptr;
+    if (rows > 0) {
+        e = cudaMallocAsync(reinterpret_cast<void**>(&part),
+                            sizeof(float) * static_cast<size_t>(rows) * kattn::kode_part_width(n_bands), s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(Kerr-ODE partial sums)");
+    }
+    int launches = 0;
+    const kattn::ProjStatus st =
+        kattn::kode_backward(s, ctx->num_sms, dy, ld_dy, x, ld_x, gamma_raw, omega, alpha_beta, dx, ld_dx, d_gamma_raw,
+                             d_omega, d_alpha_beta, M, n_bands, n_steps, accumulate, part, rows, &launches);
+    if (part) {
+        const cudaError_t ef = cudaFreeAsync(part, s);
+        if (st.ok() && ef != cudaSuccess) return cuda_fail(ef, "cudaFreeAsync(Kerr-ODE partial sums)");
+    }
+    return proj_result(st, launches);
+}
+
 #pragma GCC visibility pop
 }  // extern "C"

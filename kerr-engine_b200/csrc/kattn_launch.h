@@ -104,4 +104,27 @@ ProjStatus ln_forward(cudaStream_t s, int num_sms, const float* x, long ld_x, co
 ProjStatus ln_backward(cudaStream_t s, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
                        float* dx, long ld_dx, float* dw, float* db, int M, int n, int accumulate, int* launches);
 
+// Kerr-ODE over rows of 2 nb interleaved (r, s) floats (kode.cu).  nb a
+// multiple of 4, at most KODE_MAX_BANDS; rows 16-byte aligned, strides
+// multiples of 4 floats.  gamma_raw / omega: nb floats, alpha_beta: 2 floats,
+// all device memory.  The backward's `part` holds part_rows rows of
+// kode_part_width(nb) floats, part_rows from kode_backward_grid; its parameter
+// gradients are added to when `accumulate`, written otherwise.
+constexpr int KODE_MAX_THREADS = 256;
+// A partial row: d_gamma [nb], d_omega [nb], d_alpha, d_beta, padded to a
+// multiple of 4 floats so that every row starts on a 16-byte boundary (the
+// per-band sums are stored as float4).
+inline __host__ __device__ int kode_part_width(int nb) { return 2 * nb + 4; }
+constexpr int KODE_MAX_BANDS = 4 * KODE_MAX_THREADS;
+constexpr size_t KODE_MAX_SMEM = 227 * 1024;
+bool kode_supported(int nb, int n_steps);
+ProjStatus kode_forward(cudaStream_t s, int num_sms, const float* x, long ld_x, float* y, long ld_y,
+                        const float* gamma_raw, const float* omega, const float* alpha_beta, int M, int nb,
+                        int n_steps, int* launches);
+cudaError_t kode_backward_grid(int num_sms, int M, int nb, int n_steps, int* grid);
+ProjStatus kode_backward(cudaStream_t s, int num_sms, const float* dy, long ld_dy, const float* x, long ld_x,
+                         const float* gamma_raw, const float* omega, const float* alpha_beta, float* dx, long ld_dx,
+                         float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int M, int nb, int n_steps,
+                         int accumulate, float* part, int part_rows, int* launches);
+
 }  // namespace kattn

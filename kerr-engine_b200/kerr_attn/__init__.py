@@ -43,10 +43,13 @@ EXPORTED_SYMBOLS = (
     "kattn_linear_fwd", "kattn_linear_bwd_dx", "kattn_linear_bwd_dw",
     "kattn_saved_create", "kattn_saved_destroy", "kattn_fwd_host_save", "kattn_bwd_host_saved",
     "kattn_layernorm_fwd", "kattn_layernorm_bwd",
+    "kattn_kerr_ode_fwd", "kattn_kerr_ode_bwd",
 )
 
 # Widest row kattn_layernorm_fwd / _bwd accept (KATTN_LN_MAX_N).
 LN_MAX_N = 1536
+# Most bands kattn_kerr_ode_fwd / _bwd accept (KATTN_KODE_MAX_BANDS).
+KODE_MAX_BANDS = 1024
 
 # Largest B*H*T that kattn_bwd_noalloc accepts (KATTN_NOALLOC_MAX_ROWS).
 NOALLOC_MAX_ROWS = 1 << 20
@@ -122,6 +125,10 @@ def lib():
     L.kattn_linear_bwd_dx.restype = _i
     L.kattn_linear_bwd_dw.argtypes = [_p, _p, _l, _p, _l, _p, _p, _i, _i, _i, _i, _p]
     L.kattn_linear_bwd_dw.restype = _i
+    L.kattn_kerr_ode_fwd.argtypes = [_p, _p, _l, _p, _l, _p, _p, _p, _i, _i, _i, _p]
+    L.kattn_kerr_ode_fwd.restype = _i
+    L.kattn_kerr_ode_bwd.argtypes = [_p, _p, _l, _p, _l, _p, _p, _p, _p, _l, _p, _p, _p, _i, _i, _i, _i, _p]
+    L.kattn_kerr_ode_bwd.restype = _i
     _lib = L
     return L
 
@@ -468,3 +475,45 @@ def layernorm_bwd(ctx: Context, dy, x, w, dx, dw, db, accumulate: bool = True, s
     _check(st, "kattn_layernorm_bwd")
     return last_launch_count()
 
+
+
+# ---------------------------------------------------------------- Kerr-ODE
+# The FFN's ODE core (include/kerr_attn.h, kattn_kerr_ode_*): rows of x / y /
+# dy / dx are positions of 2 * n_bands interleaved (r, s) floats; gamma_raw and
+# omega are [n_bands], alpha_beta is [alpha, beta]; all float32 CUDA tensors.
+
+def kerr_ode_fwd(ctx: Context, x, gamma_raw, omega, alpha_beta, y, n_steps: int, stream=None) -> int:
+    """y = Kerr-ODE(x) per row (kerr_ode_cpu, src/backend.rs:387-417).  Returns kernels launched."""
+    px, ldx, M, n = _mat(x, "x")
+    py, ldy, My, ny = _mat(y, "y")
+    nb = n // 2
+    if (My, ny) != (M, n) or tuple(gamma_raw.shape) != (nb,) or tuple(omega.shape) != (nb,) \
+            or tuple(alpha_beta.shape) != (2,):
+        raise ValueError("shapes: x [.., 2 nb], y like x, gamma_raw [nb], omega [nb], alpha_beta [2]")
+    st = lib().kattn_kerr_ode_fwd(ctx.handle, px, ldx, py, ldy, _vec(gamma_raw, "gamma_raw"), _vec(omega, "omega"),
+                                  _vec(alpha_beta, "alpha_beta"), M, nb, int(n_steps), _stream_ptr(stream, x.device))
+    _check(st, "kattn_kerr_ode_fwd")
+    return last_launch_count()
+
+
+def kerr_ode_bwd(ctx: Context, dy, x, gamma_raw, omega, alpha_beta, dx, d_gamma_raw, d_omega, d_alpha_beta,
+                 n_steps: int, accumulate: bool = True, stream=None) -> int:
+    """dx of the Kerr-ODE; the parameter gradients summed over the rows go into
+    d_gamma_raw / d_omega / d_alpha_beta (added when `accumulate`).  Returns kernels launched."""
+    pdy, lddy, M, n = _mat(dy, "dy")
+    px, ldx, Mx, nx = _mat(x, "x")
+    pdx, lddx, Md, nd = _mat(dx, "dx")
+    nb = n // 2
+    if (Mx, nx) != (M, n) or (Md, nd) != (M, n):
+        raise ValueError("shapes: dy, x, dx [.., 2 nb]")
+    for t, name, shape in ((gamma_raw, "gamma_raw", (nb,)), (omega, "omega", (nb,)), (alpha_beta, "alpha_beta", (2,)),
+                           (d_gamma_raw, "d_gamma_raw", (nb,)), (d_omega, "d_omega", (nb,)),
+                           (d_alpha_beta, "d_alpha_beta", (2,))):
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {shape}")
+    st = lib().kattn_kerr_ode_bwd(ctx.handle, pdy, lddy, px, ldx, _vec(gamma_raw, "gamma_raw"), _vec(omega, "omega"),
+                                  _vec(alpha_beta, "alpha_beta"), pdx, lddx, _vec(d_gamma_raw, "d_gamma_raw"),
+                                  _vec(d_omega, "d_omega"), _vec(d_alpha_beta, "d_alpha_beta"), M, nb, int(n_steps),
+                                  int(accumulate), _stream_ptr(stream, dy.device))
+    _check(st, "kattn_kerr_ode_bwd")
+    return last_launch_count()

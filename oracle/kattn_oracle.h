@@ -83,6 +83,17 @@ void kproj_oracle_backward_dx(int M, int N, int K, const float* dy, long ld_dy, 
 void kproj_oracle_backward_dw(int M, int N, int K, const float* dy, long ld_dy, const float* x, long ld_x,
                               float* dw, float* db, int nthreads);
 
+/* Kerr-ODE (kode_oracle.c): M positions of 2*nb interleaved floats
+ * (r_0, s_0, r_1, s_1, ...), gamma_raw / omega of nb floats, n_steps RK4
+ * steps of dt = 1/n_steps.  The backward writes dx and SETS d_gamma_raw /
+ * d_omega (nb floats) and d_alpha_beta[0..1] to the sums over the M
+ * positions.  nthreads <= 0: all online cores (at most M). */
+void kode_oracle_forward(int M, int nb, int n_steps, const float* x, long ld_x, const float* gamma_raw,
+                         const float* omega, float alpha, float beta, float* y, long ld_y, int nthreads);
+void kode_oracle_backward(int M, int nb, int n_steps, const float* dy, long ld_dy, const float* x, long ld_x,
+                          const float* gamma_raw, const float* omega, float alpha, float beta, float* dx, long ld_dx,
+                          float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,13 @@ def lib():
         L.kln_oracle_backward.argtypes = [ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f, ctypes.c_long, _f, _f,
                                           ctypes.c_long, _f, _f, ctypes.c_int]
         L.kln_oracle_backward.restype = None
+        L.kode_oracle_forward.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f, _f,
+                                          ctypes.c_float, ctypes.c_float, _f, ctypes.c_long, ctypes.c_int]
+        L.kode_oracle_forward.restype = None
+        L.kode_oracle_backward.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, _f, ctypes.c_long, _f,
+                                           ctypes.c_long, _f, _f, ctypes.c_float, ctypes.c_float, _f, ctypes.c_long,
+                                           _f, _f, _f, ctypes.c_int]
+        L.kode_oracle_backward.restype = None
         _lib = L
     return _lib
 
@@ -187,3 +194,36 @@ def layernorm_backward(dy, x, w, dw=None, db=None):
                               _ptr(dw_o), _ptr(db_o), int(acc))
     return dx, dw_o, db_o
 
+
+
+def kerr_ode_forward(x, gamma_raw, omega, alpha, beta, n_steps, threads=0):
+    """Kerr-ODE of each row of x [M, 2*nb] (interleaved r, s bands):
+    kerr_ode_cpu, src/backend.rs:387-417, mapped over the rows."""
+    x = np.ascontiguousarray(x, np.float32)
+    M, n = x.shape
+    nb = n // 2
+    y = np.empty((M, n), np.float32)
+    lib().kode_oracle_forward(M, nb, int(n_steps), _ptr(x), n, _ptr(np.ascontiguousarray(gamma_raw, np.float32)),
+                              _ptr(np.ascontiguousarray(omega, np.float32)), float(alpha), float(beta), _ptr(y), n,
+                              threads)
+    return y
+
+
+def kerr_ode_backward(dy, x, gamma_raw, omega, alpha, beta, n_steps, threads=1):
+    """(dx, d_gamma_raw, d_omega, d_alpha, d_beta) of the Kerr-ODE over the rows
+    of x: kerr_ode_backward_batch's default, src/backend.rs:147-176.  With
+    threads=1 the parameter sums run over the positions in the reference's
+    order."""
+    dy = np.ascontiguousarray(dy, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    M, n = x.shape
+    nb = n // 2
+    dx = np.empty((M, n), np.float32)
+    dgr = np.empty(nb, np.float32)
+    dom = np.empty(nb, np.float32)
+    dab = np.empty(2, np.float32)
+    lib().kode_oracle_backward(M, nb, int(n_steps), _ptr(dy), n, _ptr(x), n,
+                               _ptr(np.ascontiguousarray(gamma_raw, np.float32)),
+                               _ptr(np.ascontiguousarray(omega, np.float32)), float(alpha), float(beta), _ptr(dx), n,
+                               _ptr(dgr), _ptr(dom), _ptr(dab), threads)
+    return dx, dgr, dom, float(dab[0]), float(dab[1])

@@ -185,3 +185,37 @@ def test_layernorm_validation(L):
     assert bwd(dx=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
     assert bwd(dw=P(0x50004)) == kerr_attn.KATTN_ERR_MISALIGNED
     assert bwd(M=0, acc=1) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+
+
+def test_kerr_ode_validation(L):
+    # The Kerr-ODE entry points reject bad arguments before touching a device.
+    ctx = _fake_ctx()
+    P = ctypes.c_void_p
+    x, y, g, o, ab = P(0x10000), P(0x20000), P(0x30000), P(0x40000), P(0x50000)
+
+    def fwd(c=ctx, x=x, ldx=768, y=y, ldy=768, g=g, o=o, ab=ab, M=64, nb=384, steps=8):
+        return L.kattn_kerr_ode_fwd(c, x, ldx, y, ldy, g, o, ab, M, nb, steps, None)
+
+    assert fwd(c=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(M=-1) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(nb=0) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(steps=0) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(nb=382, ldx=764, ldy=764) == kerr_attn.KATTN_ERR_UNSUPPORTED  # n_embd not a multiple of 8
+    assert fwd(nb=kerr_attn.KODE_MAX_BANDS + 4, ldx=4096, ldy=4096) == kerr_attn.KATTN_ERR_UNSUPPORTED
+    assert fwd(nb=1024, ldx=2048, ldy=2048, steps=64) == kerr_attn.KATTN_ERR_UNSUPPORTED  # states exceed shared memory
+    assert "shared memory" in kerr_attn.last_error()
+    assert fwd(x=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(ldx=764) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT      # ld < 2 nb
+    assert fwd(ldy=770) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert fwd(x=P(0x10008)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert fwd(g=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(ab=P(0x50002)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert fwd(M=0) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+
+    def bwd(dx=P(0x60000), dg=P(0x70000), do=P(0x80000), dab=P(0x90000), M=64, acc=1):
+        return L.kattn_kerr_ode_bwd(ctx, y, 768, x, 768, g, o, ab, dx, 768, dg, do, dab, M, 384, 8, acc, None)
+
+    assert bwd(dx=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert bwd(dg=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert bwd(dab=P(0x90001)) == kerr_attn.KATTN_ERR_MISALIGNED
+    assert bwd(M=0, acc=1) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0

@@ -181,3 +181,59 @@ def test_layernorm_oracle_against_float64():
         assert rel_err(dx, dx_ref) < 1e-6
         assert rel_err(dw, dw0 + (dy * xh).sum(0)) < 1e-5
         assert rel_err(db, dw0 + dy.sum(0)) < 1e-5
+
+
+# ---------------------------------------------------------------- Kerr-ODE
+
+@pytest.mark.parametrize("M,nb,n_steps,seed", [(6, 64, 8, 1), (3, 384, 8, 2), (2, 20, 16, 3), (4, 4, 1, 4)])
+def test_kerr_ode_oracle_against_float64_autograd(oracle_lib, M, nb, n_steps, seed):
+    # The restatement of kerr_ode_cpu / kerr_ode_backward_batch against an
+    # independent float64 autograd of the same ODE (the reference's own
+    # check of its Kerr backward, src/grad_test.rs:50-174).
+    import kerr_ode_f64
+
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, 2 * nb)).astype(np.float32)
+    dy = rng.standard_normal((M, 2 * nb)).astype(np.float32)
+    gr, om, al, be = kerr_ode_f64.init_params(nb, seed=seed)
+    y = oracle_lib.kerr_ode_forward(x, gr, om, al, be, n_steps)
+    dx, dgr, dom, da, db = oracle_lib.kerr_ode_backward(dy, x, gr, om, al, be, n_steps)
+    ry, rdx, rdgr, rdom, rda, rdb = kerr_ode_f64.forward_backward(x, dy, gr, om, al, be, n_steps)
+    assert rel_err(y, ry) < 1e-6
+    assert rel_err(dx, rdx) < 1e-5
+    assert rel_err(dgr, rdgr) < 1e-5
+    assert rel_err(dom, rdom) < 1e-5
+    assert abs(da - rda) <= 1e-5 * max(abs(rda), 1e-30) + 1e-6
+    assert abs(db - rdb) <= 1e-5 * max(abs(rdb), 1e-30) + 1e-6
+
+
+def test_kerr_ode_oracle_known_answers(oracle_lib):
+    # Algebraic known answers of the reference's ODE (src/model.rs:778-843):
+    # a zero state stays zero; with alpha = beta = 0 every band is the linear
+    # rotation-with-decay (r + i s)' = (-gamma + i omega)(r + i s), whose RK4
+    # step multiplies by the degree-4 Taylor polynomial of exp(z dt).
+    nb, n_steps = 16, 8
+    gr = np.linspace(-2, 1, nb).astype(np.float32)
+    om = np.linspace(0.1, 2, nb).astype(np.float32)
+    zero = np.zeros((2, 2 * nb), np.float32)
+    assert not oracle_lib.kerr_ode_forward(zero, gr, om, 0.1, 0.1, n_steps).any()
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((3, 2 * nb)).astype(np.float32)
+    y = oracle_lib.kerr_ode_forward(x, gr, om, 0.0, 0.0, n_steps)
+    gamma = np.log1p(np.exp(gr.astype(np.float64)))
+    z = (-gamma + 1j * om.astype(np.float64)) / n_steps
+    g = (1 + z + z ** 2 / 2 + z ** 3 / 6 + z ** 4 / 24) ** n_steps
+    c = (x[:, 0::2] + 1j * x[:, 1::2]) * g
+    want = np.stack([c.real, c.imag], axis=2).reshape(x.shape)
+    assert rel_err(y, want) < 1e-6
+
+
+def test_kerr_ode_oracle_threads_keep_forward_bits(oracle_lib):
+    import kerr_ode_f64
+
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((9, 128)).astype(np.float32)
+    gr, om, al, be = kerr_ode_f64.init_params(64)
+    a = oracle_lib.kerr_ode_forward(x, gr, om, al, be, 8, threads=1)
+    b = oracle_lib.kerr_ode_forward(x, gr, om, al, be, 8, threads=4)
+    assert np.array_equal(a, b)
