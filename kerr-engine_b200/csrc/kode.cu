@@ -424,19 +424,43 @@ __global__ void __launch_bounds__(KODE_MAX_THREADS) kode_bwd(const OdeArgs a) {
     }
 }
 
-// out[i] (+)= sum over CTAs c of part[c][i], in CTA order, for the 2 nb + 2
-// parameter gradients (rows kode_part_width(nb) floats apart); d_gamma is chained through softplus' derivative
-// sigmoid(gamma_raw) (src/backward.rs:150-153).
-__global__ void __launch_bounds__(256) kode_param_final(const float* __restrict__ part, int P, int nb,
-                                                        const float* __restrict__ gamma_raw, float* __restrict__ dgr,
-                                                        float* __restrict__ dom, float* __restrict__ dab,
-                                                        int accumulate) {
+// out[i] (+)= sum over CTAs c of part[c][i] for the 2 nb + 2 parameter
+// gradients (rows kode_part_width(nb) floats apart); d_gamma is chained
+// through softplus' derivative sigmoid(gamma_raw) (src/backward.rs:150-153).
+// A CTA of 32 x 32 threads takes 32 outputs: thread (x, y) sums rows y, y + 32,
+// ... of output x (coalesced across x), then thread (x, 0) adds the 32 sums
+// in order of y.  The order is fixed: the same partials give the same bits.
+constexpr int KODE_FINAL_COLS = 32;
+constexpr int KODE_FINAL_GROUPS = 32;
+
+__global__ void __launch_bounds__(KODE_FINAL_COLS* KODE_FINAL_GROUPS)
+    kode_param_final(const float* __restrict__ part, int P, int nb, const float* __restrict__ gamma_raw,
+                     float* __restrict__ dgr, float* __restrict__ dom, float* __restrict__ dab, int accumulate) {
+    __shared__ float sums[KODE_FINAL_GROUPS][KODE_FINAL_COLS + 1];
     pdl_enter();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int x = threadIdx.x, y = threadIdx.y;
+    const int i = blockIdx.x * KODE_FINAL_COLS + x;
     const int width = kode_part_width(nb);
-    if (i >= 2 * nb + 2) return;
+    const bool valid = i < 2 * nb + 2;
+    float acc = 0.f;
+    if (valid) {
+        const float* col = part + i;
+        int c = y;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        for (; c + 3 * KODE_FINAL_GROUPS < P; c += 4 * KODE_FINAL_GROUPS) {
+            a0 += col[static_cast<long>(c) * width];
+            a1 += col[static_cast<long>(c + KODE_FINAL_GROUPS) * width];
+            a2 += col[static_cast<long>(c + 2 * KODE_FINAL_GROUPS) * width];
+            a3 += col[static_cast<long>(c + 3 * KODE_FINAL_GROUPS) * width];
+        }
+        for (; c < P; c += KODE_FINAL_GROUPS) a0 += col[static_cast<long>(c) * width];
+        acc = (a0 + a1) + (a2 + a3);
+    }
+    sums[y][x] = acc;
+    __syncthreads();
+    if (y != 0 || !valid) return;
     float sum = 0.f;
-    for (int c = 0; c < P; ++c) sum += part[static_cast<long>(c) * width + i];
+    for (int g = 0; g < KODE_FINAL_GROUPS; ++g) sum += sums[g][x];
     float* dst;
     if (i < nb) {
         const float g = gamma_raw[i];
@@ -559,7 +583,8 @@ ProjStatus kode_backward(cudaStream_t s, int num_sms, const float* dy, long ld_d
         *launches += 1;
     }
     const int outputs = 2 * nb + 2;
-    e = launch_pdl(kode_param_final, dim3(static_cast<unsigned>((outputs + 255) / 256)), dim3(256), 0, s,
+    e = launch_pdl(kode_param_final, dim3(static_cast<unsigned>((outputs + KODE_FINAL_COLS - 1) / KODE_FINAL_COLS)),
+                   dim3(KODE_FINAL_COLS, KODE_FINAL_GROUPS), 0, s,
                    static_cast<const float*>(part), P, nb, gamma_raw, d_gamma_raw, d_omega, d_alpha_beta, accumulate);
     if (e != cudaSuccess) {
         st.cuda = e;
