@@ -237,3 +237,14 @@ def test_kerr_ode_oracle_threads_keep_forward_bits(oracle_lib):
     a = oracle_lib.kerr_ode_forward(x, gr, om, al, be, 8, threads=1)
     b = oracle_lib.kerr_ode_forward(x, gr, om, al, be, 8, threads=4)
     assert np.array_equal(a, b)
+
+
+def test_training_loop_on_the_oracle_descends(oracle_lib):
+    # The CPU half of the loss-curve comparison (tests/test_gpu_train.py):
+    # the oracle's layers compose into a trainable stack whose loss falls.
+    import train_stack
+
+    blocks, h0, target = train_stack.init(2, 32, 64, 2, 2, seed=3)
+    losses = train_stack.train_oracle(blocks, h0, target, 2, 8, 0.03)
+    assert all(np.isfinite(losses))
+    assert all(b < a for a, b in zip(losses, losses[1:]))
