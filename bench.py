@@ -703,28 +703,22 @@ def run_kerr(args):
     bwd_tf = work["bwd_flops"] / (bwd_ms / 1e3) / 1e12
     ctx.check_device()
 
-    # End to end: host x and dy in, host y and dx out per block (pinned), the
-    # parameters resident; copies on the compute stream inside the timed region.
+    # End to end through the host-buffer ABI (kattn_kerr_ode_fwd_host /
+    # _bwd_host, the trait's host-slice boundary): pinned host x, dy and
+    # KerrWeights in; y, dx and the parameter gradients out, every call.
     hx = [b["x"].cpu().pin_memory() for b in blocks]
     hdy = [b["dy"].cpu().pin_memory() for b in blocks]
     hy = [torch.empty(M, n).pin_memory() for _ in blocks]
     hdx = [torch.empty(M, n).pin_memory() for _ in blocks]
-    hpar = torch.empty(NB, 2 * nb + 2).pin_memory()
+    hg, ho = gamma_raw.cpu(), omega.cpu()
+    hpar = [(torch.empty(nb), torch.empty(nb), torch.empty(2)) for _ in blocks]
 
     def step_e2e():
-        for i, b in enumerate(blocks):
-            b["x"].copy_(hx[i], non_blocking=True)
-            kerr_attn.kerr_ode_fwd(ctx, b["x"], gamma_raw, omega, ab, b["y"], n_steps, stream=stream)
-            hy[i].copy_(b["y"], non_blocking=True)
+        for i in range(NB):
+            kerr_attn.kerr_ode_fwd_host(ctx, hx[i], hg, ho, 0.1, 0.1, hy[i], n_steps)
         for i in reversed(range(NB)):
-            b = blocks[i]
-            b["dy"].copy_(hdy[i], non_blocking=True)
-            kerr_attn.kerr_ode_bwd(ctx, b["dy"], b["x"], gamma_raw, omega, ab, b["dx"], b["dg"], b["do"], b["dab"],
-                                   n_steps, accumulate=False, stream=stream)
-            hdx[i].copy_(b["dx"], non_blocking=True)
-            hpar[i, :nb].copy_(b["dg"], non_blocking=True)
-            hpar[i, nb:2 * nb].copy_(b["do"], non_blocking=True)
-            hpar[i, 2 * nb:].copy_(b["dab"], non_blocking=True)
+            kerr_attn.kerr_ode_bwd_host(ctx, hdy[i], hx[i], hg, ho, 0.1, 0.1, hdx[i], *hpar[i], n_steps,
+                                        accumulate=False)
 
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     step_e2e()
@@ -744,14 +738,16 @@ def run_kerr(args):
             "data": "synthetic (seeded x, dy ~ N(0,1); the reference's initial KerrWeights)",
             "config": dict(K, global_batch=B * world, parallelism=f"dp{world} (positions sharded, no exchange)"),
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": NB * 2 * M * n * 4, "d2h_bytes_per_step": NB * (2 * M * n + 2 * nb + 2) * 4,
-                    "api": "kattn_kerr_ode_fwd / _bwd per block, pinned host x, dy in and y, dx, parameter "
-                           "gradients out, copies on the launching stream"},
+                    "h2d_bytes_per_step": NB * (3 * M * n + 2 * (2 * nb + 2)) * 4,
+                    "d2h_bytes_per_step": NB * (2 * M * n + 2 * nb + 2) * 4,
+                    "api": "kattn_kerr_ode_fwd_host / _bwd_host per block (synchronous host-buffer calls): pinned "
+                           "x (twice) and dy up, y, dx and the parameter gradients down"},
             "gpu_launches": launches,
             "roofline": {"kernel": "kode_bwd + kode_param_final (one kattn_kerr_ode_bwd call, one block)",
                          "bound": "fp32", "achieved": bwd_tf, "peak": fp32_peak, "unit": "TFLOP/s",
                          "frac": bwd_tf / fp32_peak, "launch_ms": bwd_ms,
                          "algorithmic_flops_per_launch": work["bwd_flops"],
+                         "traffic": profiled_traffic("kode_bwd"),
                          "peak_source": f"nominal FP32 FMA rate (148 SMs x 128 lanes x 2) at the sampled "
                                         f"{sm_mhz:.0f} MHz; not in MEASURED_PEAKS.json",
                          "hbm": {"achieved_gbs": work["bwd_bytes"] / (bwd_ms / 1e3) / 1e9, "peak_gbs": hbm,

@@ -268,6 +268,24 @@ int kattn_kerr_ode_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float*
                        float* dx, long ld_dx, float* d_gamma_raw, float* d_omega, float* d_alpha_beta,
                        int M, int n_bands, int n_steps, int accumulate, void* stream);
 
+/* The same two operations on HOST buffers, the trait's own boundary
+ * (kerr_ode_batch / kerr_ode_backward_batch take host slices and
+ * &KerrWeights): x, y, dy, dx, gamma_raw, omega and the gradient outputs are
+ * host memory and alpha, beta are values.  Synchronous: the results are in
+ * the host arrays on return.  The positions move in up to 8 chunks on three
+ * streams (copies up, kernels, copies down), so with pinned host memory one
+ * chunk's copies overlap another's kernels.  Staging is a per-context device
+ * buffer that grows to the largest call; calls on one context are
+ * serialised.  The backward's accumulate has the meaning above (the host
+ * d_gamma_raw / d_omega / d_alpha_beta are added to). */
+int kattn_kerr_ode_fwd_host(kattn_ctx* ctx, const float* x, long ld_x, float* y, long ld_y,
+                            const float* gamma_raw, const float* omega, float alpha, float beta,
+                            int M, int n_bands, int n_steps);
+int kattn_kerr_ode_bwd_host(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
+                            const float* gamma_raw, const float* omega, float alpha, float beta,
+                            float* dx, long ld_dx, float* d_gamma_raw, float* d_omega, float* d_alpha_beta,
+                            int M, int n_bands, int n_steps, int accumulate);
+
 #ifdef __cplusplus
 }
 #endif

@@ -942,5 +942,172 @@ int kattn_kerr_ode_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float*
     return proj_result(st, launches);
 }
 
+namespace {
+
+// Host arrays of the Kerr-ODE parameters -> the device block
+// [gamma_raw | omega | alpha, beta] (the layout the kernels read).
+cudaError_t upload_kode_params(float* d, const float* gamma_raw, const float* omega, float alpha, float beta, int nb,
+                               cudaStream_t s) {
+    const float ab[2] = {alpha, beta};  // pageable: staged before cudaMemcpyAsync returns
+    cudaError_t e = cudaMemcpyAsync(d, gamma_raw, sizeof(float) * nb, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d + nb, omega, sizeof(float) * nb, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d + 2 * nb, ab, sizeof(ab), cudaMemcpyHostToDevice, s);
+    return e;
+}
+
+int kode_host_checks(const kattn_ctx* ctx, int M, int n_bands, int n_steps, const float* gamma_raw,
+                     const float* omega) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    // Device-side alignment does not apply to host arrays: check shapes with
+    // an aligned stand-in for the parameter pointers.
+    KATTN_TRY(kode_checks(ctx, M, n_bands, n_steps, gamma_raw, omega, gamma_raw));
+    return KATTN_OK;
+}
+
+int check_host_rows(const char* name, const void* p, long ld, long rows, long cols) {
+    if (rows > 0 && !p) return fail(KATTN_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+    if (ld < cols) return fail(KATTN_ERR_INVALID_ARGUMENT, "%s row stride %ld < %ld columns", name, ld, cols);
+    return KATTN_OK;
+}
+
+}  // namespace
+
+int kattn_kerr_ode_fwd_host(kattn_ctx* ctx, const float* x, long ld_x, float* y, long ld_y, const float* gamma_raw,
+                            const float* omega, float alpha, float beta, int M, int n_bands, int n_steps) {
+    g_last_launches = 0;
+    if (!gamma_raw || !omega) return fail(KATTN_ERR_INVALID_ARGUMENT, "gamma_raw / omega is NULL");
+    KATTN_TRY(kode_host_checks(ctx, M, n_bands, n_steps, gamma_raw, omega));
+    const int n = 2 * n_bands;
+    KATTN_TRY(check_host_rows("x", x, ld_x, M, n));
+    KATTN_TRY(check_host_rows("y", y, ld_y, M, n));
+    if (M == 0) return ok_with_launches(0);
+    std::lock_guard<std::mutex> lock(ctx->host_mu);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    const size_t par_b = align256(sizeof(float) * (2 * static_cast<size_t>(n_bands) + 2));
+    const size_t rows_b = align256(sizeof(float) * static_cast<size_t>(M) * n);
+    KATTN_TRY(ensure_arena(ctx, par_b + 2 * rows_b));
+    float* d_par = reinterpret_cast<float*>(ctx->arena);
+    float* d_x = reinterpret_cast<float*>(ctx->arena + par_b);
+    float* d_y = reinterpret_cast<float*>(ctx->arena + par_b + rows_b);
+    const Chunks ch(M, 2 * sizeof(float) * static_cast<size_t>(M) * n);  // x up, y down
+    KATTN_TRY(ensure_events(ctx, 2 * static_cast<size_t>(ch.n)));
+    int launches = 0;
+    const char* what = "host-to-device copy";
+    cudaError_t e = upload_kode_params(d_par, gamma_raw, omega, alpha, beta, n_bands, ctx->h2d);
+    for (int c = 0; c < ch.n && e == cudaSuccess; ++c) {
+        const long r0 = ch.b0(c), rows = ch.count(c, M);
+        what = "host-to-device copy";
+        e = copy_rows(d_x + r0 * n, n, x + r0 * ld_x, ld_x, n, rows, cudaMemcpyHostToDevice, ctx->h2d);
+        if (e == cudaSuccess) e = hand_off(ctx->h2d, ctx->stream, ctx->events[2 * c]);
+        if (e != cudaSuccess) break;
+        what = "Kerr-ODE forward launch";
+        const kattn::ProjStatus st =
+            kattn::kode_forward(ctx->stream, ctx->num_sms, d_x + r0 * n, n, d_y + r0 * n, n, d_par, d_par + n_bands,
+                                d_par + 2 * n_bands, static_cast<int>(rows), n_bands, n_steps, &launches);
+        e = st.cuda;
+        if (e == cudaSuccess) e = hand_off(ctx->stream, ctx->d2h, ctx->events[2 * c + 1]);
+        if (e != cudaSuccess) break;
+        what = "device-to-host copy";
+        e = copy_rows(y + r0 * ld_y, ld_y, d_y + r0 * n, n, n, rows, cudaMemcpyDeviceToHost, ctx->d2h);
+    }
+    const cudaError_t es = drain_host_streams(ctx);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    if (es != cudaSuccess) return cuda_fail(es, "cudaStreamSynchronize");
+    return ok_with_launches(launches);
+}
+
+int kattn_kerr_ode_bwd_host(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
+                            const float* gamma_raw, const float* omega, float alpha, float beta, float* dx, long ld_dx,
+                            float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int M, int n_bands, int n_steps,
+                            int accumulate) {
+    g_last_launches = 0;
+    if (!gamma_raw || !omega) return fail(KATTN_ERR_INVALID_ARGUMENT, "gamma_raw / omega is NULL");
+    KATTN_TRY(kode_host_checks(ctx, M, n_bands, n_steps, gamma_raw, omega));
+    const int n = 2 * n_bands;
+    KATTN_TRY(check_host_rows("dy", dy, ld_dy, M, n));
+    KATTN_TRY(check_host_rows("x", x, ld_x, M, n));
+    KATTN_TRY(check_host_rows("dx", dx, ld_dx, M, n));
+    if (!d_gamma_raw || !d_omega || !d_alpha_beta)
+        return fail(KATTN_ERR_INVALID_ARGUMENT, "d_gamma_raw / d_omega / d_alpha_beta is NULL");
+    if (M == 0) {
+        // No positions: the sums are zero (nothing to add when accumulating).
+        if (!accumulate) {
+            std::memset(d_gamma_raw, 0, sizeof(float) * n_bands);
+            std::memset(d_omega, 0, sizeof(float) * n_bands);
+            d_alpha_beta[0] = d_alpha_beta[1] = 0.f;
+        }
+        return ok_with_launches(0);
+    }
+    std::lock_guard<std::mutex> lock(ctx->host_mu);
+    DeviceScope scope(ctx->device);
+    if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+    const Chunks ch(M, 3 * sizeof(float) * static_cast<size_t>(M) * n);  // x, dy up; dx down
+    // Partial-row slices of the chunks' backward launches, one after another.
+    std::vector<int> part0(ch.n + 1, 0);
+    for (int c = 0; c < ch.n; ++c) {
+        int g = 0;
+        const cudaError_t eg = kattn::kode_backward_grid(ctx->num_sms, ch.count(c, M), n_bands, n_steps, &g);
+        if (eg != cudaSuccess) return cuda_fail(eg, "Kerr-ODE backward occupancy");
+        part0[c + 1] = part0[c] + g;
+    }
+    const size_t width = static_cast<size_t>(kattn::kode_part_width(n_bands));
+    const size_t par_b = align256(sizeof(float) * (2 * static_cast<size_t>(n_bands) + 2));
+    const size_t rows_b = align256(sizeof(float) * static_cast<size_t>(M) * n);
+    const size_t part_b = align256(sizeof(float) * width * part0[ch.n]);
+    KATTN_TRY(ensure_arena(ctx, 2 * par_b + 2 * rows_b + part_b));
+    float* d_par = reinterpret_cast<float*>(ctx->arena);
+    float* d_grads = reinterpret_cast<float*>(ctx->arena + par_b);  // [d_gamma_raw | d_omega | d_alpha, d_beta]
+    float* d_x = reinterpret_cast<float*>(ctx->arena + 2 * par_b);
+    float* d_dy = reinterpret_cast<float*>(ctx->arena + 2 * par_b + rows_b);  // dx overwrites dy in place
+    float* d_part = reinterpret_cast<float*>(ctx->arena + 2 * par_b + 2 * rows_b);
+    KATTN_TRY(ensure_events(ctx, 2 * static_cast<size_t>(ch.n) + 2));
+    int launches = 0;
+    const char* what = "host-to-device copy";
+    cudaError_t e = upload_kode_params(d_par, gamma_raw, omega, alpha, beta, n_bands, ctx->h2d);
+    if (e == cudaSuccess && accumulate)
+        e = upload_kode_params(d_grads, d_gamma_raw, d_omega, d_alpha_beta[0], d_alpha_beta[1], n_bands, ctx->h2d);
+    for (int c = 0; c < ch.n && e == cudaSuccess; ++c) {
+        const long r0 = ch.b0(c), rows = ch.count(c, M);
+        what = "host-to-device copy";
+        e = copy_rows(d_x + r0 * n, n, x + r0 * ld_x, ld_x, n, rows, cudaMemcpyHostToDevice, ctx->h2d);
+        if (e == cudaSuccess)
+            e = copy_rows(d_dy + r0 * n, n, dy + r0 * ld_dy, ld_dy, n, rows, cudaMemcpyHostToDevice, ctx->h2d);
+        if (e == cudaSuccess) e = hand_off(ctx->h2d, ctx->stream, ctx->events[2 * c]);
+        if (e != cudaSuccess) break;
+        what = "Kerr-ODE backward launch";
+        const kattn::ProjStatus st = kattn::kode_backward_rows(
+            ctx->stream, d_dy + r0 * n, n, d_x + r0 * n, n, d_par, d_par + n_bands, d_par + 2 * n_bands,
+            d_dy + r0 * n, n, static_cast<int>(rows), n_bands, n_steps, d_part + width * part0[c],
+            part0[c + 1] - part0[c], &launches);
+        e = st.cuda;
+        if (e == cudaSuccess) e = hand_off(ctx->stream, ctx->d2h, ctx->events[2 * c + 1]);
+        if (e != cudaSuccess) break;
+        what = "device-to-host copy";
+        e = copy_rows(dx + r0 * ld_dx, ld_dx, d_dy + r0 * n, n, n, rows, cudaMemcpyDeviceToHost, ctx->d2h);
+    }
+    if (e == cudaSuccess) {
+        what = "Kerr-ODE parameter-gradient launch";
+        const kattn::ProjStatus st =
+            kattn::kode_backward_final(ctx->stream, d_part, part0[ch.n], n_bands, d_par, d_grads, d_grads + n_bands,
+                                       d_grads + 2 * n_bands, accumulate, &launches);
+        e = st.cuda;
+        if (e == cudaSuccess) e = hand_off(ctx->stream, ctx->d2h, ctx->events[2 * ch.n]);
+        what = "device-to-host copy";
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_gamma_raw, d_grads, sizeof(float) * n_bands, cudaMemcpyDeviceToHost, ctx->d2h);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_omega, d_grads + n_bands, sizeof(float) * n_bands, cudaMemcpyDeviceToHost,
+                                ctx->d2h);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_alpha_beta, d_grads + 2 * n_bands, 2 * sizeof(float), cudaMemcpyDeviceToHost,
+                                ctx->d2h);
+    }
+    const cudaError_t es = drain_host_streams(ctx);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    if (es != cudaSuccess) return cuda_fail(es, "cudaStreamSynchronize");
+    return ok_with_launches(launches);
+}
+
 #pragma GCC visibility pop
 }  // extern "C"

@@ -122,6 +122,15 @@ ProjStatus kode_forward(cudaStream_t s, int num_sms, const float* x, long ld_x, 
                         const float* gamma_raw, const float* omega, const float* alpha_beta, int M, int nb,
                         int n_steps, int* launches);
 cudaError_t kode_backward_grid(int num_sms, int M, int nb, int n_steps, int* grid);
+// The two halves of kode_backward: the backward kernel over M rows writing
+// part_rows partial rows at `part`, and the fixed-order sum of part_rows
+// partial rows into the parameter gradients.
+ProjStatus kode_backward_rows(cudaStream_t s, const float* dy, long ld_dy, const float* x, long ld_x,
+                              const float* gamma_raw, const float* omega, const float* alpha_beta, float* dx,
+                              long ld_dx, int M, int nb, int n_steps, float* part, int part_rows, int* launches);
+ProjStatus kode_backward_final(cudaStream_t s, const float* part, int part_rows, int nb, const float* gamma_raw,
+                               float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int accumulate,
+                               int* launches);
 ProjStatus kode_backward(cudaStream_t s, int num_sms, const float* dy, long ld_dy, const float* x, long ld_x,
                          const float* gamma_raw, const float* omega, const float* alpha_beta, float* dx, long ld_dx,
                          float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int M, int nb, int n_steps,

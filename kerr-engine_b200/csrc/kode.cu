@@ -549,11 +549,11 @@ ProjStatus kode_forward(cudaStream_t s, int num_sms, const float* x, long ld_x, 
     return st;
 }
 
-ProjStatus kode_backward(cudaStream_t s, int num_sms, const float* dy, long ld_dy, const float* x, long ld_x,
-                         const float* gamma_raw, const float* omega, const float* alpha_beta, float* dx, long ld_dx,
-                         float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int M, int nb, int n_steps,
-                         int accumulate, float* part, int part_rows, int* launches) {
+ProjStatus kode_backward_rows(cudaStream_t s, const float* dy, long ld_dy, const float* x, long ld_x,
+                              const float* gamma_raw, const float* omega, const float* alpha_beta, float* dx,
+                              long ld_dx, int M, int nb, int n_steps, float* part, int part_rows, int* launches) {
     ProjStatus st;
+    if (M == 0) return st;
     OdeArgs a = {};
     a.x = x;
     a.ld_x = ld_x;
@@ -570,22 +570,26 @@ ProjStatus kode_backward(cudaStream_t s, int num_sms, const float* dy, long ld_d
     a.n_steps = n_steps;
     const int NB = kode_nb(nb), threads = kode_threads(nb);
     const size_t smem = bwd_smem(threads, NB, n_steps);
-    cudaError_t e = cudaSuccess;
-    int P = 0;
-    if (M > 0) {
-        P = part_rows;
-        e = NB == 2 ? launch_ode<2>(true, a, threads, smem, P, s) : launch_ode<4>(true, a, threads, smem, P, s);
-        if (e != cudaSuccess) {
-            st.cuda = e;
-            st.what = "Kerr-ODE backward launch";
-            return st;
-        }
-        *launches += 1;
+    const cudaError_t e = NB == 2 ? launch_ode<2>(true, a, threads, smem, part_rows, s)
+                                  : launch_ode<4>(true, a, threads, smem, part_rows, s);
+    if (e != cudaSuccess) {
+        st.cuda = e;
+        st.what = "Kerr-ODE backward launch";
+        return st;
     }
+    *launches += 1;
+    return st;
+}
+
+ProjStatus kode_backward_final(cudaStream_t s, const float* part, int part_rows, int nb, const float* gamma_raw,
+                               float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int accumulate,
+                               int* launches) {
+    ProjStatus st;
     const int outputs = 2 * nb + 2;
-    e = launch_pdl(kode_param_final, dim3(static_cast<unsigned>((outputs + KODE_FINAL_COLS - 1) / KODE_FINAL_COLS)),
-                   dim3(KODE_FINAL_COLS, KODE_FINAL_GROUPS), 0, s,
-                   static_cast<const float*>(part), P, nb, gamma_raw, d_gamma_raw, d_omega, d_alpha_beta, accumulate);
+    const cudaError_t e =
+        launch_pdl(kode_param_final, dim3(static_cast<unsigned>((outputs + KODE_FINAL_COLS - 1) / KODE_FINAL_COLS)),
+                   dim3(KODE_FINAL_COLS, KODE_FINAL_GROUPS), 0, s, part, part_rows, nb, gamma_raw, d_gamma_raw,
+                   d_omega, d_alpha_beta, accumulate);
     if (e != cudaSuccess) {
         st.cuda = e;
         st.what = "Kerr-ODE parameter-gradient launch";
@@ -593,6 +597,18 @@ ProjStatus kode_backward(cudaStream_t s, int num_sms, const float* dy, long ld_d
     }
     *launches += 1;
     return st;
+}
+
+ProjStatus kode_backward(cudaStream_t s, int num_sms, const float* dy, long ld_dy, const float* x, long ld_x,
+                         const float* gamma_raw, const float* omega, const float* alpha_beta, float* dx, long ld_dx,
+                         float* d_gamma_raw, float* d_omega, float* d_alpha_beta, int M, int nb, int n_steps,
+                         int accumulate, float* part, int part_rows, int* launches) {
+    (void)num_sms;
+    ProjStatus st = kode_backward_rows(s, dy, ld_dy, x, ld_x, gamma_raw, omega, alpha_beta, dx, ld_dx, M, nb,
+                                       n_steps, part, part_rows, launches);
+    if (!st.ok()) return st;
+    return kode_backward_final(s, part, M > 0 ? part_rows : 0, nb, gamma_raw, d_gamma_raw, d_omega, d_alpha_beta,
+                               accumulate, launches);
 }
 
 cudaError_t kode_backward_grid(int num_sms, int M, int nb, int n_steps, int* grid) {

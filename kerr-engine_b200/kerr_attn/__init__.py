@@ -43,7 +43,7 @@ EXPORTED_SYMBOLS = (
     "kattn_linear_fwd", "kattn_linear_bwd_dx", "kattn_linear_bwd_dw",
     "kattn_saved_create", "kattn_saved_destroy", "kattn_fwd_host_save", "kattn_bwd_host_saved",
     "kattn_layernorm_fwd", "kattn_layernorm_bwd",
-    "kattn_kerr_ode_fwd", "kattn_kerr_ode_bwd",
+    "kattn_kerr_ode_fwd", "kattn_kerr_ode_bwd", "kattn_kerr_ode_fwd_host", "kattn_kerr_ode_bwd_host",
 )
 
 # Widest row kattn_layernorm_fwd / _bwd accept (KATTN_LN_MAX_N).
@@ -129,6 +129,10 @@ def lib():
     L.kattn_kerr_ode_fwd.restype = _i
     L.kattn_kerr_ode_bwd.argtypes = [_p, _p, _l, _p, _l, _p, _p, _p, _p, _l, _p, _p, _p, _i, _i, _i, _i, _p]
     L.kattn_kerr_ode_bwd.restype = _i
+    L.kattn_kerr_ode_fwd_host.argtypes = [_p, _p, _l, _p, _l, _p, _p, _fl, _fl, _i, _i, _i]
+    L.kattn_kerr_ode_fwd_host.restype = _i
+    L.kattn_kerr_ode_bwd_host.argtypes = [_p, _p, _l, _p, _l, _p, _p, _fl, _fl, _p, _l, _p, _p, _p, _i, _i, _i, _i]
+    L.kattn_kerr_ode_bwd_host.restype = _i
     _lib = L
     return L
 
@@ -516,4 +520,40 @@ def kerr_ode_bwd(ctx: Context, dy, x, gamma_raw, omega, alpha_beta, dx, d_gamma_
                                   _vec(d_omega, "d_omega"), _vec(d_alpha_beta, "d_alpha_beta"), M, nb, int(n_steps),
                                   int(accumulate), _stream_ptr(stream, dy.device))
     _check(st, "kattn_kerr_ode_bwd")
+    return last_launch_count()
+
+
+def kerr_ode_fwd_host(ctx: Context, x, gamma_raw, omega, alpha: float, beta: float, y, n_steps: int) -> int:
+    """Synchronous Kerr-ODE forward on host (CPU) float32 tensors: rows of x / y
+    are positions; gamma_raw / omega host vectors; alpha, beta floats."""
+    px, ldx, M, n = _mat(x, "x")
+    py, ldy, My, ny = _mat(y, "y")
+    nb = n // 2
+    if (My, ny) != (M, n) or tuple(gamma_raw.shape) != (nb,) or tuple(omega.shape) != (nb,):
+        raise ValueError("shapes: x [.., 2 nb], y like x, gamma_raw [nb], omega [nb]")
+    st = lib().kattn_kerr_ode_fwd_host(ctx.handle, px, ldx, py, ldy, _vec(gamma_raw, "gamma_raw"),
+                                       _vec(omega, "omega"), float(alpha), float(beta), M, nb, int(n_steps))
+    _check(st, "kattn_kerr_ode_fwd_host")
+    return last_launch_count()
+
+
+def kerr_ode_bwd_host(ctx: Context, dy, x, gamma_raw, omega, alpha: float, beta: float, dx, d_gamma_raw, d_omega,
+                      d_alpha_beta, n_steps: int, accumulate: bool = True) -> int:
+    """Synchronous Kerr-ODE backward on host float32 tensors (see kerr_ode_bwd)."""
+    pdy, lddy, M, n = _mat(dy, "dy")
+    px, ldx, Mx, nx = _mat(x, "x")
+    pdx, lddx, Md, nd = _mat(dx, "dx")
+    nb = n // 2
+    if (Mx, nx) != (M, n) or (Md, nd) != (M, n):
+        raise ValueError("shapes: dy, x, dx [.., 2 nb]")
+    for t, name, shape in ((gamma_raw, "gamma_raw", (nb,)), (omega, "omega", (nb,)),
+                           (d_gamma_raw, "d_gamma_raw", (nb,)), (d_omega, "d_omega", (nb,)),
+                           (d_alpha_beta, "d_alpha_beta", (2,))):
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {shape}")
+    st = lib().kattn_kerr_ode_bwd_host(ctx.handle, pdy, lddy, px, ldx, _vec(gamma_raw, "gamma_raw"),
+                                       _vec(omega, "omega"), float(alpha), float(beta), pdx, lddx,
+                                       _vec(d_gamma_raw, "d_gamma_raw"), _vec(d_omega, "d_omega"),
+                                       _vec(d_alpha_beta, "d_alpha_beta"), M, nb, int(n_steps), int(accumulate))
+    _check(st, "kattn_kerr_ode_bwd_host")
     return last_launch_count()

@@ -219,3 +219,37 @@ def test_kerr_ode_validation(L):
     assert bwd(dg=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
     assert bwd(dab=P(0x90001)) == kerr_attn.KATTN_ERR_MISALIGNED
     assert bwd(M=0, acc=1) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+
+
+def test_kerr_ode_host_validation(L):
+    # The host-buffer Kerr-ODE entry points check their arguments before any
+    # device call (host arrays carry no alignment requirement).
+    ctx = _fake_ctx()
+    P = ctypes.c_void_p
+    x, y, g, o = P(0x10004), P(0x20004), P(0x30004), P(0x40004)
+
+    def fwd(c=ctx, x=x, ldx=768, y=y, ldy=768, g=g, o=o, M=64, nb=384, steps=8):
+        return L.kattn_kerr_ode_fwd_host(c, x, ldx, y, ldy, g, o, 0.1, 0.1, M, nb, steps)
+
+    assert fwd(c=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(g=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(x=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(ldy=700) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(nb=382, ldx=764, ldy=764) == kerr_attn.KATTN_ERR_UNSUPPORTED
+    assert fwd(steps=0) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert fwd(M=0) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+
+    def bwd(dx=P(0x50004), dg=P(0x60004), M=64, acc=1):
+        return L.kattn_kerr_ode_bwd_host(ctx, y, 768, x, 768, g, o, 0.1, 0.1, dx, 768, dg, P(0x70004), P(0x80004),
+                                         M, 384, 8, acc)
+
+    assert bwd(dx=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert bwd(dg=None) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+    assert bwd(M=0, acc=1) == kerr_attn.KATTN_OK and kerr_attn.last_launch_count() == 0
+    # No positions and accumulate=0: the host gradients are set to zero.
+    dgr = (ctypes.c_float * 384)(*([5.0] * 384))
+    dom = (ctypes.c_float * 384)(*([5.0] * 384))
+    dab = (ctypes.c_float * 2)(5.0, 5.0)
+    st = L.kattn_kerr_ode_bwd_host(ctx, y, 768, x, 768, g, o, 0.1, 0.1, P(0x50004), 768, dgr, dom, dab, 0, 384, 8, 0)
+    assert st == kerr_attn.KATTN_OK
+    assert not any(dgr) and not any(dom) and not any(dab)

@@ -174,3 +174,39 @@ def test_empty(ctx):
     torch.cuda.synchronize()
     assert torch.count_nonzero(dgr).item() == 0 and torch.count_nonzero(dom).item() == 0
     assert torch.count_nonzero(dab).item() == 0
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_buffer_calls(ctx, oracle_lib, pinned):
+    # kattn_kerr_ode_fwd_host / _bwd_host (the trait's host-slice boundary):
+    # the same results as the device calls, positions split into chunks.
+    M, nb, n_steps = 3001, 384, 8
+    n = 2 * nb
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((M, n)).astype(np.float32)
+    dy = rng.standard_normal((M, n)).astype(np.float32)
+    gr, om, al, be = kerr_ode_f64.init_params(nb, seed=4)
+
+    def host(a):
+        t = torch.from_numpy(np.ascontiguousarray(a, np.float32))
+        return t.pin_memory() if pinned else t.clone()
+
+    hy = host(np.full((M, n), np.nan))
+    assert kerr_attn.kerr_ode_fwd_host(ctx, host(x), host(gr), host(om), al, be, hy, n_steps) >= 1
+    y_dev = gpu_forward(ctx, x, gr, om, al, be, n_steps)
+    assert np.array_equal(hy.numpy(), y_dev)  # positions are independent: same bits
+    hdx = host(np.full((M, n), np.nan))
+    g0 = rng.standard_normal(nb).astype(np.float32)
+    hdg, hdo, hdab = host(g0), host(np.zeros(nb)), host(np.array([1.0, 2.0]))
+    launches = kerr_attn.kerr_ode_bwd_host(ctx, host(dy), host(x), host(gr), host(om), al, be, hdx, hdg, hdo, hdab,
+                                           n_steps, accumulate=True)
+    assert launches >= 2
+    dx_dev, dgr_dev, dom_dev, da_dev, db_dev = gpu_backward(ctx, dy, x, gr, om, al, be, n_steps)
+    assert np.array_equal(hdx.numpy(), dx_dev)
+    assert rel_err(hdg.numpy(), g0 + dgr_dev) < 1e-5
+    assert rel_err(hdo.numpy(), dom_dev) < 1e-5
+    assert abs(hdab[0].item() - (1.0 + da_dev)) <= 1e-4 * abs(1.0 + da_dev)
+    assert abs(hdab[1].item() - (2.0 + db_dev)) <= 1e-4 * abs(2.0 + db_dev)
+    rdx, rdgr, rdom, rda, rdb = oracle_lib.kerr_ode_backward(dy, x, gr, om, al, be, n_steps, threads=0)
+    assert rel_err(hdx.numpy(), rdx) < BWD_TOL
+    assert rel_err(hdg.numpy() - g0, rdgr) < BWD_TOL
