@@ -34,10 +34,21 @@ namespace {
 
 // src [rows][ld] f32 -> three bf16 copies of it (each either hi or lo:
 // segment g is lo when bit g of `lo_mask` is set), concatenated along the
-// columns (dst [rows][3*cols]) or along the rows (dst [3*rows][cols]).
-// cols % 4 == 0, ld % 4 == 0.
+// columns (dst [rows][pitch], pitch >= 3*cols) or along the rows
+// (dst [3*rows][cols]).  cols % 4 == 0, ld % 4 == 0.  Along the columns, the
+// pitch - 3*cols extra bf16 of each row (a multiple of 4) are written too:
+// zeros, except the first two, which are (1, 1) for EXTRA_ONES and
+// (bf16(b[r]), bf16(b[r] - bf16(b[r]))) for EXTRA_BIAS.  Contracting an
+// operand that ends in ones against one that ends in the bias pair adds
+// b_hi + b_lo (= b to ~1e-5 relative) to every output: the bias rides in
+// the GEMM instead of a separate fill and a read-modify-write of y.
+constexpr int EXTRA_NONE = 0;
+constexpr int EXTRA_ONES = 1;
+constexpr int EXTRA_BIAS = 2;
+
 __global__ void __launch_bounds__(256) proj_split3(const float* __restrict__ src, long ld, int rows, int cols,
-                                                   uint2* __restrict__ dst, int along_rows, int lo_mask) {
+                                                   uint2* __restrict__ dst, int along_rows, int lo_mask, int pitch4,
+                                                   int extra, const float* __restrict__ bias) {
     pdl_enter();
     const int c4 = cols / 4;
     const long n = static_cast<long>(rows) * c4;
@@ -51,8 +62,21 @@ __global__ void __launch_bounds__(256) proj_split3(const float* __restrict__ src
         sm100::split2(v.z, v.w, h.y, l.y);
 #pragma unroll
         for (int g = 0; g < 3; ++g) {
-            const long o = along_rows ? (static_cast<long>(g) * rows + r) * c4 + c : r * 3 * c4 + g * c4 + c;
+            const long o = along_rows ? (static_cast<long>(g) * rows + r) * c4 + c : r * pitch4 + g * c4 + c;
             dst[o] = (lo_mask >> g) & 1 ? l : h;
+        }
+        if (!along_rows && c == 0 && pitch4 > 3 * c4) {
+            uint2 e = make_uint2(0u, 0u);
+            if (extra == EXTRA_ONES) {
+                e.x = sm100::pack_bf16(1.f, 1.f);
+            } else if (extra == EXTRA_BIAS) {
+                uint32_t bh, bl;
+                sm100::split2(bias[r], 0.f, bh, bl);
+                e.x = (bh & 0xFFFFu) | (bl << 16);  // (b_hi, b_lo)
+            }
+            uint2* row = dst + r * pitch4 + 3 * c4;
+            row[0] = e;
+            for (int k = 1; k < pitch4 - 3 * c4; ++k) row[k] = make_uint2(0u, 0u);
         }
     }
 }
@@ -84,15 +108,28 @@ __global__ void __launch_bounds__(256) proj_colsum_part(const float* __restrict_
     part[static_cast<long>(p) * N + n] = s;
 }
 
-// db[n] (+)= sum over p of part[p][n], p in order: deterministic.
-__global__ void __launch_bounds__(256) proj_colsum_final(const float* __restrict__ part, int P, int N,
-                                                         float* __restrict__ db, int accumulate) {
+// db[n] (+)= sum over p of part[p][n]: a CTA of 32 x 32 threads takes 32
+// columns, thread (x, y) sums partials y, y + 32, ... of column x, then
+// thread (x, 0) adds the 32 sums in order of y.  The order is fixed:
+// deterministic.
+constexpr int COLSUM_COLS = 32;
+constexpr int COLSUM_GROUPS = 32;
+
+__global__ void __launch_bounds__(COLSUM_COLS* COLSUM_GROUPS)
+    proj_colsum_final(const float* __restrict__ part, int P, int N, float* __restrict__ db, int accumulate) {
+    __shared__ float sums[COLSUM_GROUPS][COLSUM_COLS + 1];
     pdl_enter();
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= N) return;
+    const int x = threadIdx.x, y = threadIdx.y;
+    const int n = blockIdx.x * COLSUM_COLS + x;
     float s = 0.f;
-    for (int p = 0; p < P; ++p) s += part[static_cast<long>(p) * N + n];
-    db[n] = accumulate ? db[n] + s : s;
+    if (n < N)
+        for (int p = y; p < P; p += COLSUM_GROUPS) s += part[static_cast<long>(p) * N + n];
+    sums[y][x] = s;
+    __syncthreads();
+    if (y != 0 || n >= N) return;
+    float t = 0.f;
+    for (int g = 0; g < COLSUM_GROUPS; ++g) t += sums[g][x];
+    db[n] = accumulate ? db[n] + t : t;
 }
 
 unsigned grid_for(long items, int num_sms) {
@@ -102,19 +139,24 @@ unsigned grid_for(long items, int num_sms) {
     return static_cast<unsigned>(g < 1 ? 1 : g);
 }
 
-// One operand as three bf16 copies along its contraction (see proj_split3).
+// One operand as three bf16 copies along its contraction (see proj_split3):
+// along the columns, rows of `pitch` bf16 (3*cols plus any extra columns).
 struct Cat3 {
     uint2* p;
     int along_rows;
     int lo_mask;
+    int pitch = 0;
+    int extra = EXTRA_NONE;
+    const float* bias = nullptr;
 };
 
 ProjStatus launch_split3(const float* src, long ld, int rows, int cols, Cat3 out, int num_sms, cudaStream_t s,
                          int* launches) {
     const long n = static_cast<long>(rows) * (cols / 4);
     if (n == 0) return {};
+    const int pitch4 = (out.pitch > 0 ? out.pitch : 3 * cols) / 4;
     const cudaError_t e = launch_pdl(proj_split3, dim3(grid_for(n, num_sms)), dim3(256), 0, s, src, ld, rows, cols,
-                                     out.p, out.along_rows, out.lo_mask);
+                                     out.p, out.along_rows, out.lo_mask, pitch4, out.extra, out.bias);
     if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "operand split"};
     ++*launches;
     return {};
@@ -150,6 +192,17 @@ Cat3 carve(char*& p, long elems, int along_rows, int lo_mask) {
     return c;
 }
 
+// Contraction length of the forward with a bias: 3K plus the two bias
+// columns, rounded up to a multiple of 8 bf16 (16-byte rows for the GEMM).
+int biased_pitch(int K) { return (3 * K + 2 + 7) / 8 * 8; }
+
+// A [rows][pitch] bf16 operand (pitch a multiple of 4) carved from p.
+Cat3 carve_pitched(char*& p, long rows, int pitch, int lo_mask, int extra, const float* bias) {
+    Cat3 c{reinterpret_cast<uint2*>(p), 0, lo_mask, pitch, extra, bias};
+    p += ((rows * pitch * 2 + 255) / 256) * 256;
+    return c;
+}
+
 // Segment patterns (bit g set: lo in segment g) so that the three products
 // are hi*hi + lo*hi + hi*lo.
 constexpr int PAT_HHL = 0b100;  // hi, hi, lo
@@ -162,32 +215,34 @@ ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t s, const float* 
     if (M == 0 || N == 0) return {};
     cublasHandle_t h = static_cast<cublasHandle_t>(handle);
     cudaError_t e;
-    if (K == 0 && !b) {
-        e = cudaMemset2DAsync(y, ld_y * 4, 0, static_cast<size_t>(N) * 4, M, s);
-        return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, CUBLAS_STATUS_SUCCESS, "cudaMemset2DAsync"};
-    }
-    float beta = 0.f;
-    if (b) {
+    if (K == 0) {
+        if (!b) {
+            e = cudaMemset2DAsync(y, ld_y * 4, 0, static_cast<size_t>(N) * 4, M, s);
+            return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, CUBLAS_STATUS_SUCCESS, "cudaMemset2DAsync"};
+        }
         e = launch_pdl(proj_fill_bias, dim3(grid_for(static_cast<long>(M) * N, num_sms)), dim3(256), 0, s, y, ld_y, M,
                        N, b);
         if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "bias fill"};
         ++*launches;
-        beta = 1.f;
+        return {};
     }
-    if (K == 0) return {};
     Workspace ws;
     ws.s = s;
-    const long ex = static_cast<long>(M) * K, ew = static_cast<long>(N) * K;
-    e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), cat3_bytes(ex) + cat3_bytes(ew), s);
+    // x' [M][Kp] = [x_hi | x_hi | x_lo (| 1, 1, 0...)], w' [N][Kp] = [w_hi | w_lo | w_hi (| b_hi, b_lo, 0...)]:
+    // with a bias, the contraction carries it (Kp = 3K + 2 rounded up to 8).
+    const int Kp = b ? biased_pitch(K) : 3 * K;
+    const long xb = ((static_cast<long>(M) * Kp * 2 + 255) / 256) * 256;
+    const long wb = ((static_cast<long>(N) * Kp * 2 + 255) / 256) * 256;
+    e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), xb + wb, s);
     if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
     char* p = ws.base;
-    // x' [M][3K] = [x_hi | x_hi | x_lo], w' [N][3K] = [w_hi | w_lo | w_hi].
-    const Cat3 xc = carve(p, ex, 0, PAT_HHL), wc = carve(p, ew, 0, PAT_HLH);
+    const Cat3 xc = carve_pitched(p, M, Kp, PAT_HHL, b ? EXTRA_ONES : EXTRA_NONE, nullptr);
+    const Cat3 wc = carve_pitched(p, N, Kp, PAT_HLH, b ? EXTRA_BIAS : EXTRA_NONE, b);
     ProjStatus st = launch_split3(x, ld_x, M, K, xc, num_sms, s, launches);
     if (!st.ok()) return st;
     st = launch_split3(w, K, N, K, wc, num_sms, s, launches);
     if (!st.ok()) return st;
-    return gemm(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, 3 * K, wc.p, 3 * K, xc.p, 3 * K, beta, y, ld_y, gemms);
+    return gemm(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, Kp, wc.p, Kp, xc.p, Kp, 0.f, y, ld_y, gemms);
 }
 
 ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, const float* dy, long ld_dy, const float* w,
@@ -237,8 +292,8 @@ ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, const flo
             if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "column sums"};
             ++*launches;
         }
-        e = launch_pdl(proj_colsum_final, dim3((N + 255) / 256), dim3(256), 0, s, static_cast<const float*>(part),
-                       M > 0 ? P : 0, N, db, accumulate);
+        e = launch_pdl(proj_colsum_final, dim3((N + COLSUM_COLS - 1) / COLSUM_COLS), dim3(COLSUM_COLS, COLSUM_GROUPS),
+                       0, s, static_cast<const float*>(part), M > 0 ? P : 0, N, db, accumulate);
         if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "column sums"};
         ++*launches;
     }
