@@ -16,8 +16,8 @@
 // w and b are staged in shared memory once per block.  Rows are independent;
 // the column sums of dw and db are formed without atomics in a fixed order
 // (each lane accumulates its columns over its warp's rows, the warps of a
-// block add theirs in turn, then one pass sums the per-block partials in
-// block order), so results do not depend on scheduling.  The two-pass variance
+// block add theirs in turn, then one pass sums the per-block partials in a
+// fixed grouping), so results do not depend on scheduling.  The two-pass variance
 // (deviations from the mean, as the reference computes it) keeps the
 // precision of the reference's formula.
 #include <cuda_runtime.h>
@@ -30,7 +30,7 @@ namespace kattn {
 namespace {
 
 constexpr int LN_WARPS = 8;     // warps (rows in flight) per block
-constexpr int LN_ROWS = 64;     // rows per block in the backward (column partials)
+constexpr int LN_ROWS = 16;     // rows per block in the backward (column partials): 256 blocks at 4096 rows
 constexpr int LN_MAX_V = LN_MAX_N / 128;
 constexpr float LN_EPS = 1e-5f;
 
@@ -197,17 +197,32 @@ __global__ void __launch_bounds__(32 * LN_WARPS) ln_bwd(const float* __restrict_
     for (int c = threadIdx.x; c < 2 * n4; c += blockDim.x) out[c] = acc[c];
 }
 
-// dw[c] (+)= sum_p part[p][0][c], db[c] (+)= sum_p part[p][1][c], p in order.
-__global__ void __launch_bounds__(256) ln_colsum(const float* __restrict__ part, int P, int n, float* __restrict__ dw,
-                                                 float* __restrict__ db, int accumulate) {
+// dw[c] (+)= sum_p part[p][0][c], db[c] (+)= sum_p part[p][1][c]: a CTA of
+// 32 x 32 threads takes 32 of the 2n outputs, thread (x, y) sums partials
+// y, y + 32, ... of output x, then thread (x, 0) adds the 32 sums in order of
+// y.  The order is fixed: deterministic.
+constexpr int LN_FINAL_COLS = 32;
+constexpr int LN_FINAL_GROUPS = 32;
+
+__global__ void __launch_bounds__(LN_FINAL_COLS* LN_FINAL_GROUPS)
+    ln_colsum(const float* __restrict__ part, int P, int n, float* __restrict__ dw, float* __restrict__ db,
+              int accumulate) {
+    __shared__ float sums[LN_FINAL_GROUPS][LN_FINAL_COLS + 1];
     pdl_enter();
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= 2 * n) return;
-    const int which = c / n, cc = c - which * n;
+    const int x = threadIdx.x, y = threadIdx.y;
+    const int c = blockIdx.x * LN_FINAL_COLS + x;
+    const bool valid = c < 2 * n;
+    const int which = valid ? c / n : 0, cc = c - which * n;
     float s = 0.f;
-    for (int p = 0; p < P; ++p) s += part[(static_cast<long>(p) * 2 + which) * n + cc];
+    if (valid)
+        for (int p = y; p < P; p += LN_FINAL_GROUPS) s += part[(static_cast<long>(p) * 2 + which) * n + cc];
+    sums[y][x] = s;
+    __syncthreads();
+    if (y != 0 || !valid) return;
+    float t = 0.f;
+    for (int g = 0; g < LN_FINAL_GROUPS; ++g) t += sums[g][x];
     float* dst = which ? db : dw;
-    if (dst) dst[cc] = accumulate ? dst[cc] + s : s;
+    if (dst) dst[cc] = accumulate ? dst[cc] + t : t;
 }
 
 template <int V>
@@ -299,8 +314,9 @@ ProjStatus ln_backward(cudaStream_t s, const float* dy, long ld_dy, const float*
     }
     if (e == cudaSuccess) {
         *launches += 1;
-        e = launch_pdl(ln_colsum, dim3(static_cast<unsigned>((2 * n + 255) / 256)), dim3(256), 0, s,
-                       static_cast<const float*>(part), P, n, dw, db, accumulate);
+        e = launch_pdl(ln_colsum, dim3(static_cast<unsigned>((2 * n + LN_FINAL_COLS - 1) / LN_FINAL_COLS)),
+                       dim3(LN_FINAL_COLS, LN_FINAL_GROUPS), 0, s, static_cast<const float*>(part), P, n, dw, db,
+                       accumulate);
         if (e == cudaSuccess) *launches += 1;
     }
     const cudaError_t ef = cudaFreeAsync(part, s);
