@@ -84,10 +84,11 @@ def test_reference_gpu_check_inputs(ctx, oracle_lib, case):
 
 # (M positions, n_bands, n_steps): the 128-dim model (B=4, T=64), the 768-dim
 # model (B=16, T=256) and the 1280-dim model (B=32, T=512) at rk4_n_steps 8;
-# 16 steps (src/gpu_validate.rs:122); a single step; the fewest bands (one
-# live thread) and the most bands supported.
-SHAPES = [(256, 64, 8), (4096, 384, 8), (16384, 640, 8), (300, 384, 16), (64, 128, 1), (33, 4, 8),
-          (40, kerr_attn.KODE_MAX_BANDS, 8)]
+# 16 steps (src/gpu_validate.rs:122); a single step; a band count that is not
+# a multiple of the 128 bands of a warp (196); the fewest bands (one live
+# thread) and the most bands supported.
+SHAPES = [(256, 64, 8), (4096, 384, 8), (16384, 640, 8), (300, 384, 16), (64, 128, 1), (45, 196, 8),
+          (33, 4, 8), (40, kerr_attn.KODE_MAX_BANDS, 8)]
 
 
 @pytest.mark.parametrize("M,nb,n_steps", SHAPES)
