@@ -374,9 +374,11 @@ def run_ours(args):
     ctx.check_device()
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "value_per_gpu": value / world,
+        "value_is": "whole-job tokens/s over all ranks (value_per_gpu: the same divided by n_gpus)",
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded q,k,v ~ N(0,1)/8, dout ~ N(0,1))",
-        "config": dict(WORKLOAD, global_batch=B * world, parallelism=f"dp{world} (batch shards, no exchange)"),
+        "config": dict(WORKLOAD, global_batch=B * world, parallelism=f"dp{world}: batch shards; attention itself has no exchange (the sublayer step with its gradient all-reduce is the dp_step record)"),
         "e2e": {"value": tokens_per_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "api": "kattn_fwd_host_save + kattn_bwd_host_saved per block (forward state kept on the "
@@ -401,6 +403,17 @@ def run_ours(args):
         },
         "clocks": ck,
     }
+    # The data-parallel step around the path at this world size: the
+    # sublayer with its per-block gradient all-reduce, at the 768-dim model
+    # and at the 1280-dim model (B=32 per GPU, H=20, T=512), and the
+    # long-context configuration sharded across the ranks.  Every rank runs
+    # these in the same order (they hold collectives).
+    if not args.no_nested:
+        n_steps, n_warm = max(3, min(args.steps, 20)), 3
+        line["dp_step"] = [
+            dp_step_object(ctx, dev, world, rank, 768, 12, 256, 16, 4, n_steps, n_warm, 3000),
+            dp_step_object(ctx, dev, world, rank, 1280, 20, 512, 32, 4, n_steps, n_warm, 4000)]
+        line["long_context"] = long_context_object(ctx, dev, world, rank, n_steps, n_warm)
     if world == 1 and not args.no_cpu_baseline:
         cores = os.cpu_count() or 1
         n_seq = min(cores, B)
@@ -455,40 +468,29 @@ def layer_cpu_sample(n_seq: int, T: int, H: int, d: int, threads: int, seed: int
     return time.perf_counter() - t0
 
 
-def run_layer(args):
-    """The whole attention sublayer of the 768-dim model per block
-    (src/pipeline.rs:236-249): LN1, c_attn, attention, c_proj forward; their
-    backward in reverse block order; each block's parameter gradients (c_attn,
-    c_proj, ln_1) all-reduced across the ranks (NCCL) as soon as its backward
-    is enqueued, overlapping the blocks below (the data-parallel exchange of
-    the step)."""
+def dp_layer_step(ctx, dev, world, C, H, T, B, NB, steps, warmup, seed, exchange=True):
+    """Times the data-parallel training step of the attention sublayer on
+    this rank: per block LN1, c_attn, attention and c_proj forward, then the
+    blocks' backward in reverse order, each block's parameter gradients
+    all-reduced across the ranks (NCCL) in two segments, c_proj's as soon as
+    its dW is enqueued and the rest when the block's backward is, both
+    overlapping the backward still to come (kerr_attn.dist.ProjGradBuckets;
+    the reference's host-side gradient sum, src/train.rs:257-269).
+    exchange=False skips the all-reduce (the same step on one rank's data
+    alone).  Returns the step time (max over ranks) and what it moved."""
     import torch
-    import torch.distributed as dist
 
     import kerr_attn
     from kerr_attn.dist import ProjGradBuckets
     from kerr_attn.dist import max_over_ranks as _max_over_ranks
     from kerr_attn.dist import sync as _sync
-    from kerr_attn.dist import world as _world
 
-    rank, local, world = _world()
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
-    W = WORKLOAD
-    B, T, H, d, NB = W["batch_per_gpu"], W["seq_len"], W["n_head"], W["head_dim"], W["blocks"]
-    C = H * d
-    M = B * T
-    ctx = kerr_attn.Context(local)
     g = torch.Generator(device=dev)
-    g.manual_seed(2000 + rank)
+    g.manual_seed(seed)
     blocks = []
     for _ in range(NB):
         # LayerNorm init weight 1, bias 0; linear init U(+-1/sqrt(fan_in)),
-        # bias 0 (src/init.rs:54-181).
+        # bias 0 (src/init.rs:9-23).
         blk = {"h": torch.randn(B, T, C, device=dev, generator=g),
                "lnw": torch.ones(C, device=dev), "lnb": torch.zeros(C, device=dev),
                "x": torch.empty(B, T, C, device=dev), "dh": torch.empty(B, T, C, device=dev),
@@ -517,32 +519,171 @@ def run_layer(args):
             aw, ab, pw, pb = buckets.views(i)
             n += kerr_attn.linear_bwd_dx(ctx, b["dy"], b["wp"], b["d_o"])
             n += kerr_attn.linear_bwd_dw(ctx, b["dy"], b["o"], pw, pb, accumulate=False)
+            if exchange:
+                buckets.launch_proj(i)
             n += kerr_attn.bwd(ctx, b["q"], b["k"], b["v"], b["o"], b["d_o"], b["lse"], b["dq"], b["dk"], b["dv"], H)
             n += kerr_attn.linear_bwd_dx(ctx, b["dqkv"], b["wa"], b["dx"])
             n += kerr_attn.linear_bwd_dw(ctx, b["dqkv"], b["x"], aw, ab, accumulate=False)
             lw, lb = buckets.ln_views(i)
             n += kerr_attn.layernorm_bwd(ctx, b["dx"], b["h"], b["lnw"], b["dh"], lw, lb, accumulate=False)
-            buckets.launch(i)
+            if exchange:
+                buckets.launch(i)
         buckets.finish()
         return n
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     _sync(dev)
     mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
-    clocks = ClockSampler(local)
-    clocks.start()
     t0, t1 = mk(), mk()
     _sync(dev)
     t0.record()
     launches = 0
-    for _ in range(args.steps):
+    for _ in range(steps):
         launches += step()
     t1.record()
     torch.cuda.synchronize(dev)
-    clocks.stop()
     _sync(dev)
-    ms_step = _max_over_ranks(t0.elapsed_time(t1), dev) / args.steps
+    ms_step = _max_over_ranks(t0.elapsed_time(t1), dev) / steps
+    del blocks
+    return {"ms_per_step": ms_step, "tokens_per_s": B * T * world / (ms_step / 1e3), "steps": steps,
+            "gpu_launches": launches,
+            "allreduce": {"segments_per_step": 2 * NB if (exchange and world > 1) else 0,
+                          "bytes_per_step": NB * buckets.numel * 4 if (exchange and world > 1) else 0,
+                          "backend": "nccl" if (exchange and world > 1) else "none"}}
+
+
+def dp_step_object(ctx, dev, world, rank, C, H, T, B, NB, steps, warmup, seed):
+    """The nested record of one data-parallel sublayer configuration: the
+    step with its gradient all-reduce, the same step without the exchange,
+    and the ratio of the two (the exchange's cost at this world size)."""
+    import torch
+
+    full = dp_layer_step(ctx, dev, world, C, H, T, B, NB, steps, warmup, seed + rank, exchange=True)
+    torch.cuda.empty_cache()
+    alone = dp_layer_step(ctx, dev, world, C, H, T, B, NB, steps, warmup, seed + rank, exchange=False)
+    torch.cuda.empty_cache()
+    d = C // H
+    work = algorithmic(B, T, H, d)
+    flops = NB * (24.0 * B * T * C * C + work["fwd_flops"] + work["bwd_flops"])
+    return {"workload": f"attention sublayer (ln_1, c_attn, causal attention, c_proj) fwd+bwd, n_embd {C}, "
+                        f"{H} heads, seq_len {T}, {B} sequences per GPU, {NB} blocks",
+            "n_gpus": world, "global_batch": B * world, **full,
+            "ms_per_step_without_exchange": alone["ms_per_step"],
+            "efficiency_vs_no_exchange": alone["ms_per_step"] / full["ms_per_step"],
+            "algorithmic_tflops": flops / (full["ms_per_step"] / 1e3) / 1e12}
+
+
+LONG_CONTEXT = {"batch": 8, "n_head": 12, "head_dim": 64, "seq_lens": (1024, 2048, 4096)}
+
+
+def long_context_object(ctx, dev, world, rank, steps, warmup):
+    """The long-context configuration (B=8, H=12, d=64, T = 1024, 2048,
+    4096; q, k, v ~ N(0,1)/8, dout ~ N(0,1)) with its 96 (batch, head) slabs
+    sharded across the ranks by whole sequences (rank r owns
+    shard_batch(8, world, r); no exchange).  Per T: fwd+bwd time (max over
+    ranks), whole-job tokens/s and the fraction of this GPU's roofline for
+    the shard it ran (the larger of its HBM bytes at the measured copy rate
+    and its tensor-core flops, 3 bf16 MMAs per product, at the measured bf16
+    rate)."""
+    import torch
+
+    import kerr_attn
+    from kerr_attn.dist import max_over_ranks as _max_over_ranks
+    from kerr_attn.dist import shard_batch
+    from kerr_attn.dist import sync as _sync
+
+    L = LONG_CONTEXT
+    H, d = L["n_head"], L["head_dim"]
+    C = H * d
+    b0, b1 = shard_batch(L["batch"], world, rank)
+    nb = b1 - b0
+    peaks, peak_src = measured_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_HBM_GBS)
+    bf16 = peaks.get("bf16_tflops") or 1590.0
+    stream = torch.cuda.current_stream(dev)
+    out = []
+    for T in L["seq_lens"]:
+        g = torch.Generator(device=dev)
+        g.manual_seed(5000 + T + 17 * rank)
+        per_set = 4 * max(nb, 1) * T * 9 * C
+        nbuf = max(1, math.ceil(256e6 / per_set))  # rotate distinct buffers: > L2 per round
+        bufs = []
+        for _ in range(nbuf if nb else 0):
+            qkv = torch.randn(nb, T, 3 * C, device=dev, generator=g) / 8
+            b = {"qkv": qkv, "o": torch.empty(nb, T, C, device=dev), "lse": torch.empty(nb, H, T, device=dev),
+                 "dout": torch.randn(nb, T, C, device=dev, generator=g), "dqkv": torch.empty_like(qkv)}
+            b["q"], b["k"], b["v"] = kerr_attn.split_qkv(b["qkv"], C)
+            b["dq"], b["dk"], b["dv"] = kerr_attn.split_qkv(b["dqkv"], C)
+            bufs.append(b)
+
+        def one(i):
+            if not bufs:
+                return 0
+            b = bufs[i % len(bufs)]
+            n = kerr_attn.fwd(ctx, b["q"], b["k"], b["v"], b["o"], b["lse"], H, stream=stream)
+            return n + kerr_attn.bwd(ctx, b["q"], b["k"], b["v"], b["o"], b["dout"], b["lse"], b["dq"], b["dk"],
+                                     b["dv"], H, stream=stream)
+
+        for i in range(warmup):
+            one(i)
+        reps = max(nbuf, steps)
+        _sync(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        launches = 0
+        for i in range(reps):
+            launches += one(i)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        _sync(dev)
+        ms = _max_over_ranks(t0.elapsed_time(t1) / reps, dev)
+        w = algorithmic(max(nb, 1), T, H, d)
+        byts = w["fwd_bytes"] + w["bwd_bytes"]
+        flops = w["fwd_flops"] + w["bwd_flops"]
+        t_roof_ms = 1e3 * max(byts / (hbm * 1e9), 3 * flops / (bf16 * 1e12))
+        out.append({"seq_len": T, "sequences_per_gpu": nb, "slabs_per_gpu": nb * H, "ms_per_step": ms,
+                    "tokens_per_s": L["batch"] * T / (ms / 1e3), "steps": reps, "gpu_launches": launches,
+                    "roofline_frac": t_roof_ms / ms, "roofline_ms": t_roof_ms,
+                    "bound": "tensor" if 3 * flops / (bf16 * 1e12) > byts / (hbm * 1e9) else "hbm",
+                    "algorithmic_tflops": flops / (ms / 1e3) / 1e12,
+                    "l2": f"{nbuf} distinct buffer sets rotated" if nbuf > 1 else "inputs exceed L2"})
+        del bufs
+        torch.cuda.empty_cache()
+    return {"workload": "long-context causal attention fwd+bwd, B=8, H=12, d=64, 96 (batch, head) slabs sharded "
+                        "by whole sequences across the ranks, no exchange",
+            "peaks": f"HBM {hbm} GB/s, bf16 {bf16} TF/s ({peak_src})", "per_seq_len": out}
+
+
+def run_layer(args):
+    """The whole attention sublayer of the 768-dim model per block
+    (src/pipeline.rs:236-249) as the data-parallel step of dp_layer_step:
+    LN1, c_attn, attention, c_proj forward; their backward in reverse block
+    order; each block's parameter gradients (c_attn, c_proj, ln_1) all-reduced
+    across the ranks (NCCL) while the blocks below run their backward."""
+    import torch
+    import torch.distributed as dist
+
+    import kerr_attn
+    from kerr_attn.dist import world as _world
+
+    rank, local, world = _world()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    W = WORKLOAD
+    B, T, H, d, NB = W["batch_per_gpu"], W["seq_len"], W["n_head"], W["head_dim"], W["blocks"]
+    C = H * d
+    M = B * T
+    ctx = kerr_attn.Context(local)
+    clocks = ClockSampler(local)
+    clocks.start()
+    r = dp_layer_step(ctx, dev, world, C, H, T, B, NB, args.steps, args.warmup, 2000 + rank)
+    clocks.stop()
+    ms_step = r["ms_per_step"]
     tokens = B * T * world
     work = algorithmic(B, T, H, d)
     gemm_flops = 24.0 * M * C * C  # c_attn and c_proj: forward, dx and dW (2 flops per MAC)
@@ -560,10 +701,8 @@ def run_layer(args):
             "config": dict(W, workload="kerr-engine 768-dim attention sublayer fwd+bwd (ln_1, c_attn, attention, "
                                        "c_proj), 4 blocks per step", global_batch=B * world,
                            parallelism=f"dp{world}, sublayer parameter gradients all-reduced per block"),
-            "gpu_launches": launches,
-            "cublas_gemms_per_step": NB * 6,
-            "allreduce": {"buckets_per_step": NB, "floats_per_bucket": buckets.numel,
-                          "bytes_per_step": NB * buckets.numel * 4, "backend": "nccl" if world > 1 else "none"},
+            "gpu_launches": r["gpu_launches"],
+            "allreduce": r["allreduce"],
             "roofline": {"bound": "tensor", "achieved": achieved, "unit": "TFLOP/s",
                          "algorithmic_flops_per_step": flops_step,
                          "executed_tflops": 3 * achieved, "peak": bf16,
@@ -806,10 +945,14 @@ def run_sweep(args):
     props = torch.cuda.get_device_properties(dev)
     mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     stream = torch.cuda.current_stream(dev)
-    for name, B, H, T, d, sig in (("attention microbenchmark d=32", 64, 4, 256, 32, 1 / math.sqrt(32)),
-                                  ("long-context T=1024", 8, 12, 1024, 64, 1 / 8),
-                                  ("long-context T=2048", 8, 12, 2048, 64, 1 / 8),
-                                  ("long-context T=4096", 8, 12, 4096, 64, 1 / 8)):
+    configs = (("d32", "attention microbenchmark d=32", 64, 4, 256, 32, 1 / math.sqrt(32)),
+               ("t1024", "long-context T=1024", 8, 12, 1024, 64, 1 / 8),
+               ("t2048", "long-context T=2048", 8, 12, 2048, 64, 1 / 8),
+               ("t4096", "long-context T=4096", 8, 12, 4096, 64, 1 / 8))
+    only = set(args.sweep_only.split(",")) if args.sweep_only else None
+    for key, name, B, H, T, d, sig in configs:
+        if only is not None and key not in only:
+            continue
         C = H * d
         g = torch.Generator(device=dev)
         g.manual_seed(B * T + d)
@@ -885,6 +1028,10 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep-only", default="",
+                    help="--workload sweep: comma-separated subset of d32, t1024, t2048, t4096")
+    ap.add_argument("--no-nested", action="store_true",
+                    help="skip the nested data-parallel step and long-context records of the headline line")
     ap.add_argument("--path", choices=("auto", "ffma", "tensor"), default="auto",
                     help="kernel family (auto: tensor cores where supported)")
     ap.add_argument("--workload", choices=("attention", "layer", "kerr", "sweep"), default="attention",

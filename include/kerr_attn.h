@@ -33,8 +33,12 @@
  *     thread.
  *   - kattn_fwd / kattn_bwd only enqueue work on `stream` (a cudaStream_t,
  *     NULL = legacy default stream) and never synchronise the host.
- *     kattn_bwd takes a [B][H][T] float workspace from the device's
- *     stream-ordered memory pool on that stream and returns it there.
+ *     kattn_bwd takes a [B][H][T] float workspace on that stream from a
+ *     stream-ordered memory pool the context owns and returns it there.
+ *   - Workspace pool: each context creates its own pool (cudaMemPoolCreate)
+ *     on its device.  Freed blocks stay cached in it until kattn_destroy
+ *     (at most the largest workspace that calls in flight held at once);
+ *     the device's default pool and its settings are not touched.
  *   - A context may be shared by threads: the device-pointer calls keep no
  *     per-call state in it; the host-buffer calls serialise on a lock inside
  *     it (as the reference's GPU backend serialises on its buffer pool,
@@ -115,7 +119,7 @@ int kattn_bwd(kattn_ctx* ctx,
 /* kattn_bwd for callers that cannot allocate device memory: a framework that
  * accounts for every byte through its own caching allocator, or a runtime
  * that reserves all device memory up front, cannot let a library take
- * memory from the device's stream-ordered pool as kattn_bwd does for its
+ * memory from a stream-ordered pool as kattn_bwd does for its
  * [B][H][T] workspace.  This variant allocates nothing: the workspace is a
  * fixed array in the library's device image, whose address kattn_create
  * looks up once per context (so create the context before relying on this
@@ -198,7 +202,7 @@ int kattn_last_launch_count(void);
  * (hi*hi + hi*lo + lo*hi, f32 accumulation; ~1e-5 relative) by one cuBLAS
  * GEMM over a threefold contraction of operands this library splits and
  * concatenates.  Workspace comes from the
- * device's stream-ordered pool; nothing synchronises the host. */
+ * context's stream-ordered pool; nothing synchronises the host. */
 
 /* y[m][n] = b[n] + sum_k w[n][k] x[m][k];  b may be NULL (no bias). */
 int kattn_linear_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, const float* b,
@@ -262,7 +266,7 @@ int kattn_kerr_ode_fwd(kattn_ctx* ctx, const float* x, long ld_x, float* y, long
  * M rows: added to when accumulate != 0 (the += of src/pipeline.rs:627-632),
  * written otherwise.  The sums run in a fixed order (no atomics): the same
  * inputs give the same bits.  Workspace (one row of 2 n_bands + 4 floats per
- * CTA) comes from the device's stream-ordered pool. */
+ * CTA) comes from the context's stream-ordered pool. */
 int kattn_kerr_ode_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float* x, long ld_x,
                        const float* gamma_raw, const float* omega, const float* alpha_beta,
                        float* dx, long ld_dx, float* d_gamma_raw, float* d_omega, float* d_alpha_beta,

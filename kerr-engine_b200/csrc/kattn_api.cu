@@ -30,6 +30,7 @@ struct kattn_ctx {
     char* arena = nullptr;          // device staging for the host-buffer entry points
     size_t arena_bytes = 0;
     float* noalloc_ws = nullptr;    // device address of g_noalloc_ws on this device
+    cudaMemPool_t pool = nullptr;   // the context's own stream-ordered pool for per-call workspace
     void* cublas = nullptr;         // cublasHandle_t of the projection GEMMs, created on first use
     std::mutex proj_mu;             // binds the handle to a stream and enqueues a call as one step
 };
@@ -481,24 +482,38 @@ int kattn_create(int device, kattn_ctx** out) {
         delete ctx;
         return cuda_fail(e, "status word");
     }
-    // kattn_bwd takes its workspace from the stream-ordered pool: keep freed
-    // blocks cached in the pool instead of returning them at each sync.
-    // Device address of the fixed workspace (this device is current here).
+    // Device address of the fixed workspace of kattn_bwd_noalloc (this
+    // device is current here).
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ctx->noalloc_ws), g_noalloc_ws);
+    const char* what = "cudaGetSymbolAddress(workspace)";
+    if (e == cudaSuccess) {
+        // Per-call workspace (the backward's [B][H][T] rows, column-sum
+        // partials) comes from a pool this context owns.  It keeps freed
+        // blocks cached until kattn_destroy, so a steady stream of calls does
+        // not return memory to the driver at every synchronisation; the
+        // device's default pool and its settings are left as they are.
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.handleTypes = cudaMemHandleTypeNone;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        what = "cudaMemPoolCreate";
+        e = cudaMemPoolCreate(&ctx->pool, &props);
+        if (e == cudaSuccess) {
+            uint64_t keep = UINT64_MAX;
+            what = "cudaMemPoolSetAttribute";
+            e = cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+    }
     if (e != cudaSuccess) {
+        if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
         cudaStreamDestroy(ctx->stream);
         cudaStreamDestroy(ctx->h2d);
         cudaStreamDestroy(ctx->d2h);
         cudaFree(ctx->d_status);
         delete ctx;
-        return cuda_fail(e, "cudaGetSymbolAddress(workspace)");
+        return cuda_fail(e, what);
     }
-    cudaMemPool_t pool;
-    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
-        uint64_t keep = UINT64_MAX;
-        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
-    }
-    cudaGetLastError();
     *out = ctx;
     return KATTN_OK;
 }
@@ -518,6 +533,9 @@ int kattn_destroy(kattn_ctx* ctx) {
         if (ctx->arena) cudaFree(ctx->arena);
         if (ctx->d_status) cudaFree(ctx->d_status);
         if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
+        // Blocks still owed to the pool by work in flight on callers' streams
+        // are released by the driver once that work frees them.
+        if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
     }
     delete ctx;
     return status;
@@ -572,8 +590,8 @@ int kattn_bwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, lo
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     float* dsum = nullptr;
     const size_t ws = sizeof(float) * static_cast<size_t>(B) * H * T;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&dsum), ws, s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(workspace)");
+    cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&dsum), ws, ctx->pool, s);
+    if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
     kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, dsum, B, T, H, d, scale, causal};
     int launches = 0;
     e = dispatch_bwd(ctx, a, s, &launches);
@@ -779,7 +797,7 @@ int kattn_linear_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, 
     KATTN_TRY(proj_handle(ctx, s, &h));
     int launches = 0, gemms = 0;
     const kattn::ProjStatus st =
-        kattn::proj_forward(h, ctx->num_sms, s, x, ld_x, w, b, y, ld_y, M, N, K, &launches, &gemms);
+        kattn::proj_forward(h, ctx->num_sms, s, ctx->pool, x, ld_x, w, b, y, ld_y, M, N, K, &launches, &gemms);
     return proj_result(st, launches);
 }
 
@@ -800,7 +818,7 @@ int kattn_linear_bwd_dx(kattn_ctx* ctx, const float* dy, long ld_dy, const float
     KATTN_TRY(proj_handle(ctx, s, &h));
     int launches = 0, gemms = 0;
     const kattn::ProjStatus st =
-        kattn::proj_backward_dx(h, ctx->num_sms, s, dy, ld_dy, w, dx, ld_dx, M, N, K, &launches, &gemms);
+        kattn::proj_backward_dx(h, ctx->num_sms, s, ctx->pool, dy, ld_dy, w, dx, ld_dx, M, N, K, &launches, &gemms);
     return proj_result(st, launches);
 }
 
@@ -821,7 +839,7 @@ int kattn_linear_bwd_dw(kattn_ctx* ctx, const float* dy, long ld_dy, const float
     void* h = nullptr;
     KATTN_TRY(proj_handle(ctx, s, &h));
     int launches = 0, gemms = 0;
-    const kattn::ProjStatus st = kattn::proj_backward_dw(h, ctx->num_sms, s, dy, ld_dy, x, ld_x, dw, db, M, N, K,
+    const kattn::ProjStatus st = kattn::proj_backward_dw(h, ctx->num_sms, s, ctx->pool, dy, ld_dy, x, ld_x, dw, db, M, N, K,
                                                          accumulate, &launches, &gemms);
     return proj_result(st, launches);
 }
@@ -861,7 +879,7 @@ int kattn_layernorm_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
     int launches = 0;
-    const kattn::ProjStatus st = kattn::ln_backward(static_cast<cudaStream_t>(stream), dy, ld_dy, x, ld_x, w, dx,
+    const kattn::ProjStatus st = kattn::ln_backward(static_cast<cudaStream_t>(stream), ctx->pool, dy, ld_dy, x, ld_x, w, dx,
                                                     ld_dx, dw, db, M, N, accumulate, &launches);
     return proj_result(st, launches);
 }
@@ -927,9 +945,10 @@ int kattn_kerr_ode_bwd(kattn_ctx* ctx, const float* dy, long ld_dy, const float*
     if (e != cudaSuccess) return cuda_fail(e, "Kerr-ODE backward occupancy");
     float* part = nullptr;
     if (rows > 0) {
-        e = cudaMallocAsync(reinterpret_cast<void**>(&part),
-                            sizeof(float) * static_cast<size_t>(rows) * kattn::kode_part_width(n_bands), s);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(Kerr-ODE partial sums)");
+        e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&part),
+                                    sizeof(float) * static_cast<size_t>(rows) * kattn::kode_part_width(n_bands),
+                                    ctx->pool, s);
+        if (e != cudaSuccess) return cuda_fail(e, "workspace allocation (Kerr-ODE partial sums)");
     }
     int launches = 0;
     const kattn::ProjStatus st =

@@ -85,11 +85,11 @@ struct ProjStatus {
 // `handle` is a cublasHandle_t already bound to `stream`.  Arrays are
 // row-major f32; w is [N][K] contiguous, dw [N][K] contiguous.  *launches
 // counts this library's kernels, *gemms the cuBLAS GEMM calls.
-ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t stream, const float* x, long ld_x, const float* w,
+ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t stream, cudaMemPool_t pool, const float* x, long ld_x, const float* w,
                         const float* b, float* y, long ld_y, int M, int N, int K, int* launches, int* gemms);
-ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t stream, const float* dy, long ld_dy,
+ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t stream, cudaMemPool_t pool, const float* dy, long ld_dy,
                             const float* w, float* dx, long ld_dx, int M, int N, int K, int* launches, int* gemms);
-ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t stream, const float* dy, long ld_dy,
+ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t stream, cudaMemPool_t pool, const float* dy, long ld_dy,
                             const float* x, long ld_x, float* dw, float* db, int M, int N, int K, int accumulate,
                             int* launches, int* gemms);
 
@@ -101,7 +101,7 @@ constexpr int LN_MAX_N = KATTN_LN_MAX_N;
 bool ln_supported(int n);
 ProjStatus ln_forward(cudaStream_t s, int num_sms, const float* x, long ld_x, const float* w, const float* b, float* y,
                       long ld_y, int M, int n, int* launches);
-ProjStatus ln_backward(cudaStream_t s, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
+ProjStatus ln_backward(cudaStream_t s, cudaMemPool_t pool, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
                        float* dx, long ld_dx, float* dw, float* db, int M, int n, int accumulate, int* launches);
 
 // Kerr-ODE over rows of 2 nb interleaved (r, s) floats (kode.cu).  nb a

@@ -274,7 +274,7 @@ ProjStatus ln_forward(cudaStream_t s, int num_sms, const float* x, long ld_x, co
     return st;
 }
 
-ProjStatus ln_backward(cudaStream_t s, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
+ProjStatus ln_backward(cudaStream_t s, cudaMemPool_t pool, const float* dy, long ld_dy, const float* x, long ld_x, const float* w,
                        float* dx, long ld_dx, float* dw, float* db, int M, int n, int accumulate, int* launches) {
     ProjStatus st;
     if (M == 0) {
@@ -292,7 +292,7 @@ ProjStatus ln_backward(cudaStream_t s, const float* dy, long ld_dy, const float*
     }
     const int P = (M + LN_ROWS - 1) / LN_ROWS;
     float* part = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&part), sizeof(float) * 2 * static_cast<size_t>(P) * n, s);
+    cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&part), sizeof(float) * 2 * static_cast<size_t>(P) * n, pool, s);
     if (e != cudaSuccess) {
         st.cuda = e;
         st.what = "layer-norm workspace";

@@ -210,7 +210,7 @@ constexpr int PAT_HLH = 0b010;  // hi, lo, hi
 
 }  // namespace
 
-ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t s, const float* x, long ld_x, const float* w,
+ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t s, cudaMemPool_t pool, const float* x, long ld_x, const float* w,
                         const float* b, float* y, long ld_y, int M, int N, int K, int* launches, int* gemms) {
     if (M == 0 || N == 0) return {};
     cublasHandle_t h = static_cast<cublasHandle_t>(handle);
@@ -233,8 +233,8 @@ ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t s, const float* 
     const int Kp = b ? biased_pitch(K) : 3 * K;
     const long xb = ((static_cast<long>(M) * Kp * 2 + 255) / 256) * 256;
     const long wb = ((static_cast<long>(N) * Kp * 2 + 255) / 256) * 256;
-    e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), xb + wb, s);
-    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws.base), xb + wb, pool, s);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "workspace allocation"};
     char* p = ws.base;
     const Cat3 xc = carve_pitched(p, M, Kp, PAT_HHL, b ? EXTRA_ONES : EXTRA_NONE, nullptr);
     const Cat3 wc = carve_pitched(p, N, Kp, PAT_HLH, b ? EXTRA_BIAS : EXTRA_NONE, b);
@@ -245,7 +245,7 @@ ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t s, const float* 
     return gemm(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, Kp, wc.p, Kp, xc.p, Kp, 0.f, y, ld_y, gemms);
 }
 
-ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, const float* dy, long ld_dy, const float* w,
+ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, cudaMemPool_t pool, const float* dy, long ld_dy, const float* w,
                             float* dx, long ld_dx, int M, int N, int K, int* launches, int* gemms) {
     if (M == 0 || K == 0) return {};
     cublasHandle_t h = static_cast<cublasHandle_t>(handle);
@@ -256,8 +256,8 @@ ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, const flo
     Workspace ws;
     ws.s = s;
     const long ed = static_cast<long>(M) * N, ew = static_cast<long>(N) * K;
-    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base), cat3_bytes(ed) + cat3_bytes(ew), s);
-    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
+    const cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws.base), cat3_bytes(ed) + cat3_bytes(ew), pool, s);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "workspace allocation"};
     char* p = ws.base;
     // dy' [M][3N] = [dy_hi | dy_hi | dy_lo], w' [3N][K] = [w_hi; w_lo; w_hi].
     const Cat3 dc = carve(p, ed, 0, PAT_HHL), wc = carve(p, ew, 1, PAT_HLH);
@@ -268,7 +268,7 @@ ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t s, const flo
     return gemm(h, CUBLAS_OP_N, CUBLAS_OP_N, K, M, 3 * N, wc.p, K, dc.p, 3 * N, 0.f, dx, ld_dx, gemms);
 }
 
-ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, const float* dy, long ld_dy, const float* x,
+ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, cudaMemPool_t pool, const float* dy, long ld_dy, const float* x,
                             long ld_x, float* dw, float* db, int M, int N, int K, int accumulate, int* launches,
                             int* gemms) {
     if (N == 0) return {};
@@ -279,9 +279,9 @@ ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t s, const flo
     const int R = 64;  // rows per column-sum partial
     const int P = M > 0 ? (M + R - 1) / R : 1;
     const long part_bytes = ((static_cast<long>(P) * N * 4 + 255) / 256) * 256;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws.base),
-                                    cat3_bytes(ed) + cat3_bytes(ex) + (db ? part_bytes : 0), s);
-    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "cudaMallocAsync(workspace)"};
+    cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws.base),
+                                            cat3_bytes(ed) + cat3_bytes(ex) + (db ? part_bytes : 0), pool, s);
+    if (e != cudaSuccess) return {e, CUBLAS_STATUS_SUCCESS, "workspace allocation"};
     char* p = ws.base;
     // x' [3M][K] = [x_hi; x_hi; x_lo], dy' [3M][N] = [dy_hi; dy_lo; dy_hi].
     const Cat3 xc = carve(p, ex, 1, PAT_HHL), dc = carve(p, ed, 1, PAT_HLH);

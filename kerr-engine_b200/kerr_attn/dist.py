@@ -60,18 +60,21 @@ def sync(device=None) -> None:
 
 
 class ProjGradBuckets:
-    """Gradients of the attention projections, one flat bucket per block, all-
-    reduced (sum) across the data-parallel ranks.
+    """Gradients of the attention sublayer's parameters, one flat buffer per
+    block in two all-reduce segments, summed across the data-parallel ranks.
 
-    Bucket i holds block i's c_attn weight [3C][C] and bias [3C], then c_proj's
-    weight [C][C] and bias [C], then ln_1's weight [C] and bias [C]
-    (4C^2 + 6C floats, the reference's attn_c_attn_w / _b, attn_c_proj_w / _b,
-    ln_1_weight / _bias).  ``launch(i)`` starts block i's
-    all-reduce as soon as its backward has been enqueued, so it overlaps the
-    backward of the blocks below it; ``finish()`` waits for every bucket and
-    divides by world * batch_per_rank: the reference sums per-sequence
-    gradients over the batch and divides by batch_size (src/train.rs:257-269),
-    and over ranks the batch is world * batch_per_rank sequences.
+    Block i's buffer holds c_proj's weight [C][C] and bias [C] first (the
+    "proj" segment), then c_attn's weight [3C][C] and bias [3C] and ln_1's
+    weight [C] and bias [C] (the "rest" segment): 4C^2 + 6C floats, the
+    reference's attn_c_proj_w / _b, attn_c_attn_w / _b, ln_1_weight / _bias.
+    The backward of a block produces c_proj's gradients first, so
+    ``launch_proj(i)`` starts that segment's all-reduce as soon as c_proj's
+    dW is enqueued and ``launch(i)`` the rest once the block's backward is;
+    both overlap the backward still to come.  ``finish()`` waits for every
+    segment and divides by world * batch_per_rank: the reference sums
+    per-sequence gradients over the batch and divides by batch_size
+    (src/train.rs:257-269), and over ranks the batch is world *
+    batch_per_rank sequences.
     """
 
     def __init__(self, n_blocks: int, n_embd: int, batch_per_rank: int, device=None):
@@ -81,16 +84,19 @@ class ProjGradBuckets:
         self.n_blocks = n_blocks
         self.batch_per_rank = batch_per_rank
         self.numel = 4 * n_embd * n_embd + 6 * n_embd
+        self.proj_numel = n_embd * n_embd + n_embd
         self.flat = torch.zeros(n_blocks, self.numel, device=device)
         self._work = []
+        self._proj_sent = set()
 
     def views(self, i: int):
         """(c_attn_w [3C, C], c_attn_b [3C], c_proj_w [C, C], c_proj_b [C]) of block i."""
         C = self.C
         f = self.flat[i]
-        a = 3 * C * C
-        return (f[:a].view(3 * C, C), f[a:a + 3 * C], f[a + 3 * C:a + 3 * C + C * C].view(C, C),
-                f[a + 3 * C + C * C:a + 4 * C + C * C])
+        p = C * C
+        a = p + C
+        return (f[a:a + 3 * C * C].view(3 * C, C), f[a + 3 * C * C:a + 3 * C * C + 3 * C], f[:p].view(C, C),
+                f[p:p + C])
 
     def ln_views(self, i: int):
         """(ln_1_w [C], ln_1_b [C]) of block i."""
@@ -102,12 +108,30 @@ class ProjGradBuckets:
     def zero_(self):
         self.flat.zero_()
 
-    def launch(self, i: int):
-        """Start block i's all-reduce (no-op without a process group of >1 ranks)."""
+    @staticmethod
+    def _group():
         import torch.distributed as dist
 
-        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
-            self._work.append(dist.all_reduce(self.flat[i], op=dist.ReduceOp.SUM, async_op=True))
+        return dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+
+    def launch_proj(self, i: int):
+        """Start the all-reduce of block i's c_proj segment (no-op without a
+        process group of more than one rank)."""
+        import torch.distributed as dist
+
+        if self._group():
+            self._work.append(dist.all_reduce(self.flat[i, :self.proj_numel], op=dist.ReduceOp.SUM, async_op=True))
+        self._proj_sent.add(i)
+
+    def launch(self, i: int):
+        """Start the all-reduce of the rest of block i's buffer (all of it if
+        launch_proj(i) was not called)."""
+        import torch.distributed as dist
+
+        start = self.proj_numel if i in self._proj_sent else 0
+        self._proj_sent.discard(i)
+        if self._group():
+            self._work.append(dist.all_reduce(self.flat[i, start:], op=dist.ReduceOp.SUM, async_op=True))
 
     def finish(self) -> int:
         """Wait for every launched all-reduce, then scale to the batch mean.
@@ -117,6 +141,7 @@ class ProjGradBuckets:
         for w in self._work:
             w.wait()
         self._work.clear()
+        self._proj_sent.clear()
         world = dist.get_world_size() if (dist.is_available() and dist.is_initialized()) else 1
         self.flat.mul_(1.0 / (world * self.batch_per_rank))
         return world

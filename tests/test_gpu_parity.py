@@ -13,7 +13,7 @@ import pytest
 import torch
 
 import kerr_attn
-from conftest import make_inputs, rel_err
+from conftest import elem_rel_err, make_inputs, record_errors, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -69,13 +69,18 @@ def oracle_fwd_bwd(oracle_lib, qkv, dout, H):
     return o, lse, dq, dk, dv
 
 
-def assert_parity(got, ref):
+def assert_parity(got, ref, case=""):
+    """Norm-wise relative error (the tolerance measure) of each output, with
+    the elementwise relative error (absolute floor 1e-3 of the largest
+    element) reported beside it and recorded."""
     names = ("o", "lse", "dq", "dk", "dv")
     errs = {n: rel_err(g, r) for n, g, r in zip(names, got, ref)}
+    elem = {f"elem_{n}": elem_rel_err(g, r) for n, g, r in zip(names, got, ref)}
+    record_errors(case, {**errs, **elem})
     for n in names:
         assert np.all(np.isfinite(got[names.index(n)])), n
-    assert errs["o"] < FWD_TOL and errs["lse"] < FWD_TOL, errs
-    assert errs["dq"] < GRAD_TOL and errs["dk"] < GRAD_TOL and errs["dv"] < GRAD_TOL, errs
+    assert errs["o"] < FWD_TOL and errs["lse"] < FWD_TOL, (errs, elem)
+    assert errs["dq"] < GRAD_TOL and errs["dk"] < GRAD_TOL and errs["dv"] < GRAD_TOL, (errs, elem)
     return errs
 
 
@@ -98,7 +103,8 @@ SHAPES = [
 @pytest.mark.parametrize("B,T,H,d", SHAPES)
 def test_parity_with_oracle(ctx, oracle_lib, B, T, H, d, path):
     qkv, dout = make_inputs(B, T, H, d, seed=B * 1000 + T + d)
-    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, path=path), oracle_fwd_bwd(oracle_lib, qkv, dout, H))
+    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, path=path), oracle_fwd_bwd(oracle_lib, qkv, dout, H),
+                  case=f"shape B={B} T={T} H={H} d={d} {path}")
 
 
 @pytest.mark.parametrize("path", ["ffma", "tensor"])
@@ -106,7 +112,7 @@ def test_parity_with_oracle(ctx, oracle_lib, B, T, H, d, path):
 def test_parity_with_golden(ctx, name, path):
     z = np.load(os.path.join(GOLDEN, name))
     got = gpu_fwd_bwd(ctx, z["qkv"], z["dout"], int(z["n_head"]), path=path)
-    assert_parity(got, (z["o"], z["lse"], z["dq"], z["dk"], z["dv"]))
+    assert_parity(got, (z["o"], z["lse"], z["dq"], z["dk"], z["dv"]), case=f"golden {name} {path}")
 
 
 @pytest.mark.parametrize("path", ["ffma", "tensor"])
@@ -117,7 +123,8 @@ def test_full_size_against_oracle(ctx, oracle_lib, B, T, H, d, sigma, path):
     # model's per-layer batch (B=16, H=12, T=256, d=64) at full size; sigma=1
     # gives sharper softmax rows than the 1/sqrt(d) default.
     qkv, dout = make_inputs(B, T, H, d, seed=2024, qkv_sigma=sigma)
-    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, path=path), oracle_fwd_bwd(oracle_lib, qkv, dout, H))
+    assert_parity(gpu_fwd_bwd(ctx, qkv, dout, H, path=path), oracle_fwd_bwd(oracle_lib, qkv, dout, H),
+                  case=f"full B={B} T={T} H={H} d={d} sigma={sigma} {path}")
 
 
 def torch_f64(qkv, dout, H, causal):

@@ -71,10 +71,12 @@ def _bucket_worker(rank, world, port, out):
         g = ProjGradBuckets(blocks, C, batch)
         for i in reversed(range(blocks)):  # the backward walks the blocks top-down
             aw, ab, pw, pb = g.views(i)
-            aw.fill_(rank + 1.0 + i)
-            ab.fill_(10.0 * (rank + 1))
             pw.fill_(-1.0 * (rank + 1))
             pb.fill_(float(i))
+            if i % 2 == 0:  # c_proj's segment sent first on even blocks, with the rest on odd ones
+                g.launch_proj(i)
+            aw.fill_(rank + 1.0 + i)
+            ab.fill_(10.0 * (rank + 1))
             lw, lb = g.ln_views(i)
             lw.fill_(2.0 * (rank + 1))
             lb.fill_(-float(i) * (rank + 1))
