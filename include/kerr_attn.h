@@ -92,6 +92,21 @@ int kattn_destroy(kattn_ctx* ctx);
  * KATTN_ERR_INVALID_ARGUMENT for an unknown value. */
 int kattn_set_path(kattn_ctx* ctx, int path);
 
+/* Wall-time limit, in nanoseconds, of every bounded wait inside the
+ * tensor-core kernels launched on this context from now on (0 restores the
+ * default of one second).  A kernel whose wait runs out sets the context's
+ * device status word, frees its tensor memory and returns; kattn_check_device
+ * then reports KATTN_ERR_DEVICE_TIMEOUT.  No counterpart in the reference,
+ * whose GPU backend panics on device errors (src/gpu_ops_forward.rs:63). */
+int kattn_set_wait_limit(kattn_ctx* ctx, unsigned long long ns);
+
+/* Diagnostic for the bounded waits: the next tensor-core forward launched on
+ * this context issues no copy of its first key tile, so the waits on that
+ * tile run out after the wait limit and the kernel unwinds as above (its
+ * outputs are undefined).  Later calls run normally.  For tests of the
+ * timeout path; no counterpart in the reference. */
+int kattn_test_withhold_next_load(kattn_ctx* ctx);
+
 /* Waits for the context's device to finish its work and reports whether any
  * kernel gave up a bounded wait since the last check (KATTN_ERR_DEVICE_TIMEOUT,
  * after which results of the affected calls are undefined); clears the flag. */

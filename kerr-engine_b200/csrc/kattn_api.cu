@@ -17,6 +17,8 @@
 #include "kattn_launch.h"
 #include "kerr_attn.h"
 
+constexpr unsigned long long kDefaultWaitNs = 1000000000ull;  // one second
+
 struct kattn_ctx {
     int device = 0;
     int num_sms = 0;
@@ -31,6 +33,8 @@ struct kattn_ctx {
     size_t arena_bytes = 0;
     float* noalloc_ws = nullptr;    // device address of g_noalloc_ws on this device
     cudaMemPool_t pool = nullptr;   // the context's own stream-ordered pool for per-call workspace
+    std::atomic<unsigned long long> wait_ns{kDefaultWaitNs};  // limit of the kernels' bounded waits
+    std::atomic<int> withhold_next_load{0};  // diagnostic hook (kattn_test_withhold_next_load)
     void* cublas = nullptr;         // cublasHandle_t of the projection GEMMs, created on first use
     std::mutex proj_mu;             // binds the handle to a stream and enqueues a call as one step
 };
@@ -168,18 +172,27 @@ int ok_with_launches(int n) {
     return KATTN_OK;
 }
 
-// Forward launch on the kernel family the context selects.
+// Forward launch on the kernel family the context selects, with the
+// context's wait limit (and, once, its diagnostic hook) on the tensor path.
 cudaError_t dispatch_fwd(kattn_ctx* ctx, const kattn::FwdArgs& a, cudaStream_t s, int* launches) {
     const int path = ctx->path.load(std::memory_order_relaxed);
-    if (path != KATTN_PATH_FFMA && kattn::fwd_tc_supported(a)) return kattn::launch_fwd_tc(a, ctx->num_sms, ctx->d_status, s, launches);
+    if (path != KATTN_PATH_FFMA && kattn::fwd_tc_supported(a)) {
+        kattn::FwdArgs b = a;
+        b.wait_ns = ctx->wait_ns.load(std::memory_order_relaxed);
+        b.withhold_first_key_load = ctx->withhold_next_load.exchange(0);
+        return kattn::launch_fwd_tc(b, ctx->num_sms, ctx->d_status, s, launches);
+    }
     return kattn::launch_fwd(a, ctx->num_sms, s, launches);
 }
 
 // Backward launch on the kernel family the context selects.
 cudaError_t dispatch_bwd(kattn_ctx* ctx, const kattn::BwdArgs& a, cudaStream_t s, int* launches) {
     const int path = ctx->path.load(std::memory_order_relaxed);
-    if (path != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a))
-        return kattn::launch_bwd_tc(a, ctx->num_sms, ctx->d_status, s, launches);
+    if (path != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a)) {
+        kattn::BwdArgs b = a;
+        b.wait_ns = ctx->wait_ns.load(std::memory_order_relaxed);
+        return kattn::launch_bwd_tc(b, ctx->num_sms, ctx->d_status, s, launches);
+    }
     return kattn::launch_bwd(a, ctx->num_sms, s, launches);
 }
 
@@ -546,6 +559,18 @@ int kattn_set_path(kattn_ctx* ctx, int path) {
     if (path != KATTN_PATH_AUTO && path != KATTN_PATH_FFMA && path != KATTN_PATH_TENSOR)
         return fail(KATTN_ERR_INVALID_ARGUMENT, "unknown path %d", path);
     ctx->path.store(path);
+    return KATTN_OK;
+}
+
+int kattn_set_wait_limit(kattn_ctx* ctx, unsigned long long ns) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    ctx->wait_ns.store(ns == 0 ? kDefaultWaitNs : ns);
+    return KATTN_OK;
+}
+
+int kattn_test_withhold_next_load(kattn_ctx* ctx) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    ctx->withhold_next_load.store(1);
     return KATTN_OK;
 }
 

@@ -121,6 +121,7 @@ struct Params {
     int n_ktiles;  // 128-row key tiles
     int n_qtiles;  // 64-row query tiles
     int n_work;    // work items: n_ktiles * B * H
+    unsigned long long wait_ns;  // wall-time limit of every bounded wait
 };
 
 // The r-th work item of CTA c in a grid of G: the snake order over the item
@@ -311,7 +312,7 @@ __device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm
         stg_k[row * 16 + ((8 * hf + i) ^ (row & 15))] =
             make_float4(a[4 * i] * p.scale, a[4 * i + 1] * p.scale, a[4 * i + 2] * p.scale, a[4 * i + 3] * p.scale);
     mbar_arrive(&sm.stg_full);
-    if (!mbar_wait_warp(&sm.stg_full, r & 1)) return false;
+    if (!mbar_wait_warp(&sm.stg_full, r & 1, p.wait_ns)) return false;
     const long row0 = static_cast<long>(it.b) * p.T + it.k0;
     float* dvg = p.dv + row0 * p.ld_d + it.h * D;
     float* dkg = p.dk + row0 * p.ld_d + it.h * D;
@@ -328,7 +329,7 @@ __device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm
         }
     }
     mbar_arrive(&sm.stg_done);  // staging reads done before the next tile's dS^T writes
-    return mbar_wait_warp(&sm.stg_done, r & 1);
+    return mbar_wait_warp(&sm.stg_done, r & 1, p.wait_ns);
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
@@ -403,7 +404,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         for (int n = 0; !failed; ++n) {
             if (cl.valid()) {
                 const int s = n % STAGES;
-                if (n >= STAGES && !mbar_wait_warp(&sm.empty[s], ((n - STAGES) / STAGES) & 1)) {
+                if (n >= STAGES && !mbar_wait_warp(&sm.empty[s], ((n - STAGES) / STAGES) & 1, p.wait_ns)) {
                     failed = true;  // warp-uniform: the dQ epilogue below is warp-collective
                     break;
                 }
@@ -420,7 +421,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
             if (n >= 2) {
                 if (!cq.valid()) break;
                 const int m = n - 2;
-                if (!mbar_wait_warp(&sm.bar_d[m & 1], (m >> 1) & 1)) {
+                if (!mbar_wait_warp(&sm.bar_d[m & 1], (m >> 1) & 1, p.wait_ns)) {
                     failed = true;
                     break;
                 }
@@ -482,7 +483,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 } else {
                     const uint64_t now = globaltimer_ns();
                     if (t_idle == 0) t_idle = now;
-                    else if (now - t_idle > 1000000000ull) failed = true;
+                    else if (now - t_idle > p.wait_ns) failed = true;
                     __nanosleep(20);
                 }
             }
@@ -512,12 +513,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 const int buf = g & 1;     // TMEM / dS buffer
                 const int q0 = (it.it0 + n) * BQ;
                 // full[s]: the loaders' lse / D writes for this tile are visible.
-                if (!mbar_wait_warp(&sm.bar_s[buf], (g >> 1) & 1) ||
-                    !mbar_wait_warp(&sm.full[s], (g / STAGES) & 1)) {
+                if (!mbar_wait_warp(&sm.bar_s[buf], (g >> 1) & 1, p.wait_ns) ||
+                    !mbar_wait_warp(&sm.full[s], (g / STAGES) & 1, p.wait_ns)) {
                     failed = true;
                     break;
                 }
-                if (g >= 2 && !mbar_wait_warp(&sm.bar_d[buf], ((g - 2) >> 1) & 1)) {
+                if (g >= 2 && !mbar_wait_warp(&sm.bar_d[buf], ((g - 2) >> 1) & 1, p.wait_ns)) {
                     failed = true;  // dS^T buffer `buf` is read by tile g-2's dQ product
                     break;
                 }
@@ -597,7 +598,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 tc::Rows2<BK, NELEM> kv;
                 kv.load(p.k + base * p.ld_qkv + nx.h * D, p.ld_qkv, p.v + base * p.ld_qkv + nx.h * D, p.ld_qkv,
                         nx.k0, p.T, tid);
-                if (!mbar_wait_warp(&sm.kv_free, r & 1)) {
+                if (!mbar_wait_warp(&sm.kv_free, r & 1, p.wait_ns)) {
                     failed = true;
                     break;
                 }
@@ -606,7 +607,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 mbar_arrive(&sm.kv_full);
             }
             const int gl_ = g - 1;  // this item's last tile
-            if (!mbar_wait_warp(&sm.bar_d[gl_ & 1], (gl_ >> 1) & 1)) {
+            if (!mbar_wait_warp(&sm.bar_d[gl_ & 1], (gl_ >> 1) & 1, p.wait_ns)) {
                 failed = true;
                 break;
             }
@@ -647,6 +648,7 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     p.dv = a.dv;
     p.ld_d = a.ld_d;
     p.status = status;
+    p.wait_ns = a.wait_ns;
     p.B = a.B;
     p.T = a.T;
     p.H = a.H;

@@ -113,6 +113,8 @@ struct alignas(64) Params {
     int n_qtiles;
     int n_ktiles;
     int n_work;  // items: n_qtiles * B * H
+    unsigned long long wait_ns;  // wall-time limit of every bounded wait
+    int withhold_first_key_load;  // diagnostic: no copy of the first key tile is issued
 };
 
 // Item round r of CTA c: item w = r*G + (r odd ? G-1-c : c) of the list
@@ -293,7 +295,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                     // issue slots to the softmax warps.
                     const uint64_t now = globaltimer_ns();
                     if (t_idle == 0) t_idle = now;
-                    else if (now - t_idle > 1000000000ull) failed = true;
+                    else if (now - t_idle > p.wait_ns) failed = true;
                     __nanosleep(IDLE_NS);
                 }
             }
@@ -332,7 +334,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 bool progressed = false;
                 if (kq.valid() && (gk < 2 || mbar_test_wait(&sm.bar_s[gk & 1], ((gk - 2) >> 1) & 1))) {
                     const int sl = kq.slab(p);
-                    load_tile(p.tk, sm.k[gk & 1], &sm.k_full[gk & 1], KV_BYTES, sl % p.H, kq.j * BN, sl / p.H);
+                    if (gk != 0 || !p.withhold_first_key_load)
+                        load_tile(p.tk, sm.k[gk & 1], &sm.k_full[gk & 1], KV_BYTES, sl % p.H, kq.j * BN, sl / p.H);
                     ++gk;
                     kq.next(p, cta, G);
                     progressed = true;
@@ -365,7 +368,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                     // issue slots to the softmax warps.
                     const uint64_t now = globaltimer_ns();
                     if (t_idle == 0) t_idle = now;
-                    else if (now - t_idle > 1000000000ull) failed = true;
+                    else if (now - t_idle > p.wait_ns) failed = true;
                     __nanosleep(IDLE_NS);
                 }
             }
@@ -402,7 +405,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
         // from swizzled box hf into TMEM lane rl.  Every S of the item before
         // has completed (the caller waited for the last one).
         auto load_q = [&](int rq) {
-            bad |= !mbar_wait(&sm.q_full, rq & 1);
+            bad |= !mbar_wait(&sm.q_full, rq & 1, p.wait_ns);
             const uint8_t* box = sm.q + hf * Q_BOX_BYTES + rl * 128;
             uint32_t qh[16], ql[16];
 #pragma unroll
@@ -434,7 +437,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
             // previous item's last tile, so their first S runs meanwhile.
             if (g == 0) {
                 tc::RawTile<BN, NSM> kr;
-                bad |= !mbar_wait(&sm.k_full[0], 0);
+                bad |= !mbar_wait(&sm.k_full[0], 0, p.wait_ns);
                 kr.read(sm.k[0], tid);
                 if (named_sync_or(1, NSM, bad)) {
                     failed = true;
@@ -456,7 +459,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 if (j + 1 < n_kv || has_next) {
                     const int gn = g + 1;
                     tc::RawTile<BN, NSM> kr;
-                    bad |= !mbar_wait(&sm.k_full[gn & 1], (gn >> 1) & 1);
+                    bad |= !mbar_wait(&sm.k_full[gn & 1], (gn >> 1) & 1, p.wait_ns);
                     kr.read(sm.k[gn & 1], tid);
                     if (named_sync_or(1, NSM, bad)) {
                         failed = true;
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 // -inf, eight independent chains), combined with the other
                 // half's; then the probabilities, packed bf16 hi / lo over the
                 // 32 S columns just read (hi in the first 16, lo in the next).
-                bad |= !mbar_wait(&sm.bar_s[bf], (g >> 1) & 1);
+                bad |= !mbar_wait(&sm.bar_s[bf], (g >> 1) & 1, p.wait_ns);
                 tc_fence_after();
                 // The item's last S is done, so its Q columns are free: move
                 // the next item's Q in now (its first S then runs during this
@@ -534,7 +537,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 // and V_g are ready for PV_g.
                 if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                     const int gp = g - 1;
-                    bad |= !mbar_wait(&sm.bar_o[gp & 1], (gp >> 1) & 1);
+                    bad |= !mbar_wait(&sm.bar_o[gp & 1], (gp >> 1) & 1, p.wait_ns);
                     tc_fence_after();
 #pragma unroll
                     for (int c = 0; c < 32; c += 16) {
@@ -550,7 +553,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 tmem_wait_st();
                 {
                     tc::RawTile<BN, NSM> vr;
-                    bad |= !mbar_wait(&sm.v_full[bf], (g >> 1) & 1);
+                    bad |= !mbar_wait(&sm.v_full[bf], (g >> 1) & 1, p.wait_ns);
                     vr.read(sm.v[bf], tid);
                     if (named_sync_or(1, NSM, bad)) {
                         failed = true;
@@ -570,7 +573,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
             // rows at a time, float4 chunks XOR-swizzled by row, so that the
             // global stores are whole 256-byte rows.
             const int gl = g - 1;
-            bad |= !mbar_wait(&sm.bar_o[gl & 1], (gl >> 1) & 1);
+            bad |= !mbar_wait(&sm.bar_o[gl & 1], (gl >> 1) & 1, p.wait_ns);
             tc_fence_after();
             sm.red[0][hf][rl] = l;
             if (named_sync_or(1, NSM, bad)) {
@@ -678,6 +681,8 @@ cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream
     p.ld_o = a.ld_o;
     p.lse = a.lse;
     p.status = status;
+    p.wait_ns = a.wait_ns;
+    p.withhold_first_key_load = a.withhold_first_key_load;
     p.B = a.B;
     p.T = a.T;
     p.H = a.H;

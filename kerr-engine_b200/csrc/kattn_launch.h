@@ -37,6 +37,11 @@ struct FwdArgs {
     int B, T, H, d;
     float scale;
     int causal;
+    // Wall-time limit of every bounded wait in the tensor-core kernels.
+    unsigned long long wait_ns = 1000000000ull;
+    // Diagnostic (kattn_test_withhold_next_load): the tensor-core forward
+    // issues no copy of its first key tile, so its waits on it run out.
+    int withhold_first_key_load = 0;
 };
 
 struct BwdArgs {
@@ -56,6 +61,7 @@ struct BwdArgs {
     int B, T, H, d;
     float scale;
     int causal;
+    unsigned long long wait_ns = 1000000000ull;  // wall-time limit of every bounded wait
 };
 
 // Each returns the CUDA launch status and adds the number of kernels it

@@ -111,8 +111,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
 
 // mbar_wait with a warp-uniform outcome (required before warp-collective
 // tcgen05.ld / st): true only if every lane of the warp saw the phase complete.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
-    const bool ok = mbar_wait(bar, parity);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 1000000000ull) {
+    const bool ok = mbar_wait(bar, parity, limit_ns);
     return __all_sync(0xffffffffu, ok);
 }
 

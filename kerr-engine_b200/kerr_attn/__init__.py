@@ -37,7 +37,7 @@ PATH_TENSOR = 2
 # Every function include/kerr_attn.h declares.
 EXPORTED_SYMBOLS = (
     "kattn_version", "kattn_strerror", "kattn_last_error", "kattn_create", "kattn_destroy",
-    "kattn_set_path", "kattn_check_device",
+    "kattn_set_path", "kattn_check_device", "kattn_set_wait_limit", "kattn_test_withhold_next_load",
     "kattn_fwd", "kattn_bwd", "kattn_fwd_host", "kattn_bwd_host", "kattn_last_launch_count",
     "kattn_bwd_noalloc",
     "kattn_linear_fwd", "kattn_linear_bwd_dx", "kattn_linear_bwd_dw",
@@ -95,6 +95,10 @@ def lib():
     L.kattn_set_path.restype = _i
     L.kattn_check_device.argtypes = [_p]
     L.kattn_check_device.restype = _i
+    L.kattn_set_wait_limit.argtypes = [_p, ctypes.c_ulonglong]
+    L.kattn_set_wait_limit.restype = _i
+    L.kattn_test_withhold_next_load.argtypes = [_p]
+    L.kattn_test_withhold_next_load.restype = _i
     fwd_args = [_p, _p, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _fl, _i]
     bwd_args = [_p, _p, _p, _p, _l, _p, _p, _l, _p, _p, _p, _p, _l, _i, _i, _i, _i, _fl, _i]
     L.kattn_fwd.argtypes = fwd_args + [_p]
@@ -174,6 +178,15 @@ class Context:
     def check_device(self):
         """Synchronise the device; raise if a kernel gave up a bounded wait."""
         _check(lib().kattn_check_device(self._h), "kattn_check_device")
+
+    def set_wait_limit(self, ns: int):
+        """Wall-time limit of the tensor-core kernels' bounded waits (0: one second)."""
+        _check(lib().kattn_set_wait_limit(self._h, int(ns)), "kattn_set_wait_limit")
+
+    def test_withhold_next_load(self):
+        """Diagnostic: the next tensor-core forward withholds its first key-tile
+        copy, so its bounded waits run out (kattn_test_withhold_next_load)."""
+        _check(lib().kattn_test_withhold_next_load(self._h), "kattn_test_withhold_next_load")
 
     def close(self):
         if self._h is not None and self._h.value:

@@ -248,3 +248,22 @@ def test_training_loop_on_the_oracle_descends(oracle_lib):
     losses = train_stack.train_oracle(blocks, h0, target, 2, 8, 0.03)
     assert all(np.isfinite(losses))
     assert all(b < a for a, b in zip(losses, losses[1:]))
+
+
+def test_model128_harness_on_the_oracle(oracle_lib):
+    # The oracle arm of the 128-dim model's training run (tests/model128.py):
+    # the reference's initialisation draws every weight inside its limit, the
+    # first loss is near ln 65 (uniform over the symbols) and a few Adam
+    # steps lower it.
+    import math
+
+    import model128
+
+    blocks, top = model128.init_model(42)
+    lim = 1 / math.sqrt(model128.N_EMBD)
+    assert np.abs(blocks[0]["wa"]).max() <= lim and np.abs(top["lm_head"]).max() <= lim
+    assert np.abs(blocks[0]["band_w"]).max() <= 1 / math.sqrt(2) and "band_w" not in blocks[1]
+    assert model128.active_bands(0) == 8 and model128.active_bands(998) == 8 and model128.active_bands(999) == 24
+    losses = model128.train_oracle(4)
+    assert abs(losses[0] - math.log(model128.VOCAB)) < 0.5
+    assert losses[-1] < losses[0]
