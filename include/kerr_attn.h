@@ -33,8 +33,9 @@
  *     thread.
  *   - kattn_fwd / kattn_bwd only enqueue work on `stream` (a cudaStream_t,
  *     NULL = legacy default stream) and never synchronise the host.
- *     kattn_bwd takes a [B][H][T] float workspace on that stream from a
- *     stream-ordered memory pool the context owns and returns it there.
+ *     On the FFMA kernels kattn_bwd takes a [B][H][T] float workspace on
+ *     that stream from a stream-ordered memory pool the context owns and
+ *     returns it there (the tensor-core kernels need none).
  *   - Workspace pool: each context creates its own pool (cudaMemPoolCreate)
  *     on its device.  Freed blocks stay cached in it until kattn_destroy
  *     (at most the largest workspace that calls in flight held at once);
@@ -202,8 +203,8 @@ int kattn_bwd_host_saved(kattn_ctx* ctx, const kattn_saved* saved,
                          float* dq, float* dk, float* dv, long ld_dqkv);
 
 /* Number of kernel launches the last kattn_fwd / kattn_bwd call on this
- * thread enqueued (0 for an empty problem or an error).  For the
- * kattn_linear_* calls: this library's kernels, not the cuBLAS GEMMs. */
+ * thread enqueued (0 for an empty problem or an error); the same for every
+ * other entry point below. */
 int kattn_last_launch_count(void);
 
 /* ---- Attention projections c_attn / c_proj (dense layers) -----------------
@@ -213,10 +214,10 @@ int kattn_last_launch_count(void);
  * :353 and :695-737.  Rows are positions (M = B*T); weights keep the
  * reference's [out][in] layout (src/model.rs:184-185): w is [N][K]
  * contiguous.  Device pointers, 16-byte aligned; every row stride and K, N
- * a multiple of 4 floats.  Each product is formed in bf16 hi/lo pairs
- * (hi*hi + hi*lo + lo*hi, f32 accumulation; ~1e-5 relative) by one cuBLAS
- * GEMM over a threefold contraction of operands this library splits and
- * concatenates.  Workspace comes from the
+ * a multiple of 4 floats; b and db need only 4-byte alignment.  Each product
+ * is formed in bf16 hi/lo pairs (hi*hi + hi*lo + lo*hi, f32 accumulation;
+ * ~1e-5 relative) by this library's tcgen05 GEMM, which splits the f32
+ * operands on chip.  Split-K and column-sum workspace comes from the
  * context's stream-ordered pool; nothing synchronises the host. */
 
 /* y[m][n] = b[n] + sum_k w[n][k] x[m][k];  b may be NULL (no bias). */

@@ -1,6 +1,5 @@
 // C ABI of the attention path (include/kerr_attn.h): argument checking,
 // device contexts, workspace handling and the host-buffer entry points.
-#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <climits>
@@ -35,8 +34,6 @@ struct kattn_ctx {
     cudaMemPool_t pool = nullptr;   // the context's own stream-ordered pool for per-call workspace
     std::atomic<unsigned long long> wait_ns{kDefaultWaitNs};  // limit of the kernels' bounded waits
     std::atomic<int> withhold_next_load{0};  // diagnostic hook (kattn_test_withhold_next_load)
-    void* cublas = nullptr;         // cublasHandle_t of the projection GEMMs, created on first use
-    std::mutex proj_mu;             // binds the handle to a stream and enqueues a call as one step
 };
 
 // Device-resident state of one forward (the reference's AttnCache):
@@ -221,24 +218,8 @@ int check_dims(int M, int N, int K) {
     return KATTN_OK;
 }
 
-// The context's cuBLAS handle bound to `stream` (created on first use; the
-// caller holds proj_mu and has the context's device current).
-int proj_handle(kattn_ctx* ctx, cudaStream_t stream, void** out) {
-    if (!ctx->cublas) {
-        cublasHandle_t h = nullptr;
-        const cublasStatus_t st = cublasCreate(&h);
-        if (st != CUBLAS_STATUS_SUCCESS) return fail(KATTN_ERR_CUDA, "cublasCreate: status %d", static_cast<int>(st));
-        ctx->cublas = h;
-    }
-    const cublasStatus_t st = cublasSetStream(static_cast<cublasHandle_t>(ctx->cublas), stream);
-    if (st != CUBLAS_STATUS_SUCCESS) return fail(KATTN_ERR_CUDA, "cublasSetStream: status %d", static_cast<int>(st));
-    *out = ctx->cublas;
-    return KATTN_OK;
-}
-
 int proj_result(const kattn::ProjStatus& st, int launches) {
     if (st.cuda != cudaSuccess) return cuda_fail(st.cuda, st.what);
-    if (st.cublas != 0) return fail(KATTN_ERR_CUDA, "%s: cuBLAS status %d", st.what, st.cublas);
     return ok_with_launches(launches);
 }
 
@@ -545,7 +526,6 @@ int kattn_destroy(kattn_ctx* ctx) {
         for (cudaEvent_t ev : ctx->events) cudaEventDestroy(ev);
         if (ctx->arena) cudaFree(ctx->arena);
         if (ctx->d_status) cudaFree(ctx->d_status);
-        if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
         // Blocks still owed to the pool by work in flight on callers' streams
         // are released by the driver once that work frees them.
         if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
@@ -613,14 +593,19 @@ int kattn_bwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, lo
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    float* dsum = nullptr;
-    const size_t ws = sizeof(float) * static_cast<size_t>(B) * H * T;
-    cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&dsum), ws, ctx->pool, s);
-    if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
-    kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, dsum, B, T, H, d, scale, causal};
+    kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, nullptr, B, T, H, d, scale, causal};
+    // The FFMA kernels stage D = rowsum(dout * o) in a [B][H][T] workspace;
+    // the tensor-core kernel forms it on chip and needs none.
+    const bool tensor = ctx->path.load(std::memory_order_relaxed) != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a);
+    cudaError_t e = cudaSuccess;
+    if (!tensor) {
+        const size_t ws = sizeof(float) * static_cast<size_t>(B) * H * T;
+        e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&a.dsum), ws, ctx->pool, s);
+        if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
+    }
     int launches = 0;
     e = dispatch_bwd(ctx, a, s, &launches);
-    cudaError_t ef = cudaFreeAsync(dsum, s);
+    const cudaError_t ef = a.dsum ? cudaFreeAsync(a.dsum, s) : cudaSuccess;
     if (e != cudaSuccess) return cuda_fail(e, "backward launch");
     if (ef != cudaSuccess) return cuda_fail(ef, "cudaFreeAsync(workspace)");
     return ok_with_launches(launches);
@@ -816,13 +801,10 @@ int kattn_linear_fwd(kattn_ctx* ctx, const float* x, long ld_x, const float* w, 
     if (M == 0 || N == 0) return ok_with_launches(0);
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
-    std::lock_guard<std::mutex> lock(ctx->proj_mu);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    void* h = nullptr;
-    KATTN_TRY(proj_handle(ctx, s, &h));
-    int launches = 0, gemms = 0;
-    const kattn::ProjStatus st =
-        kattn::proj_forward(h, ctx->num_sms, s, ctx->pool, x, ld_x, w, b, y, ld_y, M, N, K, &launches, &gemms);
+    int launches = 0;
+    const kattn::ProjStatus st = kattn::proj_forward(ctx->num_sms, s, ctx->pool, ctx->d_status, ctx->wait_ns.load(),
+                                                     x, ld_x, w, b, y, ld_y, M, N, K, &launches);
     return proj_result(st, launches);
 }
 
@@ -837,13 +819,11 @@ int kattn_linear_bwd_dx(kattn_ctx* ctx, const float* dy, long ld_dy, const float
     if (M == 0 || K == 0) return ok_with_launches(0);
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
-    std::lock_guard<std::mutex> lock(ctx->proj_mu);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    void* h = nullptr;
-    KATTN_TRY(proj_handle(ctx, s, &h));
-    int launches = 0, gemms = 0;
-    const kattn::ProjStatus st =
-        kattn::proj_backward_dx(h, ctx->num_sms, s, ctx->pool, dy, ld_dy, w, dx, ld_dx, M, N, K, &launches, &gemms);
+    int launches = 0;
+    const kattn::ProjStatus st = kattn::proj_backward_dx(ctx->num_sms, s, ctx->pool, ctx->d_status,
+                                                         ctx->wait_ns.load(), dy, ld_dy, w, dx, ld_dx, M, N, K,
+                                                         &launches);
     return proj_result(st, launches);
 }
 
@@ -859,13 +839,11 @@ int kattn_linear_bwd_dw(kattn_ctx* ctx, const float* dy, long ld_dy, const float
     if (N == 0 || (K == 0 && !db)) return ok_with_launches(0);
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
-    std::lock_guard<std::mutex> lock(ctx->proj_mu);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    void* h = nullptr;
-    KATTN_TRY(proj_handle(ctx, s, &h));
-    int launches = 0, gemms = 0;
-    const kattn::ProjStatus st = kattn::proj_backward_dw(h, ctx->num_sms, s, ctx->pool, dy, ld_dy, x, ld_x, dw, db, M, N, K,
-                                                         accumulate, &launches, &gemms);
+    int launches = 0;
+    const kattn::ProjStatus st = kattn::proj_backward_dw(ctx->num_sms, s, ctx->pool, ctx->d_status,
+                                                         ctx->wait_ns.load(), dy, ld_dy, x, ld_x, dw, db, M, N, K,
+                                                         accumulate, &launches);
     return proj_result(st, launches);
 }
 

@@ -47,6 +47,7 @@
 #include "kattn_launch.h"
 #include "sm100.cuh"
 #include "tc_tiles.cuh"
+#include "tma_map.h"
 
 namespace kattn {
 using namespace sm100;
@@ -649,10 +650,8 @@ EncodeTiled encode_tiled() {
     return fn;
 }
 
-// The first H*64 columns of a [B*T][ld] f32 buffer as a 3-D tensor
-// {columns, T rows, B}, boxes of `box_cols` columns x `box_rows` rows of one batch
-// (rows past T are out of bounds and read as zeros).  `base` is 16-byte
-// aligned and ld a multiple of 4 (checked at the C ABI).
+}  // namespace
+
 bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int H, int box_cols, int box_rows,
                  CUtensorMapSwizzle swizzle) {
     const EncodeTiled fn = encode_tiled();
@@ -667,7 +666,17 @@ bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
+bool encode_2d(CUtensorMap* map, const float* base, long cols, long rows, long ld, int box_cols, int box_rows) {
+    const EncodeTiled fn = encode_tiled();
+    if (fn == nullptr || cols <= 0 || rows <= 0) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 bool fwd_tc_supported(const FwdArgs& a) { return a.d == 64; }
 

@@ -79,25 +79,35 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
 // D = rowsum(dout * o) into a.dsum and dq = 0 (first kernel of every backward).
 cudaError_t launch_bwd_prep(const BwdArgs& a, int num_sms, cudaStream_t stream, int* launches);
 
-// Projection GEMMs (kproj.cu).  The outcome of a call: a CUDA error, or a
-// cuBLAS status (cublasStatus_t as int), with the step that failed.
+// The outcome of a call of the projection, LayerNorm and Kerr-ODE launchers:
+// a CUDA error with the step that failed, or success.
 struct ProjStatus {
     cudaError_t cuda = cudaSuccess;
-    int cublas = 0;
     const char* what = nullptr;
-    bool ok() const { return cuda == cudaSuccess && cublas == 0; }
+    bool ok() const { return cuda == cudaSuccess; }
 };
 
-// `handle` is a cublasHandle_t already bound to `stream`.  Arrays are
-// row-major f32; w is [N][K] contiguous, dw [N][K] contiguous.  *launches
-// counts this library's kernels, *gemms the cuBLAS GEMM calls.
-ProjStatus proj_forward(void* handle, int num_sms, cudaStream_t stream, cudaMemPool_t pool, const float* x, long ld_x, const float* w,
-                        const float* b, float* y, long ld_y, int M, int N, int K, int* launches, int* gemms);
-ProjStatus proj_backward_dx(void* handle, int num_sms, cudaStream_t stream, cudaMemPool_t pool, const float* dy, long ld_dy,
-                            const float* w, float* dx, long ld_dx, int M, int N, int K, int* launches, int* gemms);
-ProjStatus proj_backward_dw(void* handle, int num_sms, cudaStream_t stream, cudaMemPool_t pool, const float* dy, long ld_dy,
-                            const float* x, long ld_x, float* dw, float* db, int M, int N, int K, int accumulate,
-                            int* launches, int* gemms);
+// C (+)= A B^T on the tensor cores (kgemm.cu): C[m][n] = (accumulate ? C : 0)
+// + bias[n] + sum_k A(m, k) B(n, k) for m < M, n < N, k < K, the products in
+// bf16 hi / lo pairs split on chip.  A(m, k) = a[m*lda + k] (K-major) or
+// a[k*lda + m] (a_mn); B(n, k) likewise with b_mn.  Row-major f32, 16-byte
+// aligned, every ld and N a multiple of 4 floats.  Split-K workspace comes
+// from `pool`; `status` is the device word set when a bounded wait runs out.
+ProjStatus gemm_tc(cudaStream_t s, cudaMemPool_t pool, int num_sms, const float* a, long lda, bool a_mn,
+                   const float* b, long ldb, bool b_mn, float* c, long ldc, const float* bias, int M, int N, int K,
+                   int accumulate, int* status, unsigned long long wait_ns, int* launches);
+
+// Projection layers (kproj.cu).  Arrays are row-major f32; w is [N][K]
+// contiguous, dw [N][K] contiguous.  *launches counts the kernels enqueued.
+ProjStatus proj_forward(int num_sms, cudaStream_t s, cudaMemPool_t pool, int* status, unsigned long long wait_ns,
+                        const float* x, long ld_x, const float* w, const float* b, float* y, long ld_y, int M, int N,
+                        int K, int* launches);
+ProjStatus proj_backward_dx(int num_sms, cudaStream_t s, cudaMemPool_t pool, int* status, unsigned long long wait_ns,
+                            const float* dy, long ld_dy, const float* w, float* dx, long ld_dx, int M, int N, int K,
+                            int* launches);
+ProjStatus proj_backward_dw(int num_sms, cudaStream_t s, cudaMemPool_t pool, int* status, unsigned long long wait_ns,
+                            const float* dy, long ld_dy, const float* x, long ld_x, float* dw, float* db, int M, int N,
+                            int K, int accumulate, int* launches);
 
 // LayerNorm over rows of n floats (kln.cu), eps 1e-5.  n a multiple of 4,
 // at most LN_MAX_N; rows 16-byte aligned.  w, b, dw, db have n floats.

@@ -84,6 +84,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int c0, 
         : "memory");
 }
 
+// Tiled 2-D load of one box of `map` at coordinates (c0 innermost, c1) into
+// this CTA's shared memory, completing its bytes on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Brings a tensor map (address of a __grid_constant__ parameter) into the
 // TMA unit's descriptor cache ahead of its first copy.
 __device__ __forceinline__ void prefetch_tensormap(const void* map) {

@@ -144,5 +144,40 @@ struct RawTile {
     }
 };
 
+// A raw f32 tile of R rows x C floats (row-major, C*4 bytes per row, as a
+// TMA box lands it) whose columns run along an operand's M or N dimension and
+// whose rows run along K -> the same bytes rewritten as bf16 hi (first
+// R*C*2 bytes) and lo halves in the MN-major 128B-swizzled UMMA layout: C/64
+// atoms of R rows x 128 bytes, atom a holding columns 64a..64a+63, atoms
+// R*128 bytes apart (the descriptor's leading-byte offset).  Same read /
+// barrier / write protocol as RawTile.
+template <int R, int C, int NTH>
+struct RawTileMN {
+    static_assert(C % 64 == 0 && (R * C / 4) % NTH == 0, "tile items must divide evenly");
+    static constexpr int F4_PER_ROW = C / 4;
+    static constexpr int ITEMS = R * C / 4 / NTH;
+    float4 a[ITEMS];
+
+    __device__ __forceinline__ void read(const uint8_t* tile, int t) {
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) a[it] = reinterpret_cast<const float4*>(tile)[t + it * NTH];
+    }
+
+    __device__ __forceinline__ void write(uint8_t* tile, int t) const {
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+            const int f = t + it * NTH;
+            const int r = f / F4_PER_ROW;
+            const int col = 4 * (f - r * F4_PER_ROW);
+            uint2 h, l;
+            sm100::split2(a[it].x, a[it].y, h.x, l.x);
+            sm100::split2(a[it].z, a[it].w, h.y, l.y);
+            const uint32_t off = (col >> 6) * (R * 128) + sm100::sw128(r, (col & 63) >> 3) + ((col >> 2) & 1) * 8;
+            *reinterpret_cast<uint2*>(tile + off) = h;
+            *reinterpret_cast<uint2*>(tile + (C / 64) * R * 128 + off) = l;
+        }
+    }
+};
+
 }  // namespace tc
 }  // namespace kattn

@@ -40,11 +40,14 @@ def inputs(M, N, K, seed):
     return x, w, b, dy
 
 
-# (M, N, K): the 128-dim model's c_attn and c_proj (B=4, T=64), the 768-dim
-# model's (B=16, T=256), the 1280-dim model's c_attn (B=32, T=512), and a
-# ragged shape.
-SHAPES = [(256, 384, 128), (256, 128, 128), (4096, 2304, 768), (4096, 768, 768), (16384, 3840, 1280),
-          (100, 52, 36)]
+# (M, N, K): the 128-dim model's c_attn and c_proj (B=4, T=64), its maestro
+# squeeze / process_1 (maestro_dim 16) and padded lm_head (68 rows), the
+# 768-dim model's c_attn and c_proj (B=16, T=256), the 1280-dim model's
+# c_attn (B=32, T=512), and ragged shapes (edges of the 128 x 256 x 64 GEMM
+# tiles on every side, single rows, K below one stage).
+SHAPES = [(256, 384, 128), (256, 128, 128), (256, 16, 128), (256, 128, 16), (256, 68, 128),
+          (4096, 2304, 768), (4096, 768, 768), (16384, 3840, 1280),
+          (100, 52, 36), (1, 4, 4), (3, 8, 260), (300, 260, 70)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)

@@ -91,8 +91,10 @@ def test_noalloc_takes_no_device_memory():
     # The entry point's promise: no device memory is allocated by the call.
     # After one call (which loads the kernels), three more calls leave the
     # device's free memory unchanged, while kattn_bwd on the same fresh
-    # context (whose workspace pool starts empty) visibly reserves some.
+    # context (whose workspace pool starts empty) visibly reserves some.  The
+    # FFMA kernels are the ones with a [B][H][T] workspace.
     with kerr_attn.Context(0) as ctx:
+        ctx.set_path(kerr_attn.PATH_FFMA)
         H = 5
         q, k, v, o, lse, dout = _setup(6, 190, H, 64, seed=11)
         kerr_attn.fwd(ctx, q, k, v, o, lse, H)
