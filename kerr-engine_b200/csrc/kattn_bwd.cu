@@ -54,9 +54,12 @@ constexpr int ROWDOT_U = 1;
 
 template <int D>
 __global__ void __launch_bounds__(256) attn_bwd_rowdot(const BwdParams p) {
-    // The backward kernel behind this one may launch at once: its threads
-    // that read D or dq wait for this grid, and this grid finishes only
-    // after the grid before it (the one that wrote o) has.
+    // The backward kernel behind this one may launch at once: it waits for
+    // this grid before it reads D or dq, and this grid finishes only after
+    // the grid before it (the one that wrote o) has.  D must be written only
+    // after this wait: kattn_bwd_noalloc hands every call the same workspace
+    // array, and the previous call's backward kernel, which reads it, is (or
+    // precedes) the grid waited for here.
     pdl_launch();
     pdl_wait();
     constexpr int LPR = D / 4;

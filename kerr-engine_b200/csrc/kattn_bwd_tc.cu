@@ -103,7 +103,7 @@ struct alignas(1024) Smem {
     float lse2[STAGES][BQ];  // lse * log2(e), +inf beyond T
     float dsum[STAGES][BQ];  // D, 0 beyond T
     uint64_t kv_full;    // K / V of the CTA's item r landed (phase r&1)
-    uint64_t kv_read;    // every elementwise thread holds its share of the raw K / V (phase r&1)
+    uint64_t kv_read;    // every elementwise thread holds its share of the raw K, then of V (phases 2r, 2r+1)
     uint64_t kv_ready;   // K / V of item r converted
     uint64_t kv_free;    // item r's last dQ product done: K / V may be replaced
     uint64_t q_full[STAGES];   // Q / dO of a tile landed
@@ -329,7 +329,7 @@ __device__ __forceinline__ void store_dkv(const Params& p, uint32_t tm, const It
     }
 }
 
-__global__ void __maxnreg__(144) attn_bwd_tc64(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_constant__ Params p) {
     // Launched behind attn_bwd_zero_dq, which waited for every earlier grid
     // before letting this one launch: all inputs are final.  Only the dq
     // reductions wait for the clearing.
@@ -387,13 +387,16 @@ __global__ void __maxnreg__(144) attn_bwd_tc64(const __grid_constant__ Params p)
             prefetch_tensormap(&p.tdo);
             Cursor cq;
             cq.start(p, c, G);
+            int n_items = 0;  // this CTA's items
+            while (item_id(c, n_items, G) < p.n_work) ++n_items;
             int nq = 0, rkv = 0;  // query tiles / items whose copies were issued
             uint64_t t_idle = 0;
-            while (!failed && cq.valid()) {
+            while (!failed && (cq.valid() || rkv < n_items)) {
                 bool progressed = false;
-                // The next item's K / V (items are loaded in order, at most
-                // one ahead of the query tiles).
-                if (rkv <= cq.r && (rkv == 0 || mbar_test_wait(&sm.kv_free, (rkv - 1) & 1))) {
+                // The next item's K / V (items are loaded in order, never
+                // ahead of the item whose query tiles are being loaded).
+                if (rkv < n_items && (!cq.valid() || rkv <= cq.r) &&
+                    (rkv == 0 || mbar_test_wait(&sm.kv_free, (rkv - 1) & 1))) {
                     const Item it = make_item(p, item_id(c, rkv, G));
                     mbar_arrive_expect_tx(&sm.kv_full, 2 * KV_BYTES);
                     tma_load_3d(sm.k, &p.tk, it.h * D, it.k0, it.b, &sm.kv_full);
@@ -402,7 +405,7 @@ __global__ void __maxnreg__(144) attn_bwd_tc64(const __grid_constant__ Params p)
                     progressed = true;
                 }
                 const int s = nq % STAGES;
-                if (nq < STAGES || mbar_test_wait(&sm.empty[s], ((nq - STAGES) / STAGES) & 1)) {
+                if (cq.valid() && (nq < STAGES || mbar_test_wait(&sm.empty[s], ((nq - STAGES) / STAGES) & 1))) {
                     const Item it = make_item(p, cq.w);
                     const int q0 = (cq.it0 + cq.n) * BQ;
                     mbar_arrive_expect_tx(&sm.q_full[s], 2 * QT_BYTES);
@@ -534,19 +537,23 @@ __global__ void __maxnreg__(144) attn_bwd_tc64(const __grid_constant__ Params p)
                     failed = true;
                     break;
                 }
-                tc::RawTile<BQ, NSTG> qr, gr;
-                qr.read(qt, t);
-                gr.read(gt, t);
-                // D of this thread's rows (t >> 4) + 8 i: the 16 threads of a
-                // half-warp hold one row between them.
+                // D of this thread's rows (t >> 4) + 8 i from the raw dO in
+                // shared memory and the O registers: the 16 threads of a
+                // half-warp hold one row between them.  Done before the raw
+                // tiles are read for conversion, so O and the tiles are not
+                // live in registers at once.
 #pragma unroll
                 for (int i = 0; i < QI; ++i) {
-                    float dv = gr.a[i].x * ov[i].x + gr.a[i].y * ov[i].y + gr.a[i].z * ov[i].z + gr.a[i].w * ov[i].w;
+                    const float4 g = reinterpret_cast<const float4*>(gt)[t + i * NSTG];
+                    float dv = g.x * ov[i].x + g.y * ov[i].y + g.z * ov[i].z + g.w * ov[i].w;
 #pragma unroll
                     for (int off = 8; off > 0; off >>= 1) dv += __shfl_xor_sync(0xffffffffu, dv, off);
                     if ((t & 15) == 0) sm.dsum[s][(t >> 4) + 8 * i] = dv;
                 }
                 if (t < BQ) sm.lse2[s][t] = lse_t;
+                tc::RawTile<BQ, NSTG> qr, gr;
+                qr.read(qt, t);
+                gr.read(gt, t);
                 // Converted in place: every thread has read its share first.
                 mbar_arrive(&sm.q_read[s]);
                 if (!mbar_wait_warp(&sm.q_read[s], (n / STAGES) & 1, p.wait_ns)) {
@@ -601,16 +608,21 @@ __global__ void __maxnreg__(144) attn_bwd_tc64(const __grid_constant__ Params p)
                     failed = true;
                     break;
                 }
-                tc::RawTile<BK, NELEM> kr, vr;
-                kr.read(sm.k, tid);
-                vr.read(sm.v, tid);
-                mbar_arrive(&sm.kv_read);
-                if (!mbar_wait_warp(&sm.kv_read, r & 1, p.wait_ns)) {
+                // K, then V: kv_read completes twice per item (phases 2r, 2r+1).
+                bool ok = true;
+#pragma unroll 1
+                for (int u = 0; u < 2 && ok; ++u) {
+                    uint8_t* tile = u ? sm.v : sm.k;
+                    tc::RawTile<BK, NELEM> kr;
+                    kr.read(tile, tid);
+                    mbar_arrive(&sm.kv_read);
+                    ok = mbar_wait_warp(&sm.kv_read, u, p.wait_ns);
+                    if (ok) kr.write(tile, 1.f, tid);
+                }
+                if (!ok) {
                     failed = true;
                     break;
                 }
-                kr.write(sm.k, 1.f, tid);
-                vr.write(sm.v, 1.f, tid);
                 fence_async_smem();
                 mbar_arrive(&sm.kv_ready);
             }

@@ -333,6 +333,18 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
             uint64_t t_idle = 0;
             while (!failed && (kq.valid() || vq.valid() || qq.valid())) {
                 bool progressed = false;
+                // Q first: an item's first S needs Q and K_0, and at kernel
+                // start every CTA's copies queue up at once.
+                if (qq.valid() && (qq.r == 0 || mbar_test_wait(&sm.q_ready, (qq.r - 1) & 1))) {
+                    const int sl = qq.slab(p);
+                    const int q0 = (p.n_qtiles - 1 - qq.w / (p.B * p.H)) * BM;
+                    mbar_arrive_expect_tx(&sm.q_full, Q_BYTES);
+                    tma_load_3d(sm.q, &p.tq, (sl % p.H) * D, q0, sl / p.H, &sm.q_full);
+                    tma_load_3d(sm.q + Q_BOX_BYTES, &p.tq, (sl % p.H) * D + 32, q0, sl / p.H, &sm.q_full);
+                    ++qq.r;
+                    qq.set(p, cta, G);
+                    progressed = true;
+                }
                 if (kq.valid() && (gk < 2 || mbar_test_wait(&sm.bar_s[gk & 1], ((gk - 2) >> 1) & 1))) {
                     const int sl = kq.slab(p);
                     if (gk != 0 || !p.withhold_first_key_load)
@@ -350,16 +362,6 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                     load_tile(p.tv, sm.v[gv & 1], &sm.v_full[gv & 1], KV_BYTES, sl % p.H, vq.j * BN, sl / p.H);
                     ++gv;
                     vq.next(p, cta, G);
-                    progressed = true;
-                }
-                if (qq.valid() && (qq.r == 0 || mbar_test_wait(&sm.q_ready, (qq.r - 1) & 1))) {
-                    const int sl = qq.slab(p);
-                    const int q0 = (p.n_qtiles - 1 - qq.w / (p.B * p.H)) * BM;
-                    mbar_arrive_expect_tx(&sm.q_full, Q_BYTES);
-                    tma_load_3d(sm.q, &p.tq, (sl % p.H) * D, q0, sl / p.H, &sm.q_full);
-                    tma_load_3d(sm.q + Q_BOX_BYTES, &p.tq, (sl % p.H) * D + 32, q0, sl / p.H, &sm.q_full);
-                    ++qq.r;
-                    qq.set(p, cta, G);
                     progressed = true;
                 }
                 if (progressed) {

@@ -63,7 +63,8 @@ struct alignas(1024) GSmem {
     uint8_t b[G_STAGES][B_BYTES];
     float epi[NEPI / 32][32 * EPI_PITCH];  // per epilogue warp: 32 rows x 32 columns
     uint64_t full[G_STAGES];    // stage landed
-    uint64_t read[G_STAGES];    // every converter thread holds its share of the raw stage
+    uint64_t read_a[G_STAGES];  // every converter thread holds its share of the raw A tile
+    uint64_t read_b[G_STAGES];  // ... of the raw B tile
     uint64_t ready[G_STAGES];   // stage converted
     uint64_t empty[G_STAGES];   // stage's MMAs done
     uint64_t acc_full[2];       // accumulator b complete
@@ -105,7 +106,7 @@ __device__ __forceinline__ Unit make_unit(const GParams& p, int u) {
 }
 
 template <bool A_MN, bool B_MN>
-__global__ void __maxnreg__(144) gemm_bf16x3(const __grid_constant__ GParams p) {
+__global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constant__ GParams p) {
     pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     GSmem& sm = *reinterpret_cast<GSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -122,7 +123,8 @@ __global__ void __maxnreg__(144) gemm_bf16x3(const __grid_constant__ GParams p) 
     if (tid == 0) {
         for (int i = 0; i < G_STAGES; ++i) {
             mbar_init(&sm.full[i], 1);
-            mbar_init(&sm.read[i], NCONV);
+            mbar_init(&sm.read_a[i], NCONV);
+            mbar_init(&sm.read_b[i], NCONV);
             mbar_init(&sm.ready[i], NCONV);
             mbar_init(&sm.empty[i], 1);
         }
@@ -288,22 +290,34 @@ __global__ void __maxnreg__(144) gemm_bf16x3(const __grid_constant__ GParams p) 
                     failed = true;
                     break;
                 }
-                // A: [128][64] K-major or [64][128] MN-major; B: [256][64] or [64][256].
+                // A: [128][64] K-major or [64][128] MN-major; B: [256][64] or
+                // [64][256].  Each tile is rewritten in place once every
+                // thread has read its share of it; A first, then B, so that
+                // only one tile's share is live in registers at a time.
                 using ATile = typename std::conditional<A_MN, tc::RawTileMN<GK, GM, NCONV>, tc::RawTile<GM, NCONV>>::type;
                 using BTile = typename std::conditional<B_MN, tc::RawTileMN<GK, GN, NCONV>, tc::RawTile<GN, NCONV>>::type;
-                ATile ta;
-                BTile tb;
-                ta.read(sm.a[s], tid);
-                tb.read(sm.b[s], tid);
-                mbar_arrive(&sm.read[s]);
-                if (!mbar_wait_warp(&sm.read[s], ph, p.wait_ns)) {
-                    failed = true;
-                    break;
+                {
+                    ATile ta;
+                    ta.read(sm.a[s], tid);
+                    mbar_arrive(&sm.read_a[s]);
+                    if (!mbar_wait_warp(&sm.read_a[s], ph, p.wait_ns)) {
+                        failed = true;
+                        break;
+                    }
+                    if constexpr (A_MN) ta.write(sm.a[s], tid);
+                    else ta.write(sm.a[s], 1.f, tid);
                 }
-                if constexpr (A_MN) ta.write(sm.a[s], tid);
-                else ta.write(sm.a[s], 1.f, tid);
-                if constexpr (B_MN) tb.write(sm.b[s], tid);
-                else tb.write(sm.b[s], 1.f, tid);
+                {
+                    BTile tb;
+                    tb.read(sm.b[s], tid);
+                    mbar_arrive(&sm.read_b[s]);
+                    if (!mbar_wait_warp(&sm.read_b[s], ph, p.wait_ns)) {
+                        failed = true;
+                        break;
+                    }
+                    if constexpr (B_MN) tb.write(sm.b[s], tid);
+                    else tb.write(sm.b[s], 1.f, tid);
+                }
                 fence_async_smem();
                 mbar_arrive(&sm.ready[s]);
             }
