@@ -33,9 +33,8 @@
  *     thread.
  *   - kattn_fwd / kattn_bwd only enqueue work on `stream` (a cudaStream_t,
  *     NULL = legacy default stream) and never synchronise the host.
- *     On the FFMA kernels kattn_bwd takes a [B][H][T] float workspace on
- *     that stream from a stream-ordered memory pool the context owns and
- *     returns it there (the tensor-core kernels need none).
+ *     kattn_bwd takes a [B][H][T] float workspace on that stream from a
+ *     stream-ordered memory pool the context owns and returns it there.
  *   - Workspace pool: each context creates its own pool (cudaMemPoolCreate)
  *     on its device.  Freed blocks stay cached in it until kattn_destroy
  *     (at most the largest workspace that calls in flight held at once);

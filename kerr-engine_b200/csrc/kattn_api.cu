@@ -594,15 +594,10 @@ int kattn_bwd(kattn_ctx* ctx, const float* q, const float* k, const float* v, lo
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, nullptr, B, T, H, d, scale, causal};
-    // The FFMA kernels stage D = rowsum(dout * o) in a [B][H][T] workspace;
-    // the tensor-core kernel forms it on chip and needs none.
-    const bool tensor = ctx->path.load(std::memory_order_relaxed) != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a);
-    cudaError_t e = cudaSuccess;
-    if (!tensor) {
-        const size_t ws = sizeof(float) * static_cast<size_t>(B) * H * T;
-        e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&a.dsum), ws, ctx->pool, s);
-        if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
-    }
+    // D = rowsum(dout * o) is staged in a [B][H][T] workspace.
+    const size_t ws = sizeof(float) * static_cast<size_t>(B) * H * T;
+    cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&a.dsum), ws, ctx->pool, s);
+    if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
     int launches = 0;
     e = dispatch_bwd(ctx, a, s, &launches);
     const cudaError_t ef = a.dsum ? cudaFreeAsync(a.dsum, s) : cudaSuccess;

@@ -4,18 +4,12 @@
 // attn_backward_scores / attn_backward_dkv), recomputing the probabilities
 // from the forward's log-sum-exp instead of reading a cached [H][T][T] P.
 //
-// Two launches: attn_bwd_zero_dq clears dq (dQ is accumulated with vector
-// reductions), then attn_bwd_tc64 does everything else, including
-// D = rowsum(dO * O) (the reference's sum_j att[j] * d_att[j],
-// src/backward.rs:501), which it forms while it converts each dO tile.
-//
 // Work item = one 128-row key tile of one (batch, head) slab: K, V and the
 // dK, dV accumulators stay resident while the item walks the 64-row query
 // tiles on or below the diagonal.  The kernel is persistent (one CTA per SM):
 // CTA c takes items c, 2G-1-c, 2G+c, ... of the list ordered longest first
 // (a snake order, which evens out the tile counts per CTA), and its query
-// tiles form one pipeline across item boundaries.  Products (bf16x3:
-// hi*hi + hi*lo + lo*hi, f32 accumulation):
+// tiles form one pipeline across item boundaries.  Products (bf16x3: hi*hi + hi*lo + lo*hi, f32 accumulation):
 //   S^T  = K Q^T      M=128 (keys) N=64 (queries)   SS, both K-major
 //   dP^T = V dO^T     M=128 N=64                    SS, both K-major
 //   P = exp2(S^T * scale*log2e - lse*log2e),  dS = P * (dP^T - D)   (threads)
@@ -23,24 +17,24 @@
 //   dK  += dS^T Q     M=128 N=64 K=64    TS: dS from TMEM, Q MN-major
 //   dQ_i = dS K       M=64  N=64 K=128   SS: dS^T (shared) read MN-major, K MN-major;
 //                     added into global dq with vector reductions.
+// D = rowsum(dO * O) and the zeroed dq come from attn_bwd_rowdot.
 //
-// Loads are TMA copies of raw f32 tiles (3-D tensor maps over
-// [B][T][columns]; rows past T read zeros), converted in place into bf16
-// hi / lo halves in the 128B-swizzled UMMA layout: an item's K and V by the
-// elementwise warps, each query tile's Q and dO by the stage warps.
-//
-// Warp roles (448 threads, one CTA per SM):
+// Warp roles (416 threads, one CTA per SM):
 //   warps 0-7   elementwise.  Warp w reads TMEM lanes 32*(w%4).. (key rows)
-//               and query columns 32*(w/4)..+31 of each 64-column tile and
-//               writes P and dS.  At an item's start they convert its K / V.
-//   warps 8-11  stage warps: per query tile, convert Q and dO, form D from
-//               dO and O (O read from global, one tile ahead), and stage lse;
-//               then add tile n-1's finished dQ into dq; at an item's end
-//               they store its dK / dV straight from TMEM, so the elementwise
-//               warps go on with the next item meanwhile.
-//   warp 12     one lane issues every tcgen05.mma and commit, in whichever
-//               order its inputs become ready.
-//   warp 13     one lane issues every TMA copy as soon as its buffer is free.
+//               and query columns 32*(w/4)..+31 of each 64-column tile; at
+//               the end of an item it stores its half of the dK / dV rows.
+//               They also stage K / V: the next item's rows are loaded into
+//               registers at the end of an item and written to shared memory
+//               as soon as the item's last dQ product (the last reader of K)
+//               is done, while the tensor core still runs its dV / dK.
+//   warps 8-11  loaders: Q, dO, lse, D per query tile into a 3-stage ring;
+//               they also add each finished dQ tile into dq (reductions), so
+//               that wait stays off the elementwise warps.
+//   warp 12     one lane issues every tcgen05.mma and commit, from
+//               descriptors built once, in whichever order its inputs become
+//               ready (a tile's S^T / dP^T as soon as the tile is loaded and
+//               its TMEM buffer is free; a tile's gradients as soon as its P
+//               and dS are written).
 // Everything a query tile touches is double-buffered (S^T / dP^T in TMEM,
 // dS^T in shared memory, the dQ accumulator in TMEM), so the tensor core runs
 // tile i's gradient products while the elementwise warps work on tile i+1.
@@ -48,38 +42,26 @@
 // 16c..16c+15, bf16 hi goes to columns 16c..16c+7 and lo to 16c+8..16c+15,
 // which the owning warp has already read; the tensor core runs one thread's
 // MMAs in issue order, so the next S^T lands only after dV / dK read them.
-//
-// Every wait is bounded (p.wait_ns of wall time) and every hand-off inside a
-// warp group is an mbarrier, never a named barrier, so a role whose wait runs
-// out can leave its loop without stranding the others: they run out at their
-// next wait.  Copies and MMAs in flight are drained (bounded) before the
-// tensor memory is freed, and the device status word is set.
-#include <cuda.h>
-
-#include <algorithm>
 #include <atomic>
 
 #include "kattn_common.cuh"
 #include "kattn_launch.h"
 #include "sm100.cuh"
 #include "tc_tiles.cuh"
-#include "tma_map.h"
 
 namespace kattn {
 using namespace sm100;
 
 namespace {
 
-constexpr int BK = 128;  // key rows per item
+constexpr int BK = 128;  // key rows per CTA
 constexpr int BQ = 64;   // query rows per tile
 constexpr int D = 64;
 constexpr int NELEM = 256;  // elementwise threads (warps 0-7)
-constexpr int NSTG = 128;   // stage threads (warps 8-11)
-constexpr int MMA_WARP = (NELEM + NSTG) / 32;
-constexpr int TMA_WARP = MMA_WARP + 1;
-constexpr int NTHREADS = NELEM + NSTG + 64;
+constexpr int NLOAD = 128;  // loader threads (warps 8-11)
+constexpr int NTHREADS = NELEM + NLOAD + 32;
+constexpr int MMA_WARP = (NELEM + NLOAD) / 32;
 constexpr int STAGES = 3;  // query-tile ring depth (Q, dO, lse, D)
-constexpr unsigned long long DRAIN_NS = 10000000ull;  // drain waits after a failure
 
 // TMEM columns (512 allocated).  Buffer b: S^T (then P packed) at col_s(b),
 // dP^T (then dS packed) at col_dp(b), dQ tile (M=64 layout) at col_dq(b).
@@ -90,42 +72,43 @@ constexpr uint32_t COL_DV = 384;
 constexpr uint32_t COL_DK = 448;
 constexpr uint32_t TMEM_COLS = 512;
 
-constexpr uint32_t KV_BYTES = BK * 256;  // one raw f32 K or V tile; later hi (first half) | lo
-constexpr uint32_t QT_BYTES = BQ * 256;  // one raw f32 Q or dO tile; later hi | lo
-constexpr uint32_t STAGE_BYTES = 2 * QT_BYTES;
-
 struct alignas(1024) Smem {
-    uint8_t k[KV_BYTES];
-    uint8_t v[KV_BYTES];
-    uint8_t qg[STAGES][STAGE_BYTES];  // ring stage: Q tile, then dO tile
-    uint8_t sh[2][BK * 128];          // dS^T [key][64 queries], per TMEM buffer
+    uint8_t kh[BK * 128];  // [key][64 bf16], 128B swizzle
+    uint8_t kl[BK * 128];
+    uint8_t vh[BK * 128];
+    uint8_t vl[BK * 128];
+    uint8_t qh[STAGES][BQ * 128];  // [query][64 bf16]
+    uint8_t ql[STAGES][BQ * 128];
+    uint8_t gh[STAGES][BQ * 128];  // dO
+    uint8_t gl[STAGES][BQ * 128];
+    uint8_t sh[2][BK * 128];  // dS^T [key][64 queries], per TMEM buffer
     uint8_t sl[2][BK * 128];
     float lse2[STAGES][BQ];  // lse * log2(e), +inf beyond T
     float dsum[STAGES][BQ];  // D, 0 beyond T
-    uint64_t kv_full;    // K / V of the CTA's item r landed (phase r&1)
-    uint64_t kv_read;    // every elementwise thread holds its share of the raw K, then of V (phases 2r, 2r+1)
-    uint64_t kv_ready;   // K / V of item r converted
-    uint64_t kv_free;    // item r's last dQ product done: K / V may be replaced
-    uint64_t q_full[STAGES];   // Q / dO of a tile landed
-    uint64_t q_read[STAGES];   // every stage thread holds its share of the raw Q / dO
-    uint64_t q_ready[STAGES];  // Q / dO converted, lse and D staged
-    uint64_t empty[STAGES];    // gradient products of the tile in the stage done
-    uint64_t bar_s[2];    // S^T / dP^T of the tile in TMEM buffer b done
+    uint64_t kv_full;  // an item's K / V staged (phase r: the CTA's item r)
+    uint64_t kv_free;  // an item's last dQ product done: K / V may be replaced
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t bar_s[2];
     uint64_t pds[2];      // P / dS of the tile in buffer b written
     uint64_t bar_d[2];    // gradient products of the tile in buffer b done
-    uint64_t dq_free[2];  // dQ accumulator b read out by the stage warps
-    uint64_t dkv_free;    // dK / dV of item r stored (phase r&1)
-    uint64_t drain;       // MMAs drained after a failure
+    uint64_t dq_free[2];  // dQ accumulator b read out by the loaders
+    uint64_t stg_full;    // dK / dV staging written (phase r: item r)
+    uint64_t stg_done;    // dK / dV staging stored to global
     uint32_t tmem_slot;
 };
 
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory (plus alignment slack) exceeds 227 KB");
 
-struct alignas(64) Params {
-    CUtensorMap tq, tk, tv, tdo;  // {H*64 columns, T rows, B} f32; boxes {64, BQ, 1} (q, dO), {64, BK, 1} (k, v)
-    const float* o;
+struct Params {
+    const float* q;
+    const float* k;
+    const float* v;
+    long ld_qkv;
+    const float* dout;
     long ld_o;
     const float* lse;
+    const float* dsum;
     float* dq;
     float* dk;
     float* dv;
@@ -189,21 +172,22 @@ struct Cursor {
         }
     }
     __device__ __forceinline__ bool valid() const { return w >= 0; }
-    __device__ __forceinline__ bool last_of_item() const { return n + 1 == n_it; }
 };
 
-// Shared-memory descriptors, built once by the issuing thread.  A K-major
-// k-step advances 32 bytes inside the swizzled row; an MN-major k-step
-// advances 16 rows (2048 bytes).  The K-major and MN-major descriptors of one
-// tile differ only in the leading-byte offset.
+// Shared-memory descriptors, built once by the issuing thread (two ring
+// stages / two buffers, selected without indexing so they stay in registers).
+// A K-major k-step advances 32 bytes inside the swizzled row; an MN-major
+// k-step advances 16 rows (2048 bytes).  The K-major and MN-major
+// descriptors of one tile differ only in the leading-byte offset.
 struct Descs {
     uint64_t kh, kl, vh, vl;      // K / V, K-major (S^T, dP^T A operands)
     uint64_t kh_mn, kl_mn;        // K, MN-major (dQ B operand)
-    uint64_t qh, ql, gh, gl;      // Q / dO of ring stage 0, K-major; stage s is STAGE_BYTES * s further
+    uint64_t qh, ql, gh, gl;      // Q / dO ring stage 0, K-major; stage s is STAGE_BYTES * s further
     uint64_t s0h, s0l, s1h, s1l;  // dS^T buffer 0 / 1, MN-major (dQ A)
 };
 
-constexpr uint32_t MN_LBO_Q = BQ * 128;  // leading-byte offset of a 64-row MN-major tile
+constexpr uint32_t STAGE_BYTES = BQ * 128;  // one stage of one Q / dO tile
+constexpr uint32_t MN_LBO_Q = BQ * 128;     // leading-byte offset of a 64-row MN-major tile
 constexpr uint32_t MN_LBO_K = BK * 128;
 
 __device__ __forceinline__ uint64_t as_mn(uint64_t kdesc, uint32_t lbo) {
@@ -211,16 +195,16 @@ __device__ __forceinline__ uint64_t as_mn(uint64_t kdesc, uint32_t lbo) {
 }
 
 __device__ __forceinline__ void make_descs(const Smem& sm, Descs& d) {
-    d.kh = smem_desc(smem_u32(sm.k), 16, 1024);
-    d.kl = smem_desc(smem_u32(sm.k + BK * 128), 16, 1024);
-    d.vh = smem_desc(smem_u32(sm.v), 16, 1024);
-    d.vl = smem_desc(smem_u32(sm.v + BK * 128), 16, 1024);
+    d.kh = smem_desc(smem_u32(sm.kh), 16, 1024);
+    d.kl = smem_desc(smem_u32(sm.kl), 16, 1024);
+    d.vh = smem_desc(smem_u32(sm.vh), 16, 1024);
+    d.vl = smem_desc(smem_u32(sm.vl), 16, 1024);
     d.kh_mn = as_mn(d.kh, MN_LBO_K);
     d.kl_mn = as_mn(d.kl, MN_LBO_K);
-    d.qh = smem_desc(smem_u32(sm.qg[0]), 16, 1024);
-    d.ql = smem_desc(smem_u32(sm.qg[0] + BQ * 128), 16, 1024);
-    d.gh = smem_desc(smem_u32(sm.qg[0] + QT_BYTES), 16, 1024);
-    d.gl = smem_desc(smem_u32(sm.qg[0] + QT_BYTES + BQ * 128), 16, 1024);
+    d.qh = smem_desc(smem_u32(sm.qh[0]), 16, 1024);
+    d.ql = smem_desc(smem_u32(sm.ql[0]), 16, 1024);
+    d.gh = smem_desc(smem_u32(sm.gh[0]), 16, 1024);
+    d.gl = smem_desc(smem_u32(sm.gl[0]), 16, 1024);
     d.s0h = smem_desc(smem_u32(sm.sh[0]), MN_LBO_K, 1024);
     d.s0l = smem_desc(smem_u32(sm.sl[0]), MN_LBO_K, 1024);
     d.s1h = smem_desc(smem_u32(sm.sh[1]), MN_LBO_K, 1024);
@@ -281,8 +265,8 @@ __device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, in
 }
 
 // A dQ tile (M=64 accumulator: query row 16*qd + l sits in lane 32*qd + l,
-// l < 16), scaled and added into dq by the stage warp of lane quadrant qd,
-// 32 columns at a time.  The TMEM loads run on every lane (warp-collective).
+// l < 16), scaled and added into dq by the loader warp of lane quadrant qd,
+// 32 columns at a time.
 __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int lane, int q0,
                                             float* dqg) {
     const uint32_t ta = (static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b);
@@ -302,37 +286,56 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
     }
 }
 
-// dK, dV of an item -> global, by the stage warp of lane quadrant qd: key row
-// k0 + 32*qd + lane, 32 columns per TMEM load (warp-collective), stored as
-// that row's float4s.
-__device__ __forceinline__ void store_dkv(const Params& p, uint32_t tm, const Item& it, int qd, int lane) {
-    const uint32_t lb = static_cast<uint32_t>(qd * 32) << 16;
-    const int row = it.k0 + qd * 32 + lane;
-    const long g = (static_cast<long>(it.b) * p.T + row) * p.ld_d + it.h * D;
+// dK, dV of the CTA's item r -> global, by the elementwise warps.  Warp
+// (qd, hf) reads its 32 key rows x 32 columns of each accumulator (TMEM loads
+// are warp-collective and run on every lane) into the idle dS^T buffers, laid
+// out [row][16 float4] with the float4 index XOR-swizzled by row; then the 256
+// threads store whole 256-byte rows, two per warp instruction.  Rows past T
+// are not stored.  The dS^T buffers are free: the item's last dQ product has
+// completed and the next item's tiles are written by these same warps after
+// the second barrier.  The barriers are mbarriers with bounded waits, so a
+// warp that gave up earlier cannot leave the others blocked.
+__device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm, const Item& it, uint32_t lb,
+                                          int row, int hf, int tid, int r) {
+    float4* stg_v = reinterpret_cast<float4*>(sm.sh[0]);  // 128 rows x 256 B = 32 KB (sh[0], sh[1])
+    float4* stg_k = reinterpret_cast<float4*>(sm.sl[0]);
+    float a[32];
+    tmem_ld32(lb + tm + COL_DV + 32 * hf, a);
+    tmem_wait_ld();
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const uint32_t col = t ? COL_DK : COL_DV;
-        float* dst = (t ? p.dk : p.dv) + g;
-        const float mul = t ? p.scale : 1.f;
+    for (int i = 0; i < 8; ++i)
+        stg_v[row * 16 + ((8 * hf + i) ^ (row & 15))] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
+    tmem_ld32(lb + tm + COL_DK + 32 * hf, a);
+    tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float a[32];
-            tmem_ld32(lb + tm + col + 32 * h, a);
-            tmem_wait_ld();
-            if (row < p.T) {
+    for (int i = 0; i < 8; ++i)
+        stg_k[row * 16 + ((8 * hf + i) ^ (row & 15))] =
+            make_float4(a[4 * i] * p.scale, a[4 * i + 1] * p.scale, a[4 * i + 2] * p.scale, a[4 * i + 3] * p.scale);
+    mbar_arrive(&sm.stg_full);
+    if (!mbar_wait_warp(&sm.stg_full, r & 1, p.wait_ns)) return false;
+    const long row0 = static_cast<long>(it.b) * p.T + it.k0;
+    float* dvg = p.dv + row0 * p.ld_d + it.h * D;
+    float* dkg = p.dk + row0 * p.ld_d + it.h * D;
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    *reinterpret_cast<float4*>(dst + 32 * h + 4 * i) =
-                        make_float4(a[4 * i] * mul, a[4 * i + 1] * mul, a[4 * i + 2] * mul, a[4 * i + 3] * mul);
-            }
+    for (int k = 0; k < BK * 16 / NELEM; ++k) {
+        const int i = tid + k * NELEM;
+        const int r = i >> 4;
+        const int c4 = i & 15;
+        if (it.k0 + r < p.T) {
+            const float4 v = stg_v[r * 16 + (c4 ^ (r & 15))];
+            const float4 g = stg_k[r * 16 + (c4 ^ (r & 15))];
+            *reinterpret_cast<float4*>(dvg + r * p.ld_d + c4 * 4) = v;
+            *reinterpret_cast<float4*>(dkg + r * p.ld_d + c4 * 4) = g;
         }
     }
+    mbar_arrive(&sm.stg_done);  // staging reads done before the next tile's dS^T writes
+    return mbar_wait_warp(&sm.stg_done, r & 1, p.wait_ns);
 }
 
-__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_constant__ Params p) {
-    // Launched behind attn_bwd_zero_dq, which waited for every earlier grid
-    // before letting this one launch: all inputs are final.  Only the dq
-    // reductions wait for the clearing.
+__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
+    // Launched behind attn_bwd_rowdot, whose outputs (D, the zeroed dq) only
+    // the loader warps touch: they wait for it; the elementwise warps stage
+    // the first item's K / V meanwhile.
     pdl_launch();
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -348,25 +351,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_consta
         tmem_relinquish();
     }
     if (tid == 0) {
-        mbar_init(&sm.kv_full, 1);
-        mbar_init(&sm.kv_read, NELEM);
-        mbar_init(&sm.kv_ready, NELEM);
+        mbar_init(&sm.kv_full, NELEM);
         mbar_init(&sm.kv_free, 1);
         for (int i = 0; i < STAGES; ++i) {
-            mbar_init(&sm.q_full[i], 1);
-            mbar_init(&sm.q_read[i], NSTG);
-            mbar_init(&sm.q_ready[i], NSTG);
+            mbar_init(&sm.full[i], NLOAD);
             mbar_init(&sm.empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.bar_s[i], 1);
-            mbar_init(&sm.pds[i], NELEM);
             mbar_init(&sm.bar_d[i], 1);
-            mbar_init(&sm.dq_free[i], NSTG);
+            mbar_init(&sm.dq_free[i], NLOAD);
         }
-        mbar_init(&sm.dkv_free, NSTG);
-        mbar_init(&sm.drain, 1);
-        fence_barrier_init();
+        mbar_init(&sm.pds[0], NELEM);
+        mbar_init(&sm.pds[1], NELEM);
+        mbar_init(&sm.stg_full, NELEM);
+        mbar_init(&sm.stg_done, NELEM);
     }
     tc_fence_before();
     __syncthreads();
@@ -374,77 +373,77 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_consta
     const uint32_t tm = sm.tmem_slot;
     bool failed = false;
 
-    if (warp == TMA_WARP) {
-        // ------------------------------------------------------------ TMA issuer
-        //   K / V of item r     once item r-1's last dQ product is done (kv_free)
-        //   Q / dO of tile n    once tile n-STAGES's gradient products are done (empty)
-        // Each probe is unambiguous: a barrier's next phase can complete only
-        // after the copy this thread issues in response to the one probed.
-        if (lane == 0) {
-            prefetch_tensormap(&p.tq);
-            prefetch_tensormap(&p.tk);
-            prefetch_tensormap(&p.tv);
-            prefetch_tensormap(&p.tdo);
-            Cursor cq;
-            cq.start(p, c, G);
-            int n_items = 0;  // this CTA's items
-            while (item_id(c, n_items, G) < p.n_work) ++n_items;
-            int nq = 0, rkv = 0;  // query tiles / items whose copies were issued
-            uint64_t t_idle = 0;
-            while (!failed && (cq.valid() || rkv < n_items)) {
-                bool progressed = false;
-                // The next item's K / V (items are loaded in order, never
-                // ahead of the item whose query tiles are being loaded).
-                if (rkv < n_items && (!cq.valid() || rkv <= cq.r) &&
-                    (rkv == 0 || mbar_test_wait(&sm.kv_free, (rkv - 1) & 1))) {
-                    const Item it = make_item(p, item_id(c, rkv, G));
-                    mbar_arrive_expect_tx(&sm.kv_full, 2 * KV_BYTES);
-                    tma_load_3d(sm.k, &p.tk, it.h * D, it.k0, it.b, &sm.kv_full);
-                    tma_load_3d(sm.v, &p.tv, it.h * D, it.k0, it.b, &sm.kv_full);
-                    ++rkv;
-                    progressed = true;
-                }
-                const int s = nq % STAGES;
-                if (cq.valid() && (nq < STAGES || mbar_test_wait(&sm.empty[s], ((nq - STAGES) / STAGES) & 1))) {
-                    const Item it = make_item(p, cq.w);
-                    const int q0 = (cq.it0 + cq.n) * BQ;
-                    mbar_arrive_expect_tx(&sm.q_full[s], 2 * QT_BYTES);
-                    tma_load_3d(sm.qg[s], &p.tq, it.h * D, q0, it.b, &sm.q_full[s]);
-                    tma_load_3d(sm.qg[s] + QT_BYTES, &p.tdo, it.h * D, q0, it.b, &sm.q_full[s]);
-                    ++nq;
-                    cq.next(p, c, G);
-                    progressed = true;
-                }
-                if (progressed) {
-                    t_idle = 0;
-                } else {
-                    const uint64_t now = globaltimer_ns();
-                    if (t_idle == 0) t_idle = now;
-                    else if (now - t_idle > p.wait_ns) failed = true;
-                    __nanosleep(64);
-                }
+    if (warp >= NELEM / 32 && warp < MMA_WARP) {
+        // ------------------------------------------------------------ loaders
+        // Step n writes the CTA's query tile n into its ring stage from
+        // registers, issues the global loads of tile n+1 into registers, then
+        // adds tile n-2's dQ into dq (gradient products finish in tile
+        // order): the loads are in flight while the step waits for that dQ.
+        pdl_wait();
+        const int t = tid - NELEM;
+        const int qd = warp & 3;
+        Cursor cl, cq;  // tile to load, tile whose dQ is added
+        cl.start(p, c, G);
+        cq.start(p, c, G);
+        tc::Rows2<BQ, NLOAD> x;
+        float lse_t = 0.f, ds_t = 0.f;
+        auto prefetch = [&]() {
+            const Item it = make_item(p, cl.w);
+            const long base = static_cast<long>(it.b) * p.T;
+            const int q0 = (cl.it0 + cl.n) * BQ;
+            x.load(p.q + base * p.ld_qkv + it.h * D, p.ld_qkv, p.dout + base * p.ld_o + it.h * D, p.ld_o, q0, p.T,
+                   t);
+            if (t < BQ) {
+                const long bh = (static_cast<long>(it.b) * p.H + it.h) * p.T;
+                const bool ok = q0 + t < p.T;
+                lse_t = ok ? p.lse[bh + q0 + t] * kLog2e : INFINITY;
+                ds_t = ok ? p.dsum[bh + q0 + t] : 0.f;
             }
-            if (failed) {
-                // Copies still landing complete before the shared memory is
-                // released (bounded waits).  Earlier copies into a buffer were
-                // consumed before it was reloaded.
-                if (rkv > 0) mbar_wait(&sm.kv_full, (rkv - 1) & 1, DRAIN_NS);
-                for (int t = max(0, nq - STAGES); t < nq; ++t)
-                    mbar_wait(&sm.q_full[t % STAGES], (t / STAGES) & 1, DRAIN_NS);
+        };
+        if (cl.valid()) prefetch();
+        for (int n = 0; !failed; ++n) {
+            if (cl.valid()) {
+                const int s = n % STAGES;
+                if (n >= STAGES && !mbar_wait_warp(&sm.empty[s], ((n - STAGES) / STAGES) & 1, p.wait_ns)) {
+                    failed = true;  // warp-uniform: the dQ epilogue below is warp-collective
+                    break;
+                }
+                if (t < BQ) {
+                    sm.lse2[s][t] = lse_t;
+                    sm.dsum[s][t] = ds_t;
+                }
+                x.store(sm.qh[s], sm.ql[s], sm.gh[s], sm.gl[s], t);
+                fence_async_smem();
+                mbar_arrive(&sm.full[s]);
+                cl.next(p, c, G);
+                if (cl.valid()) prefetch();
+            }
+            if (n >= 2) {
+                if (!cq.valid()) break;
+                const int m = n - 2;
+                if (!mbar_wait_warp(&sm.bar_d[m & 1], (m >> 1) & 1, p.wait_ns)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                const Item it = make_item(p, cq.w);
+                float* dqg = p.dq + static_cast<long>(it.b) * p.T * p.ld_d + it.h * D;
+                dq_epilogue(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg);
+                tc_fence_before();
+                mbar_arrive(&sm.dq_free[m & 1]);
+                cq.next(p, c, G);
             }
         }
-        __syncwarp();
     } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
-        // sdp(n) needs tile n converted, for n >= 2 grads(n-2) issued (TMEM
-        // buffer n&1; the tensor core runs this thread's MMAs in order) and
-        // the item's K / V converted.  grads(n) needs P / dS of tile n
-        // written, for n >= 2 dQ buffer n&1 read out, and for an item's first
-        // tile the previous item's dK / dV stored.  An item's last dQ product
-        // commits kv_free.
         if (lane == 0) {
             Descs d;
             make_descs(sm, d);
+            // sdp(n) needs tile n loaded, for n >= 2 grads(n-2) issued (TMEM
+            // buffer n&1; the tensor core runs this thread's MMAs in order)
+            // and, for an item's first tile, the item's K / V staged.
+            // grads(n) needs P / dS of tile n written and, for n >= 2, dQ
+            // buffer n&1 read out.  An item's last dQ product commits kv_free.
             Cursor cs, cg;
             cs.start(p, c, G);
             cg.start(p, c, G);
@@ -454,11 +453,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_consta
                 bool progressed = false;
                 if (cs.valid() && ns < ng + 2) {
                     bool kv_ok = kv_round >= cs.r;
-                    if (!kv_ok && mbar_test_wait(&sm.kv_ready, cs.r & 1)) {
+                    if (!kv_ok && mbar_test_wait(&sm.kv_full, cs.r & 1)) {
                         kv_round = cs.r;
                         kv_ok = true;
                     }
-                    if (kv_ok && mbar_test_wait(&sm.q_ready[ns % STAGES], (ns / STAGES) & 1)) {
+                    if (kv_ok && mbar_test_wait(&sm.full[ns % STAGES], (ns / STAGES) & 1)) {
                         tc_fence_after();
                         issue_sdp(d, tm, ns % STAGES, ns & 1);
                         mma_commit(&sm.bar_s[ns & 1]);
@@ -468,11 +467,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_consta
                     }
                 }
                 if (ng < ns && mbar_test_wait(&sm.pds[ng & 1], (ng >> 1) & 1) &&
-                    (ng < 2 || mbar_test_wait(&sm.dq_free[ng & 1], ((ng - 2) >> 1) & 1)) &&
-                    (cg.n != 0 || cg.r == 0 || mbar_test_wait(&sm.dkv_free, (cg.r - 1) & 1))) {
+                    (ng < 2 || mbar_test_wait(&sm.dq_free[ng & 1], ((ng - 2) >> 1) & 1))) {
                     tc_fence_after();
                     issue_dq(d, tm, ng & 1);
-                    if (cg.last_of_item()) mma_commit(&sm.kv_free);
+                    if (cg.n == cg.n_it - 1) mma_commit(&sm.kv_free);
                     issue_dkv(d, tm, ng % STAGES, ng & 1, cg.n == 0);
                     mma_commit(&sm.empty[ng % STAGES]);
                     mma_commit(&sm.bar_d[ng & 1]);
@@ -489,151 +487,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_consta
                     __nanosleep(20);
                 }
             }
-            if (failed) {
-                // MMAs still in flight complete before the columns are freed.
-                mma_commit(&sm.drain);
-                mbar_wait(&sm.drain, 0, DRAIN_NS);
-            }
         }
         __syncwarp();
-    } else if (warp >= NELEM / 32) {
-        // ------------------------------------------------------------ stage warps
-        // Iteration n: convert query tile n (Q, dO; D = rowsum(dO * O) with O
-        // read from global one tile ahead; lse), then add tile n-1's dQ into
-        // dq and, if tile n-1 ended its item, store that item's dK / dV.
-        const int t = tid - NELEM;
-        const int qd = warp & 3;
-        Cursor cl, ce;  // tile to convert, tile whose dQ is added
-        cl.start(p, c, G);
-        ce.start(p, c, G);
-        constexpr int QI = BQ * 16 / NSTG;  // float4s of a 64x64 tile per thread
-        float4 ov[QI];
-        float lse_t = 0.f;
-        auto prefetch = [&]() {  // O rows and lse of the tile at cl
-            const Item it = make_item(p, cl.w);
-            const int q0 = (cl.it0 + cl.n) * BQ;
-            const float* og = p.o + static_cast<long>(it.b) * p.T * p.ld_o + it.h * D;
-#pragma unroll
-            for (int i = 0; i < QI; ++i) {
-                const int f = t + i * NSTG;  // row f >> 4, columns 4 (f & 15) ..
-                const int r = q0 + (f >> 4);
-                ov[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (r < p.T)
-                    ov[i] = __ldg(reinterpret_cast<const float4*>(og + static_cast<long>(r) * p.ld_o + 4 * (f & 15)));
-            }
-            if (t < BQ) {
-                const long bh = (static_cast<long>(it.b) * p.H + it.h) * p.T;
-                lse_t = (q0 + t < p.T) ? p.lse[bh + q0 + t] * kLog2e : INFINITY;
-            }
-        };
-        bool dq_cleared = false;
-        if (cl.valid()) prefetch();
-        for (int n = 0; !failed; ++n) {
-            if (cl.valid()) {
-                const int s = n % STAGES;
-                uint8_t* qt = sm.qg[s];
-                uint8_t* gt = sm.qg[s] + QT_BYTES;
-                if (!mbar_wait_warp(&sm.q_full[s], (n / STAGES) & 1, p.wait_ns)) {
-                    failed = true;
-                    break;
-                }
-                // D of this thread's rows (t >> 4) + 8 i from the raw dO in
-                // shared memory and the O registers: the 16 threads of a
-                // half-warp hold one row between them.  Done before the raw
-                // tiles are read for conversion, so O and the tiles are not
-                // live in registers at once.
-#pragma unroll
-                for (int i = 0; i < QI; ++i) {
-                    const float4 g = reinterpret_cast<const float4*>(gt)[t + i * NSTG];
-                    float dv = g.x * ov[i].x + g.y * ov[i].y + g.z * ov[i].z + g.w * ov[i].w;
-#pragma unroll
-                    for (int off = 8; off > 0; off >>= 1) dv += __shfl_xor_sync(0xffffffffu, dv, off);
-                    if ((t & 15) == 0) sm.dsum[s][(t >> 4) + 8 * i] = dv;
-                }
-                if (t < BQ) sm.lse2[s][t] = lse_t;
-                tc::RawTile<BQ, NSTG> qr, gr;
-                qr.read(qt, t);
-                gr.read(gt, t);
-                // Converted in place: every thread has read its share first.
-                mbar_arrive(&sm.q_read[s]);
-                if (!mbar_wait_warp(&sm.q_read[s], (n / STAGES) & 1, p.wait_ns)) {
-                    failed = true;
-                    break;
-                }
-                qr.write(qt, 1.f, t);
-                gr.write(gt, 1.f, t);
-                fence_async_smem();
-                mbar_arrive(&sm.q_ready[s]);
-                cl.next(p, c, G);
-                if (cl.valid()) prefetch();
-            }
-            if (n >= 1) {
-                if (!ce.valid()) break;
-                const int m = n - 1;
-                if (!mbar_wait_warp(&sm.bar_d[m & 1], (m >> 1) & 1, p.wait_ns)) {
-                    failed = true;
-                    break;
-                }
-                tc_fence_after();
-                if (!dq_cleared) {
-                    pdl_wait();  // attn_bwd_zero_dq has finished
-                    dq_cleared = true;
-                }
-                const Item it = make_item(p, ce.w);
-                float* dqg = p.dq + static_cast<long>(it.b) * p.T * p.ld_d + it.h * D;
-                dq_epilogue(p, tm, m & 1, qd, lane, (ce.it0 + ce.n) * BQ, dqg);
-                const bool item_end = ce.last_of_item();
-                if (item_end) store_dkv(p, tm, it, qd, lane);
-                tc_fence_before();
-                mbar_arrive(&sm.dq_free[m & 1]);
-                if (item_end) mbar_arrive(&sm.dkv_free);
-                ce.next(p, c, G);
-            }
-        }
     } else {
         // ------------------------------------------------------------ elementwise
         const int qd = warp & 3;          // TMEM lane quadrant: key rows 32*qd..
         const int hf = warp >> 2;         // query columns 32*hf..+31 (two 16-column chunks)
         const int row = qd * 32 + lane;   // key row inside the tile
         const uint32_t lb = static_cast<uint32_t>(qd * 32) << 16;
+        int w = item_id(c, 0, G);
+        Item it = make_item(p, w);
+        {
+            const long base = static_cast<long>(it.b) * p.T;
+            tc::stage_rows2<BK, NELEM>(sm.kh, sm.kl, p.k + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.vh, sm.vl,
+                                       p.v + base * p.ld_qkv + it.h * D, p.ld_qkv, it.k0, p.T, tid);
+        }
+        fence_async_smem();
+        mbar_arrive(&sm.kv_full);
+
         int g = 0;  // the CTA's query-tile sequence number
         for (int r = 0; !failed; ++r) {
-            const int w = item_id(c, r, G);
-            if (w >= p.n_work) break;
-            const Item it = make_item(p, w);
-            // The item's K / V: raw tiles converted in place (every thread
-            // reads its share before any thread writes).
-            {
-                if (!mbar_wait_warp(&sm.kv_full, r & 1, p.wait_ns)) {
-                    failed = true;
-                    break;
-                }
-                // K, then V: kv_read completes twice per item (phases 2r, 2r+1).
-                bool ok = true;
-#pragma unroll 1
-                for (int u = 0; u < 2 && ok; ++u) {
-                    uint8_t* tile = u ? sm.v : sm.k;
-                    tc::RawTile<BK, NELEM> kr;
-                    kr.read(tile, tid);
-                    mbar_arrive(&sm.kv_read);
-                    ok = mbar_wait_warp(&sm.kv_read, u, p.wait_ns);
-                    if (ok) kr.write(tile, 1.f, tid);
-                }
-                if (!ok) {
-                    failed = true;
-                    break;
-                }
-                fence_async_smem();
-                mbar_arrive(&sm.kv_ready);
-            }
             const int j = it.k0 + row;
             for (int n = 0; n < it.n_it; ++n, ++g) {
                 const int s = g % STAGES;  // ring stage of this query tile
                 const int buf = g & 1;     // TMEM / dS buffer
                 const int q0 = (it.it0 + n) * BQ;
-                // q_ready[s]: this tile's lse / D are staged.
+                // full[s]: the loaders' lse / D writes for this tile are visible.
                 if (!mbar_wait_warp(&sm.bar_s[buf], (g >> 1) & 1, p.wait_ns) ||
-                    !mbar_wait_warp(&sm.q_ready[s], (g / STAGES) & 1, p.wait_ns)) {
+                    !mbar_wait_warp(&sm.full[s], (g / STAGES) & 1, p.wait_ns)) {
                     failed = true;
                     break;
                 }
@@ -704,28 +585,46 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const __grid_consta
                 tc_fence_before();
                 mbar_arrive(&sm.pds[buf]);
             }
+            if (failed) break;
+
+            // Item end.  The next item's K / V rows go into registers now and
+            // into shared memory once this item's last dQ product is done.
+            const int wn = item_id(c, r + 1, G);
+            const bool has_next = wn < p.n_work;
+            Item nx = it;
+            if (has_next) {
+                nx = make_item(p, wn);
+                const long base = static_cast<long>(nx.b) * p.T;
+                tc::Rows2<BK, NELEM> kv;
+                kv.load(p.k + base * p.ld_qkv + nx.h * D, p.ld_qkv, p.v + base * p.ld_qkv + nx.h * D, p.ld_qkv,
+                        nx.k0, p.T, tid);
+                if (!mbar_wait_warp(&sm.kv_free, r & 1, p.wait_ns)) {
+                    failed = true;
+                    break;
+                }
+                kv.store(sm.kh, sm.kl, sm.vh, sm.vl, tid);
+                fence_async_smem();
+                mbar_arrive(&sm.kv_full);
+            }
+            const int gl_ = g - 1;  // this item's last tile
+            if (!mbar_wait_warp(&sm.bar_d[gl_ & 1], (gl_ >> 1) & 1, p.wait_ns)) {
+                failed = true;
+                break;
+            }
+            tc_fence_after();
+            if (!store_dkv(p, sm, tm, it, lb, row, hf, tid, r)) {
+                failed = true;
+                break;
+            }
+            if (!has_next) break;
+            it = nx;
         }
     }
 
-    if (__syncthreads_or(failed) && tid == 0) atomicOr(p.status, 1);
+    if (failed) atomicOr(p.status, 1);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tm, TMEM_COLS);
-}
-
-// dq = 0 over the H*64 columns of every row of a strided [rows][ld] buffer.
-// It waits for the grid before it first (dq may be that grid's input), so the
-// backward behind it launches only once every earlier grid has finished.
-__global__ void __launch_bounds__(256) attn_bwd_zero_dq(float* dq, long ld, long rows, int c4) {
-    pdl_wait();
-    pdl_launch();
-    const long n = rows * c4;
-    for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-         i += static_cast<long>(gridDim.x) * blockDim.x) {
-        const long r = i / c4;
-        const int q = static_cast<int>(i - r * c4);
-        *reinterpret_cast<float4*>(dq + r * ld + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
 }
 
 }  // namespace
@@ -733,15 +632,17 @@ __global__ void __launch_bounds__(256) attn_bwd_zero_dq(float* dq, long ld, long
 bool bwd_tc_supported(const BwdArgs& a) { return a.d == 64; }
 
 cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches) {
+    cudaError_t e = launch_bwd_prep(a, num_sms, stream, launches);
+    if (e != cudaSuccess) return e;
     Params p;
-    if (!encode_rows(&p.tq, a.q, a.ld_qkv, a.B, a.T, a.H, D, BQ, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&p.tk, a.k, a.ld_qkv, a.B, a.T, a.H, D, BK, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&p.tv, a.v, a.ld_qkv, a.B, a.T, a.H, D, BK, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&p.tdo, a.dout, a.ld_o, a.B, a.T, a.H, D, BQ, CU_TENSOR_MAP_SWIZZLE_NONE))
-        return cudaErrorInvalidValue;
-    p.o = a.o;
+    p.q = a.q;
+    p.k = a.k;
+    p.v = a.v;
+    p.ld_qkv = a.ld_qkv;
+    p.dout = a.dout;
     p.ld_o = a.ld_o;
     p.lse = a.lse;
+    p.dsum = a.dsum;
     p.dq = a.dq;
     p.dk = a.dk;
     p.dv = a.dv;
@@ -759,16 +660,6 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     const long n_work = static_cast<long>(p.n_ktiles) * a.B * a.H;
     if (n_work <= 0 || n_work > INT32_MAX) return cudaErrorInvalidValue;
     p.n_work = static_cast<int>(n_work);
-
-    const long rows = static_cast<long>(a.B) * a.T;
-    const int c4 = a.H * D / 4;
-    const long n4 = rows * c4;
-    const long zgrid = std::min<long>((n4 + 255) / 256, 4L * (num_sms > 0 ? num_sms : 148));
-    cudaError_t e = launch_pdl(attn_bwd_zero_dq, dim3(static_cast<unsigned>(zgrid)), dim3(256), 0, stream, a.dq,
-                               a.ld_d, rows, c4);
-    if (e != cudaSuccess) return e;
-    *launches += 1;
-
     const size_t smem = sizeof(Smem) + 1024;
     int dev = 0;
     e = cudaGetDevice(&dev);

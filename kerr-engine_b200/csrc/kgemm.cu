@@ -10,8 +10,11 @@
 // place as bf16 hi / lo halves in the 128B-swizzled UMMA layout, so no split
 // copy of an operand goes through HBM.
 //
-// Tiles: 128 (M) x 256 (N) per unit, K in 64-wide stages (A 32 KB + B 64 KB
-// raw per stage, two stages).  An operand is "K-major" when K runs along the
+// Tiles: 128 (M) x 256 (N) per unit, K in 32-wide stages (A 16 KB + B 32 KB
+// raw per stage, four stages, so that a stage's copy and conversion overlap
+// the MMAs of the three before it).  K-major operands are converted into the
+// 64B-swizzled layout (32 bf16 per row), MN-major ones into 128B-swizzled
+// atoms of 64 columns.  An operand is "K-major" when K runs along the
 // memory rows (x, W of the forward, dy of the dx product) and "MN-major" when
 // M or N does (W of the dx product, dy and x of the dW product); the two
 // orientations differ in the TMA box, the in-place rewrite and the MMA
@@ -45,15 +48,15 @@ namespace {
 
 constexpr int GM = 128;  // tile rows (MMA M)
 constexpr int GN = 256;  // tile columns (MMA N)
-constexpr int GK = 64;   // K per stage
+constexpr int GK = 32;   // K per stage
 constexpr int NCONV = 256;
 constexpr int NEPI = 128;
 constexpr int G_MMA_WARP = (NCONV + NEPI) / 32;
 constexpr int G_TMA_WARP = G_MMA_WARP + 1;
 constexpr int G_THREADS = NCONV + NEPI + 64;
-constexpr int G_STAGES = 2;
-constexpr uint32_t A_BYTES = GM * GK * 4;  // raw f32 A stage; later hi (16 KB) | lo
-constexpr uint32_t B_BYTES = GN * GK * 4;  // raw f32 B stage; later hi (32 KB) | lo
+constexpr int G_STAGES = 4;
+constexpr uint32_t A_BYTES = GM * GK * 4;  // raw f32 A stage; later hi (8 KB) | lo
+constexpr uint32_t B_BYTES = GN * GK * 4;  // raw f32 B stage; later hi (16 KB) | lo
 constexpr int EPI_PITCH = 36;              // floats per staged row (conflict-free float4 access)
 constexpr uint32_t G_TMEM_COLS = 512;      // two 256-column accumulators
 constexpr unsigned long long G_DRAIN_NS = 10000000ull;
@@ -76,7 +79,7 @@ struct alignas(1024) GSmem {
 static_assert(sizeof(GSmem) + 1024 <= 232448, "shared memory (plus alignment slack) exceeds 227 KB");
 
 struct alignas(64) GParams {
-    CUtensorMap ta, tb;  // A: K-major {K, M} box {64, 128} or MN-major {M, K} box {128, 64}; B likewise with N, 256
+    CUtensorMap ta, tb;  // A: K-major {K, M} box {32, 128} or MN-major {M, K} box {128, 32}; B likewise with N, 256
     float* c;
     long ldc;
     const float* bias;  // [N] or null (added when the unit writes C)
@@ -172,10 +175,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constan
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16(GM, GN, A_MN ? 1 : 0, B_MN ? 1 : 0);
-            // K-major: rows of 128 bytes, k-step 32 bytes; MN-major: 64-column
-            // atoms 64 rows apart (lbo), k-step 16 rows (2048 bytes).
-            constexpr uint32_t A_LBO = A_MN ? GK * 128 : 16, B_LBO = B_MN ? GK * 128 : 16;
+            // K-major: 64-byte rows (64B swizzle, 512-byte atoms), k-step 32
+            // bytes; MN-major: 64-column atoms GK rows apart (lbo), k-step 16
+            // rows (2048 bytes).
             constexpr uint32_t A_KSTEP = A_MN ? 2048 : 32, B_KSTEP = B_MN ? 2048 : 32;
+            auto desc = [](uint32_t addr, bool mn) -> uint64_t {
+                return mn ? smem_desc(addr, GK * 128, 1024) : smem_desc_sw64(addr, 512);
+            };
             int g = 0, i = 0;
             for (int u = c; u < p.n_units && !failed; u += G, ++i) {
                 const Unit x = make_unit(p, u);
@@ -193,10 +199,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constan
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ah = smem_desc(smem_u32(sm.a[s]), A_LBO, 1024);
-                    const uint64_t al = smem_desc(smem_u32(sm.a[s] + A_BYTES / 2), A_LBO, 1024);
-                    const uint64_t bh = smem_desc(smem_u32(sm.b[s]), B_LBO, 1024);
-                    const uint64_t bl = smem_desc(smem_u32(sm.b[s] + B_BYTES / 2), B_LBO, 1024);
+                    const uint64_t ah = desc(smem_u32(sm.a[s]), A_MN);
+                    const uint64_t al = desc(smem_u32(sm.a[s] + A_BYTES / 2), A_MN);
+                    const uint64_t bh = desc(smem_u32(sm.b[s]), B_MN);
+                    const uint64_t bl = desc(smem_u32(sm.b[s] + B_BYTES / 2), B_MN);
 #pragma unroll
                     for (int ks = 0; ks < GK / 16; ++ks) {
                         const uint32_t oa = ks * A_KSTEP, ob = ks * B_KSTEP;
@@ -290,12 +296,12 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constan
                     failed = true;
                     break;
                 }
-                // A: [128][64] K-major or [64][128] MN-major; B: [256][64] or
-                // [64][256].  Each tile is rewritten in place once every
+                // A: [128][32] K-major or [32][128] MN-major; B: [256][32] or
+                // [32][256].  Each tile is rewritten in place once every
                 // thread has read its share of it; A first, then B, so that
                 // only one tile's share is live in registers at a time.
-                using ATile = typename std::conditional<A_MN, tc::RawTileMN<GK, GM, NCONV>, tc::RawTile<GM, NCONV>>::type;
-                using BTile = typename std::conditional<B_MN, tc::RawTileMN<GK, GN, NCONV>, tc::RawTile<GN, NCONV>>::type;
+                using ATile = typename std::conditional<A_MN, tc::RawTileMN<GK, GM, NCONV>, tc::RawTile32<GM, NCONV>>::type;
+                using BTile = typename std::conditional<B_MN, tc::RawTileMN<GK, GN, NCONV>, tc::RawTile32<GN, NCONV>>::type;
                 {
                     ATile ta;
                     ta.read(sm.a[s], tid);
@@ -304,8 +310,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constan
                         failed = true;
                         break;
                     }
-                    if constexpr (A_MN) ta.write(sm.a[s], tid);
-                    else ta.write(sm.a[s], 1.f, tid);
+                    ta.write(sm.a[s], tid);
                 }
                 {
                     BTile tb;
@@ -315,8 +320,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constan
                         failed = true;
                         break;
                     }
-                    if constexpr (B_MN) tb.write(sm.b[s], tid);
-                    else tb.write(sm.b[s], 1.f, tid);
+                    tb.write(sm.b[s], tid);
                 }
                 fence_async_smem();
                 mbar_arrive(&sm.ready[s]);
@@ -409,9 +413,10 @@ ProjStatus gemm_tc(cudaStream_t s, cudaMemPool_t pool, int num_sms, const float*
     p.n_tiles = (N + GN - 1) / GN;
     p.k_stages = (K + GK - 1) / GK;
     const long tiles = static_cast<long>(p.m_tiles) * p.n_tiles;
-    // Split K while the tiles alone leave SMs idle, keeping >= 4 stages per split.
+    // Split K while the tiles alone leave SMs idle, keeping >= 8 stages
+    // (256 of K) per split so that the four-stage ring fills.
     int splits = 1;
-    if (tiles < sms) splits = static_cast<int>(std::min<long>((sms + tiles - 1) / tiles, std::max(1, p.k_stages / 4)));
+    if (tiles < sms) splits = static_cast<int>(std::min<long>((sms + tiles - 1) / tiles, std::max(1, p.k_stages / 8)));
     splits = std::min(splits, 8);
     p.stages_per_split = (p.k_stages + splits - 1) / splits;
     p.splits = (p.k_stages + p.stages_per_split - 1) / p.stages_per_split;

@@ -30,6 +30,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Arrive once with relaxed semantics: orders nothing before it, so it does
+// not wait for the thread's outstanding memory operations.  For hand-offs
+// whose data has already completed (e.g. after tcgen05.wait::ld).
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -229,6 +236,24 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     d |= static_cast<uint64_t>(1u) << 46;  // version
     d |= static_cast<uint64_t>(2u) << 61;  // SWIZZLE_128B
     return d;
+}
+
+// The same for a 64-byte-swizzled K-major tile (layout type 4): rows of 64
+// bytes (32 bf16) in 8-row atoms of 512 bytes; inside an atom, row r's
+// 16-byte chunk c sits at chunk c ^ ((r >> 1) & 3).  sbo = 512.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;  // leading-byte offset (unused for K-major swizzled)
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;  // version
+    d |= static_cast<uint64_t>(4u) << 61;  // SWIZZLE_64B
+    return d;
+}
+
+// Byte offset of (row, 16-byte chunk) inside a 64B-swizzled tile of 64-byte rows.
+__device__ __forceinline__ uint32_t sw64(uint32_t row, uint32_t chunk) {
+    return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
 }
 
 // Descriptor advanced by `bytes` (a multiple of 16) along its start address;
