@@ -680,6 +680,19 @@ bool encode_2d(CUtensorMap* map, const float* base, long cols, long rows, long l
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_2d_bf16(CUtensorMap* map, const uint16_t* base, long cols, long rows, long ld, int box_cols, int box_rows,
+                    CUtensorMapSwizzle swizzle) {
+    const EncodeTiled fn = encode_tiled();
+    if (fn == nullptr || cols <= 0 || rows <= 0) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool fwd_tc_supported(const FwdArgs& a) { return a.d == 64; }
 
 cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches) {

@@ -4,6 +4,8 @@
 
 #include <cuda.h>
 
+#include <cstdint>
+
 namespace kattn {
 
 // The first H*64 columns of a [B*T][ld] f32 buffer as a 3-D tensor
@@ -18,5 +20,10 @@ bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int
 // elements) as a 2-D tensor {cols (innermost), rows}, boxes of box_cols x
 // box_rows with no swizzle; elements past either extent read as zeros.
 bool encode_2d(CUtensorMap* map, const float* base, long cols, long rows, long ld, int box_cols, int box_rows);
+
+// The same over a row-major bf16 matrix (ld a multiple of 8 elements), with
+// the given swizzle of the box in shared memory.
+bool encode_2d_bf16(CUtensorMap* map, const uint16_t* base, long cols, long rows, long ld, int box_cols, int box_rows,
+                    CUtensorMapSwizzle swizzle);
 
 }  // namespace kattn
