@@ -544,10 +544,11 @@ ProjStatus gemm_tc(cudaStream_t s, cudaMemPool_t pool, int num_sms, const float*
     p.n_tiles = (N + GN - 1) / GN;
     p.k_stages = (K + GK - 1) / GK;
     const long tiles = static_cast<long>(p.m_tiles) * p.n_tiles;
-    // Split K while the tiles alone leave SMs idle, keeping >= 4 stages
-    // (256 of K) per split so that the ring fills.
+    // Split K while the tiles alone leave at least half the SMs idle (the
+    // partial sums cost a write and a read of splits x M x N floats), keeping
+    // >= 4 stages (256 of K) per split so that the ring fills.
     int splits = 1;
-    if (tiles < sms) splits = static_cast<int>(std::min<long>((sms + tiles - 1) / tiles, std::max(1, p.k_stages / 4)));
+    if (2 * tiles <= sms) splits = static_cast<int>(std::min<long>((sms + tiles - 1) / tiles, std::max(1, p.k_stages / 4)));
     splits = std::min(splits, 8);
     p.stages_per_split = (p.k_stages + splits - 1) / splits;
     p.splits = (p.k_stages + p.stages_per_split - 1) / p.stages_per_split;

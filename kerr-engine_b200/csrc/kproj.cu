@@ -11,7 +11,9 @@
 // it as they are:
 //   forward: y[m][n]  = sum_k x[m][k] w[n][k]      A = x (K-major), B = w (K-major)
 //   dx     : dx[m][k] = sum_n dy[m][n] w[n][k]     A = dy (K-major), B(k, n) = w[n][k] (MN-major)
-//   dW     : dW[n][k] = sum_m dy[m][n] x[m][k]     A(n, m) = dy[m][n], B(k, m) = x[m][k] (both MN-major)
+//   dW     : dW[n][k] = sum_m dy[m][n] x[m][k]     A(n, m) = dy[m][n] through a transposed copy dyT
+//                                                   (K-major; MN-major dy when M % 4 != 0), B(k, m) = x[m][k]
+//                                                   (MN-major)
 // The bias of the forward is added in the GEMM's epilogue; db is a column sum
 // in a fixed order (the kernels below), so the same inputs give the same bits.
 #include "kattn_common.cuh"
@@ -31,6 +33,34 @@ __global__ void __launch_bounds__(256) proj_fill_bias(float* __restrict__ y, lon
         const long r = i / cols;
         const int c = static_cast<int>(i - r * cols);
         y[r * ld + c] = b[c];
+    }
+}
+
+// dyT[n][m] = dy[m][n] (dyT row stride M) and part[p][n] = sum of dy[m][n]
+// over rows [32p, min(M, 32p + 32)) in row order, one 32 x 32 tile per
+// block: the dW product then reads dy^T K-major (whole-row loads), and db
+// comes from the same pass over dy.
+__global__ void __launch_bounds__(256) proj_transpose_colsum(const float* __restrict__ dy, long ld, int M, int N,
+                                                             float* __restrict__ dyT, float* __restrict__ part) {
+    pdl_enter();
+    __shared__ float tile[32][33];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = r0 + ty + 8 * i, c = c0 + tx;
+        tile[ty + 8 * i][tx] = (r < M && c < N) ? dy[static_cast<long>(r) * ld + c] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int c = c0 + ty + 8 * i, r = r0 + tx;
+        if (c < N && r < M) dyT[static_cast<long>(c) * M + r] = tile[tx][ty + 8 * i];
+    }
+    if (part && ty == 0 && c0 + tx < N) {
+        float acc = 0.f;
+        for (int r = 0; r < 32; ++r) acc += tile[r][tx];  // rows past M are zero
+        part[static_cast<long>(blockIdx.y) * N + c0 + tx] = acc;
     }
 }
 
@@ -117,38 +147,73 @@ ProjStatus proj_backward_dw(int num_sms, cudaStream_t s, cudaMemPool_t pool, int
                             const float* dy, long ld_dy, const float* x, long ld_x, float* dw, float* db, int M, int N,
                             int K, int accumulate, int* launches) {
     if (N == 0) return {};
-    cudaError_t e;
-    if (db) {
-        const int R = 64;  // rows per column-sum partial
-        const int P = M > 0 ? (M + R - 1) / R : 0;
-        float* part = nullptr;
-        if (P > 0) {
-            e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&part), sizeof(float) * static_cast<size_t>(P) * N,
-                                        pool, s);
-            if (e != cudaSuccess) return {e, "column-sum workspace"};
-            e = launch_pdl(proj_colsum_part, dim3((N + 255) / 256, P), dim3(256), 0, s, dy, ld_dy, M, N, R, part);
-            if (e == cudaSuccess) ++*launches;
-        } else {
-            e = cudaSuccess;
+    cudaError_t e = cudaSuccess;
+    // With M a multiple of 4, dy is transposed once (dyT [N][M]) so that the
+    // GEMM reads its A operand K-major, and the same pass leaves db's 32-row
+    // partial sums; otherwise the GEMM reads dy MN-major and db has its own
+    // pass.
+    const bool transpose = M > 0 && K > 0 && M % 4 == 0;
+    float* dyT = nullptr;
+    float* part = nullptr;
+    auto release = [&]() {
+        cudaError_t ef = cudaSuccess;
+        if (dyT) ef = cudaFreeAsync(dyT, s);
+        if (part) {
+            const cudaError_t e2 = cudaFreeAsync(part, s);
+            if (ef == cudaSuccess) ef = e2;
         }
-        if (e == cudaSuccess) {
+        dyT = part = nullptr;
+        return ef;
+    };
+    if (db || transpose) {
+        const int R = transpose ? 32 : 64;  // rows per column-sum partial
+        const int P = M > 0 ? (M + R - 1) / R : 0;
+        if (db && P > 0)
+            e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&part), sizeof(float) * static_cast<size_t>(P) * N, pool,
+                                        s);
+        if (e == cudaSuccess && transpose)
+            e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&dyT), sizeof(float) * static_cast<size_t>(N) * M, pool,
+                                        s);
+        if (e != cudaSuccess) {
+            release();
+            return {e, "dW workspace"};
+        }
+        if (transpose) {
+            e = launch_pdl(proj_transpose_colsum, dim3((N + 31) / 32, (M + 31) / 32), dim3(32, 8), 0, s, dy, ld_dy, M, N,
+                           dyT, part);
+        } else if (part) {
+            e = launch_pdl(proj_colsum_part, dim3((N + 255) / 256, P), dim3(256), 0, s, dy, ld_dy, M, N, R, part);
+        }
+        if (e == cudaSuccess && (transpose || part)) ++*launches;
+        if (e == cudaSuccess && db) {
             e = launch_pdl(proj_colsum_final, dim3((N + COLSUM_COLS - 1) / COLSUM_COLS),
                            dim3(COLSUM_COLS, COLSUM_GROUPS), 0, s, static_cast<const float*>(part), P, N, db,
                            accumulate);
             if (e == cudaSuccess) ++*launches;
         }
-        const cudaError_t ef = part ? cudaFreeAsync(part, s) : cudaSuccess;
-        if (e == cudaSuccess) e = ef;
-        if (e != cudaSuccess) return {e, "column sums"};
+        if (e != cudaSuccess) {
+            release();
+            return {e, "dW prologue"};
+        }
     }
-    if (K == 0) return {};
-    if (M == 0) {
-        if (accumulate) return {};
-        e = cudaMemsetAsync(dw, 0, static_cast<size_t>(N) * K * 4, s);
-        return e == cudaSuccess ? ProjStatus{} : ProjStatus{e, "cudaMemsetAsync"};
+    ProjStatus st;
+    if (K > 0) {
+        if (M == 0) {
+            if (!accumulate) {
+                e = cudaMemsetAsync(dw, 0, static_cast<size_t>(N) * K * 4, s);
+                if (e != cudaSuccess) st = {e, "cudaMemsetAsync"};
+            }
+        } else if (transpose) {
+            st = gemm_tc(s, pool, num_sms, dyT, M, false, x, ld_x, true, dw, K, nullptr, N, K, M, accumulate, status,
+                         wait_ns, launches);
+        } else {
+            st = gemm_tc(s, pool, num_sms, dy, ld_dy, true, x, ld_x, true, dw, K, nullptr, N, K, M, accumulate, status,
+                         wait_ns, launches);
+        }
     }
-    return gemm_tc(s, pool, num_sms, dy, ld_dy, true, x, ld_x, true, dw, K, nullptr, N, K, M, accumulate, status,
-                   wait_ns, launches);
+    const cudaError_t ef = release();
+    if (st.cuda == cudaSuccess && ef != cudaSuccess) st = {ef, "dW workspace release"};
+    return st;
 }
 
 }  // namespace kattn
