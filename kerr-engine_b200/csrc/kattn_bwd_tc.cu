@@ -88,7 +88,6 @@ struct alignas(1024) Smem {
     uint64_t kv_full;  // an item's K / V staged (phase r: the CTA's item r)
     uint64_t kv_free;  // an item's last dQ product done: K / V may be replaced
     uint64_t full[STAGES];
-    uint64_t empty[STAGES];
     uint64_t bar_s[2];
     uint64_t pds[2];      // P / dS of the tile in buffer b written
     uint64_t bar_d[2];    // gradient products of the tile in buffer b done
@@ -266,18 +265,27 @@ __device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, in
 
 // A dQ tile (M=64 accumulator: query row 16*qd + l sits in lane 32*qd + l,
 // l < 16), scaled and added into dq by the loader warp of lane quadrant qd,
-// 32 columns at a time.
+// 32 columns at a time.  The TMEM buffer is released on `dq_free` as soon as
+// both halves are in registers, with a relaxed arrive: a release arrive
+// would wait for this thread's outstanding global operations (the first
+// half's reductions, the next tile's prefetch loads), and the next gradient
+// products wait for this buffer.
 __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int lane, int q0,
-                                            float* dqg) {
+                                            float* dqg, uint64_t* dq_free) {
     const uint32_t ta = (static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b);
     const int r = q0 + qd * 16 + lane;
     float* dst = dqg + static_cast<long>(r) * p.ld_d;
+    const bool on = lane < 16 && r < p.T;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         float v[32];
         tmem_ld32(ta + 32 * h, v);
         tmem_wait_ld();
-        if (lane < 16 && r < p.T) {
+        if (h == 1) {
+            tc_fence_before();
+            mbar_arrive_relaxed(dq_free);
+        }
+        if (on) {
 #pragma unroll
             for (int c = 0; c < 32; c += 4)
                 red_add_v4(dst + 32 * h + c, v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale,
@@ -355,7 +363,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         mbar_init(&sm.kv_free, 1);
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&sm.full[i], NLOAD);
-            mbar_init(&sm.empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.bar_s[i], 1);
@@ -403,11 +410,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         if (cl.valid()) prefetch();
         for (int n = 0; !failed; ++n) {
             if (cl.valid()) {
+                // Stage s last held tile n - STAGES, whose gradient products
+                // these warps saw complete (bar_d) before reading its dQ in
+                // step n - 1, so the stage is free without another wait.
+                static_assert(STAGES == 3, "tile n-3's dQ is read out in step n-1");
                 const int s = n % STAGES;
-                if (n >= STAGES && !mbar_wait_warp(&sm.empty[s], ((n - STAGES) / STAGES) & 1, p.wait_ns)) {
-                    failed = true;  // warp-uniform: the dQ epilogue below is warp-collective
-                    break;
-                }
                 if (t < BQ) {
                     sm.lse2[s][t] = lse_t;
                     sm.dsum[s][t] = ds_t;
@@ -428,9 +435,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 tc_fence_after();
                 const Item it = make_item(p, cq.w);
                 float* dqg = p.dq + static_cast<long>(it.b) * p.T * p.ld_d + it.h * D;
-                dq_epilogue(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg);
-                tc_fence_before();
-                mbar_arrive(&sm.dq_free[m & 1]);
+                dq_epilogue(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg, &sm.dq_free[m & 1]);
                 cq.next(p, c, G);
             }
         }
@@ -472,8 +477,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                     issue_dq(d, tm, ng & 1);
                     if (cg.n == cg.n_it - 1) mma_commit(&sm.kv_free);
                     issue_dkv(d, tm, ng % STAGES, ng & 1, cg.n == 0);
-                    mma_commit(&sm.empty[ng % STAGES]);
-                    mma_commit(&sm.bar_d[ng & 1]);
+                    mma_commit(&sm.bar_d[ng & 1]);  // one commit: back-to-back commits stall the MMA pipe
                     ++ng;
                     cg.next(p, c, G);
                     progressed = true;
