@@ -100,6 +100,20 @@ int kattn_set_path(kattn_ctx* ctx, int path);
  * whose GPU backend panics on device errors (src/gpu_ops_forward.rs:63). */
 int kattn_set_wait_limit(kattn_ctx* ctx, unsigned long long ns);
 
+/* Deterministic dQ (on != 0; off by default).  By default the backward adds
+ * every key tile's dQ contribution into dq with floating-point reductions
+ * whose order depends on scheduling, so dq can differ in the last bits from
+ * run to run (dk, dv and the forward are always deterministic).  With the
+ * mode on, each key tile stores its contribution into its own slice of a
+ * [key tiles][B*T][H*d] float workspace from the context's pool (128 key
+ * rows per tile on the tensor-core kernels, 64 on the FFMA kernels), and one
+ * more kernel adds the slices in key-tile order: the same inputs then give
+ * the same bits, at the cost of that workspace and a pass over it.  Replaces
+ * the order the reference fixes by summing sequentially over keys
+ * (src/backward.rs:508-512).  kattn_bwd_noalloc refuses to run in this mode
+ * (KATTN_ERR_UNSUPPORTED): it allocates nothing. */
+int kattn_set_deterministic(kattn_ctx* ctx, int on);
+
 /* Diagnostic for the bounded waits: the next tensor-core forward launched on
  * this context issues no copy of its first key tile, so the waits on that
  * tile run out after the wait limit and the kernel unwinds as above (its

@@ -34,6 +34,7 @@ struct kattn_ctx {
     cudaMemPool_t pool = nullptr;   // the context's own stream-ordered pool for per-call workspace
     std::atomic<unsigned long long> wait_ns{kDefaultWaitNs};  // limit of the kernels' bounded waits
     std::atomic<int> withhold_next_load{0};  // diagnostic hook (kattn_test_withhold_next_load)
+    std::atomic<int> deterministic{0};       // dQ by ordered slices (kattn_set_deterministic)
 };
 
 // Device-resident state of one forward (the reference's AttnCache):
@@ -185,12 +186,29 @@ cudaError_t dispatch_fwd(kattn_ctx* ctx, const kattn::FwdArgs& a, cudaStream_t s
 // Backward launch on the kernel family the context selects.
 cudaError_t dispatch_bwd(kattn_ctx* ctx, const kattn::BwdArgs& a, cudaStream_t s, int* launches) {
     const int path = ctx->path.load(std::memory_order_relaxed);
-    if (path != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a)) {
-        kattn::BwdArgs b = a;
-        b.wait_ns = ctx->wait_ns.load(std::memory_order_relaxed);
-        return kattn::launch_bwd_tc(b, ctx->num_sms, ctx->d_status, s, launches);
+    const bool tensor = path != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a);
+    kattn::BwdArgs b = a;
+    b.wait_ns = ctx->wait_ns.load(std::memory_order_relaxed);
+    // Deterministic dQ: every key tile stores its contribution into its own
+    // slice of a pool workspace, and one pass adds the slices in key-tile
+    // order (the reference sums dQ over keys sequentially,
+    // src/backward.rs:508-512); otherwise the tiles add into dq directly.
+    const bool det = ctx->deterministic.load(std::memory_order_relaxed) != 0;
+    const int key_rows = tensor ? kattn::kBwdTcKeyRows : kattn::kBwdF32KeyRows;
+    if (det) {
+        const size_t n_kt = static_cast<size_t>((a.T + key_rows - 1) / key_rows);
+        const size_t bytes = sizeof(float) * n_kt * a.B * a.T * a.H * a.d;
+        const cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&b.dq_part), bytes, ctx->pool, s);
+        if (e != cudaSuccess) return e;
     }
-    return kattn::launch_bwd(a, ctx->num_sms, s, launches);
+    cudaError_t e = tensor ? kattn::launch_bwd_tc(b, ctx->num_sms, ctx->d_status, s, launches)
+                           : kattn::launch_bwd(b, ctx->num_sms, s, launches);
+    if (det) {
+        if (e == cudaSuccess) e = kattn::launch_bwd_dq_reduce(b, key_rows, ctx->num_sms, s, launches);
+        const cudaError_t ef = cudaFreeAsync(b.dq_part, s);
+        if (e == cudaSuccess) e = ef;
+    }
+    return e;
 }
 
 int path_check(const kattn_ctx* ctx, int d) {
@@ -548,6 +566,12 @@ int kattn_set_wait_limit(kattn_ctx* ctx, unsigned long long ns) {
     return KATTN_OK;
 }
 
+int kattn_set_deterministic(kattn_ctx* ctx, int on) {
+    if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    ctx->deterministic.store(on ? 1 : 0);
+    return KATTN_OK;
+}
+
 int kattn_test_withhold_next_load(kattn_ctx* ctx) {
     if (!ctx) return fail(KATTN_ERR_INVALID_ARGUMENT, "ctx is NULL");
     ctx->withhold_next_load.store(1);
@@ -620,6 +644,9 @@ int kattn_bwd_noalloc(kattn_ctx* ctx, const float* q, const float* k, const floa
                     "B*H*T = %ld exceeds the fixed workspace of the allocation-free backward (%ld)", rows,
                     static_cast<long>(KATTN_NOALLOC_MAX_ROWS));
     KATTN_TRY(path_check(ctx, d));
+    if (ctx->deterministic.load(std::memory_order_relaxed))
+        return fail(KATTN_ERR_UNSUPPORTED,
+                    "the deterministic dQ mode needs a per-call workspace: use kattn_bwd on this context");
     DeviceScope scope(ctx->device);
     if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
     kattn::BwdArgs a{q, k, v, ld_qkv, o, dout, ld_o, lse, dq, dk, dv, ld_dqkv, ctx->noalloc_ws,

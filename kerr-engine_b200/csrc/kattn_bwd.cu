@@ -14,6 +14,8 @@
 // dQ.  Kernel 2 (attn_bwd_f32): one CTA per (64-row key tile, slab) keeps K, V
 // and the dK, dV accumulators resident and walks the query tiles on or below
 // the diagonal; dQ partial sums go to global memory with vector reductions.
+#include <algorithm>
+
 #include "kattn_common.cuh"
 #include "kattn_launch.h"
 
@@ -22,6 +24,7 @@ namespace kattn {
 constexpr int BWD_BM = 64;  // query rows per tile
 constexpr int BWD_BN = 64;  // key rows per CTA
 constexpr int BWD_NT = 256;
+static_assert(BWD_BN == kBwdF32KeyRows, "dQ slices of the deterministic mode");
 
 struct BwdParams {
     const float* q;
@@ -33,6 +36,7 @@ struct BwdParams {
     long ld_o;
     const float* lse;
     float* dq;
+    float* dq_part;  // deterministic mode: [key tiles][B*T][H*D] slices, or null
     float* dk;
     float* dv;
     long ld_d;
@@ -304,7 +308,12 @@ __global__ void __launch_bounds__(BWD_NT, (D <= 64 ? 2 : 1)) attn_bwd_f32(const 
                 dqa[3][cc] = fmaf(sc.w, kr.x[cc], dqa[3][cc]);
             }
         }
-        float* dqg = p.dq + row0 * p.ld_d + h * D;
+        // dQ: added into dq, or (deterministic mode) stored into this key
+        // tile's slice for attn_bwd_dq_reduce.
+        const long hd = static_cast<long>(p.H) * D;
+        float* dqg = p.dq_part ? p.dq_part + (static_cast<long>(jt) * p.B * p.T + row0) * hd + h * D
+                               : p.dq + row0 * p.ld_d + h * D;
+        const long ldq = p.dq_part ? hd : p.ld_d;
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
             const int r = q0 + ty * 4 + a;
@@ -312,7 +321,8 @@ __global__ void __launch_bounds__(BWD_NT, (D <= 64 ? 2 : 1)) attn_bwd_f32(const 
                 Frag<DC> f;
 #pragma unroll
                 for (int cc = 0; cc < DC; ++cc) f.x[cc] = dqa[a][cc] * p.scale;
-                f.red_add(dqg + static_cast<long>(r) * p.ld_d + tx * DC);
+                if (p.dq_part) f.store(dqg + static_cast<long>(r) * ldq + tx * DC);
+                else f.red_add(dqg + static_cast<long>(r) * ldq + tx * DC);
             }
         }
     }
@@ -347,6 +357,7 @@ static BwdParams make_params(const BwdArgs& a) {
     p.ld_o = a.ld_o;
     p.lse = a.lse;
     p.dq = a.dq;
+    p.dq_part = a.dq_part;
     p.dk = a.dk;
     p.dv = a.dv;
     p.ld_d = a.ld_d;
@@ -383,6 +394,45 @@ cudaError_t launch_bwd_prep(const BwdArgs& a, int num_sms, cudaStream_t stream, 
         case 128: return launch_prep_d<128>(p, num_sms, stream, launches);
         default: return cudaErrorInvalidValue;
     }
+}
+
+// Deterministic dQ: dq[row][h*D + c] = sum of the key tiles' slices in tile
+// order.  One thread per float4 of dq's H*D columns, grid-stride.
+__global__ void __launch_bounds__(256) attn_bwd_dq_reduce(float* dq, long ld_d, const float* __restrict__ part,
+                                                          long rows, int T, int hd, int n_kt, int key_rows,
+                                                          int causal) {
+    pdl_enter();
+    const int c4 = hd / 4;
+    const long plane = rows * hd;
+    const long total = rows * c4;
+    for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const long r = i / c4;
+        const int c = 4 * static_cast<int>(i - r * c4);
+        const int t = static_cast<int>(r % T);
+        const int jmax = causal ? min(n_kt - 1, t / key_rows) : n_kt - 1;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j <= jmax; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(part + j * plane + r * hd + c);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(dq + r * ld_d + c) = acc;
+    }
+}
+
+cudaError_t launch_bwd_dq_reduce(const BwdArgs& a, int key_rows, int num_sms, cudaStream_t stream, int* launches) {
+    const long rows = static_cast<long>(a.B) * a.T;
+    const int hd = a.H * a.d;
+    const int n_kt = (a.T + key_rows - 1) / key_rows;
+    const long n4 = rows * (hd / 4);
+    const long grid = std::min<long>((n4 + 255) / 256, 8L * (num_sms > 0 ? num_sms : 148));
+    cudaError_t e = launch_pdl(attn_bwd_dq_reduce, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, a.dq,
+                               a.ld_d, static_cast<const float*>(a.dq_part), rows, a.T, hd, n_kt, key_rows, a.causal);
+    if (e == cudaSuccess) *launches += 1;
+    return e;
 }
 
 template <int D>

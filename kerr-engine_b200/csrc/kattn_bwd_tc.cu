@@ -62,6 +62,7 @@ constexpr int NLOAD = 128;  // loader threads (warps 8-11)
 constexpr int NTHREADS = NELEM + NLOAD + 32;
 constexpr int MMA_WARP = (NELEM + NLOAD) / 32;
 constexpr int STAGES = 3;  // query-tile ring depth (Q, dO, lse, D)
+static_assert(BK == kBwdTcKeyRows, "dQ slices of the deterministic mode");
 
 // TMEM columns (512 allocated).  Buffer b: S^T (then P packed) at col_s(b),
 // dP^T (then dS packed) at col_dp(b), dQ tile (M=64 layout) at col_dq(b).
@@ -109,6 +110,7 @@ struct Params {
     const float* lse;
     const float* dsum;
     float* dq;
+    float* dq_part;  // deterministic mode: [key tiles][B*T][H*64] slices, or null
     float* dk;
     float* dv;
     long ld_d;
@@ -270,11 +272,12 @@ __device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, in
 // would wait for this thread's outstanding global operations (the first
 // half's reductions, the next tile's prefetch loads), and the next gradient
 // products wait for this buffer.
+template <bool DET>
 __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int lane, int q0,
-                                            float* dqg, uint64_t* dq_free) {
+                                            float* dqg, long ldq, uint64_t* dq_free) {
     const uint32_t ta = (static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b);
     const int r = q0 + qd * 16 + lane;
-    float* dst = dqg + static_cast<long>(r) * p.ld_d;
+    float* dst = dqg + static_cast<long>(r) * ldq;
     const bool on = lane < 16 && r < p.T;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -287,9 +290,14 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
         }
         if (on) {
 #pragma unroll
-            for (int c = 0; c < 32; c += 4)
-                red_add_v4(dst + 32 * h + c, v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale,
-                           v[c + 3] * p.scale);
+            for (int c = 0; c < 32; c += 4) {
+                if (DET)  // deterministic mode: this key tile's slice, summed in order later
+                    *reinterpret_cast<float4*>(dst + 32 * h + c) =
+                        make_float4(v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale, v[c + 3] * p.scale);
+                else
+                    red_add_v4(dst + 32 * h + c, v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale,
+                               v[c + 3] * p.scale);
+            }
         }
     }
 }
@@ -340,6 +348,8 @@ __device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm
     return mbar_wait_warp(&sm.stg_done, r & 1, p.wait_ns);
 }
 
+// DET: the deterministic dQ mode (slices in p.dq_part instead of reductions into dq).
+template <bool DET>
 __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     // Launched behind attn_bwd_rowdot, whose outputs (D, the zeroed dq) only
     // the loader warps touch: they wait for it; the elementwise warps stage
@@ -404,6 +414,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 const long bh = (static_cast<long>(it.b) * p.H + it.h) * p.T;
                 const bool ok = q0 + t < p.T;
                 lse_t = ok ? p.lse[bh + q0 + t] * kLog2e : INFINITY;
+                // D is read only after this warp's pdl_wait, and attn_bwd_rowdot
+                // writes it only after its own griddepcontrol.wait: calls queued
+                // on one stream may share one workspace array (kattn_bwd_noalloc).
                 ds_t = ok ? p.dsum[bh + q0 + t] : 0.f;
             }
         };
@@ -434,8 +447,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 }
                 tc_fence_after();
                 const Item it = make_item(p, cq.w);
-                float* dqg = p.dq + static_cast<long>(it.b) * p.T * p.ld_d + it.h * D;
-                dq_epilogue(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg, &sm.dq_free[m & 1]);
+                const long hd = static_cast<long>(p.H) * D;
+                float* dqg = DET ? p.dq_part + (static_cast<long>(it.k0 / BK) * p.B + it.b) * p.T * hd + it.h * D
+                                 : p.dq + static_cast<long>(it.b) * p.T * p.ld_d + it.h * D;
+                dq_epilogue<DET>(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg, DET ? hd : p.ld_d,
+                            &sm.dq_free[m & 1]);
                 cq.next(p, c, G);
             }
         }
@@ -648,6 +664,7 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     p.lse = a.lse;
     p.dsum = a.dsum;
     p.dq = a.dq;
+    p.dq_part = a.dq_part;
     p.dk = a.dk;
     p.dv = a.dv;
     p.ld_d = a.ld_d;
@@ -668,16 +685,17 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static std::atomic<uint64_t> attr_done{0};  // one bit per device: the attribute is per device
-    const uint64_t bit = 1ull << (dev & 63);
+    static std::atomic<uint64_t> attr_done{0};  // one bit per device and variant: the attribute is per device
+    const uint64_t bit = 1ull << ((2 * dev + (p.dq_part ? 1 : 0)) & 63);
+    auto kernel = p.dq_part ? attn_bwd_tc64<true> : attn_bwd_tc64<false>;
     if (!(attr_done.load(std::memory_order_relaxed) & bit)) {
-        e = cudaFuncSetAttribute(attn_bwd_tc64, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         attr_done.fetch_or(bit);
     }
     // Persistent: one CTA per SM (the shared-memory footprint allows no more).
     const int grid = static_cast<int>(n_work < num_sms ? n_work : num_sms);
-    e = launch_pdl(attn_bwd_tc64, dim3(static_cast<unsigned>(grid)), dim3(NTHREADS), smem, stream, p);
+    e = launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(NTHREADS), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

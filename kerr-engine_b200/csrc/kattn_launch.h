@@ -62,7 +62,20 @@ struct BwdArgs {
     float scale;
     int causal;
     unsigned long long wait_ns = 1000000000ull;  // wall-time limit of every bounded wait
+    // Deterministic dQ: when set, each key tile's dQ contribution is stored
+    // (not added) into its slice of [key tiles][B*T][H*d] and
+    // launch_bwd_dq_reduce sums the slices in key-tile order into dq.
+    float* dq_part = nullptr;
 };
+
+// Key rows per backward work item (the dQ partial slices of the
+// deterministic mode): tensor-core kernel, FFMA kernel.
+constexpr int kBwdTcKeyRows = 128;
+constexpr int kBwdF32KeyRows = 64;
+
+// dq[b*T + t][h*d + c] = sum over key tiles j (in order; for causal, only
+// j*key_rows <= t) of part[j][b*T + t][h*d + c].
+cudaError_t launch_bwd_dq_reduce(const BwdArgs& a, int key_rows, int num_sms, cudaStream_t stream, int* launches);
 
 // Each returns the CUDA launch status and adds the number of kernels it
 // enqueued to *launches.

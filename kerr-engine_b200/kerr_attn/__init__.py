@@ -38,6 +38,7 @@ PATH_TENSOR = 2
 EXPORTED_SYMBOLS = (
     "kattn_version", "kattn_strerror", "kattn_last_error", "kattn_create", "kattn_destroy",
     "kattn_set_path", "kattn_check_device", "kattn_set_wait_limit", "kattn_test_withhold_next_load",
+    "kattn_set_deterministic",
     "kattn_fwd", "kattn_bwd", "kattn_fwd_host", "kattn_bwd_host", "kattn_last_launch_count",
     "kattn_bwd_noalloc",
     "kattn_linear_fwd", "kattn_linear_bwd_dx", "kattn_linear_bwd_dw",
@@ -97,6 +98,8 @@ def lib():
     L.kattn_check_device.restype = _i
     L.kattn_set_wait_limit.argtypes = [_p, ctypes.c_ulonglong]
     L.kattn_set_wait_limit.restype = _i
+    L.kattn_set_deterministic.argtypes = [_p, _i]
+    L.kattn_set_deterministic.restype = _i
     L.kattn_test_withhold_next_load.argtypes = [_p]
     L.kattn_test_withhold_next_load.restype = _i
     fwd_args = [_p, _p, _p, _p, _l, _p, _l, _p, _i, _i, _i, _i, _fl, _i]
@@ -182,6 +185,10 @@ class Context:
     def set_wait_limit(self, ns: int):
         """Wall-time limit of the tensor-core kernels' bounded waits (0: one second)."""
         _check(lib().kattn_set_wait_limit(self._h, int(ns)), "kattn_set_wait_limit")
+
+    def set_deterministic(self, on: bool = True):
+        """dQ by per-key-tile slices summed in a fixed order (same inputs, same bits)."""
+        _check(lib().kattn_set_deterministic(self._h, 1 if on else 0), "kattn_set_deterministic")
 
     def test_withhold_next_load(self):
         """Diagnostic: the next tensor-core forward withholds its first key-tile
