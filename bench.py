@@ -414,6 +414,7 @@ def run_ours(args):
             dp_step_object(ctx, dev, world, rank, 768, 12, 256, 16, 4, n_steps, n_warm, 3000),
             dp_step_object(ctx, dev, world, rank, 1280, 20, 512, 32, 4, n_steps, n_warm, 4000)]
         line["long_context"] = long_context_object(ctx, dev, world, rank, n_steps, n_warm)
+        line["block_pipeline"] = block_pipeline_object(ctx, dev, world, rank, n_steps, n_warm)
     if world == 1 and not args.no_cpu_baseline:
         cores = os.cpu_count() or 1
         n_seq = min(cores, B)
@@ -572,6 +573,77 @@ def dp_step_object(ctx, dev, world, rank, C, H, T, B, NB, steps, warmup, seed):
             "ms_per_step_without_exchange": alone["ms_per_step"],
             "efficiency_vs_no_exchange": alone["ms_per_step"] / full["ms_per_step"],
             "algorithmic_tflops": flops / (full["ms_per_step"] / 1e3) / 1e12}
+
+
+def block_pipeline_object(ctx, dev, world, rank, steps, warmup, C=768, H=12, T=256, B=16, NB=4, rk4=8):
+    """The device-resident block pipeline (kattn_block_*): the 768-dim
+    model's 4 blocks, each LN1, c_attn, attention, c_proj and the residual,
+    then LN2 and the Kerr-ODE FFN core (rk4_n_steps 8) with its residual,
+    forward through the blocks and backward in reverse, two C-ABI calls per
+    block with every intermediate on the device (the reference's
+    forward_backward_batch, src/pipeline.rs:764-1222, without the FFN's dense
+    maestro layers).  Each rank runs its own 16 sequences: no exchange."""
+    import torch
+
+    import kerr_attn
+    from kerr_attn.dist import max_over_ranks as _max_over_ranks
+    from kerr_attn.dist import sync as _sync
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(5000 + rank)
+    nb = C // 2
+
+    def lin(n_out, n_in):
+        return (torch.rand(n_out, n_in, device=dev, generator=g) * 2 - 1) / math.sqrt(n_in), \
+            torch.zeros(n_out, device=dev)
+
+    params, grads, blocks = [], [], []
+    for _ in range(NB):
+        wa, ba = lin(3 * C, C)
+        wp, bp = lin(C, C)
+        P = {"ln1_w": torch.ones(C, device=dev), "ln1_b": torch.zeros(C, device=dev), "w_attn": wa, "b_attn": ba,
+             "w_proj": wp, "b_proj": bp, "ln2_w": torch.ones(C, device=dev), "ln2_b": torch.zeros(C, device=dev),
+             "gamma_raw": torch.full((nb,), math.log(math.expm1(0.1)), device=dev),
+             "omega": (torch.arange(nb, device=dev, dtype=torch.float32) + 1) / nb,
+             "alpha_beta": torch.tensor([0.1, 0.1], device=dev)}
+        params.append(P)
+        grads.append({k: torch.empty_like(v) for k, v in P.items()})
+        blocks.append(kerr_attn.Block(ctx, B, T, C, H, rk4))
+    hs = [torch.randn(B, T, C, device=dev, generator=g)] + [torch.empty(B, T, C, device=dev) for _ in range(NB)]
+    dy = torch.randn(B, T, C, device=dev, generator=g)
+    dh = torch.empty(B, T, C, device=dev)
+
+    def step():
+        n = 0
+        for i in range(NB):
+            n += blocks[i].fwd(params[i], hs[i], hs[i + 1])
+        src = dy
+        for i in reversed(range(NB)):
+            n += blocks[i].bwd(src, dh, grads[i])
+            src = dh
+        return n
+
+    for _ in range(warmup):
+        step()
+    _sync(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    launches = 0
+    for _ in range(steps):
+        launches += step()
+    t1.record()
+    torch.cuda.synchronize(dev)
+    _sync(dev)
+    ms = _max_over_ranks(t0.elapsed_time(t1), dev) / steps
+    for b in blocks:
+        b.close()
+    del hs, params, grads
+    torch.cuda.empty_cache()
+    return {"workload": f"device-resident block pipeline (kattn_block_fwd / _bwd): n_embd {C}, {H} heads, "
+                        f"seq_len {T}, {B} sequences per GPU, {NB} blocks of LN1, c_attn, causal attention, "
+                        f"c_proj, LN2 and the Kerr-ODE FFN core (rk4_n_steps {rk4}) with residuals, fwd+bwd",
+            "n_gpus": world, "ms_per_step": ms, "tokens_per_s": B * T * world / (ms / 1e3), "steps": steps,
+            "gpu_launches": launches, "exchange": "none (independent sequences per rank)"}
 
 
 LONG_CONTEXT = {"batch": 8, "n_head": 12, "head_dim": 64, "seq_lens": (1024, 2048, 4096)}

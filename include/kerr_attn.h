@@ -319,6 +319,75 @@ int kattn_kerr_ode_bwd_host(kattn_ctx* ctx, const float* dy, long ld_dy, const f
                             float* dx, long ld_dx, float* d_gamma_raw, float* d_omega, float* d_alpha_beta,
                             int M, int n_bands, int n_steps, int accumulate);
 
+/* ---- Device-resident block pipeline ----------------------------------------
+ * One transformer block of the reference's batched pipeline, as far as this
+ * library covers it, run on the device with every intermediate kept there
+ * between the forward and the backward (forward_backward_batch,
+ * src/pipeline.rs:764-1222; per block :236-360 forward, :670-750 backward):
+ *
+ *   x1 = LN1(h);  qkv = c_attn(x1);  o = causal_attention(qkv);
+ *   h1 = h + c_proj(o);
+ *   h_out = h1 + KerrODE(LN2(h1))     (with the FFN; h_out = h1 without)
+ *
+ * The FFN's maestro squeeze / process and out_proj layers are dense layers
+ * outside this library: the FFN runs as its ODE core (KerrWeights), and a
+ * block created with rk4_n_steps = 0 is the attention sublayer alone.  Rows
+ * are positions (M = B*T), contiguous [M][C] arrays; head_dim = C / H;
+ * scale 1/sqrt(head_dim); causal.  Parameters are device pointers in the
+ * reference's layouts (src/model.rs:184-205): w_attn [3C][C], w_proj [C][C],
+ * gamma_raw / omega of C/2 bands, alpha_beta = {alpha, beta}.  Each call
+ * enqueues its kernels on `stream` and returns; nothing synchronises the
+ * host. */
+typedef struct kattn_block kattn_block;
+
+typedef struct {
+    const float* ln1_w;
+    const float* ln1_b;
+    const float* w_attn;
+    const float* b_attn;
+    const float* w_proj;
+    const float* b_proj;
+    const float* ln2_w;      /* FFN only (ignored when rk4_n_steps = 0) */
+    const float* ln2_b;
+    const float* gamma_raw;
+    const float* omega;
+    const float* alpha_beta;
+} kattn_block_params;
+
+/* Gradient outputs, one per parameter above (FFN entries ignored without
+ * the FFN); written, or added to when accumulate != 0. */
+typedef struct {
+    float* ln1_w;
+    float* ln1_b;
+    float* w_attn;
+    float* b_attn;
+    float* w_proj;
+    float* b_proj;
+    float* ln2_w;
+    float* ln2_b;
+    float* gamma_raw;
+    float* omega;
+    float* alpha_beta;
+} kattn_block_grads;
+
+/* Allocates the block's device activations for B x T positions of width C
+ * (x1, qkv, o, lse, h1, x2 and the backward's temporaries: 13 M*C floats
+ * with the FFN, 10 without).  C a multiple of 8, C / H in {32, 64, 128}, C <=
+ * KATTN_LN_MAX_N; rk4_n_steps 0 (no FFN) or the Kerr-ODE's steps. */
+int kattn_block_create(kattn_ctx* ctx, int B, int T, int C, int H, int rk4_n_steps, kattn_block** out);
+int kattn_block_destroy(kattn_block* blk);
+
+/* Forward of h [M][C] into h_out [M][C] (h_out must not alias h).  h and
+ * the parameters must stay unchanged until the matching kattn_block_bwd,
+ * which reads them (the reference's block cache holds the same). */
+int kattn_block_fwd(kattn_ctx* ctx, kattn_block* blk, const kattn_block_params* params, const float* h,
+                    float* h_out, void* stream);
+
+/* Backward of the last forward: dh [M][C] = d(loss)/dh from dh_out =
+ * d(loss)/dh_out (dh may alias dh_out), and the parameter gradients. */
+int kattn_block_bwd(kattn_ctx* ctx, kattn_block* blk, const float* dh_out, float* dh,
+                    const kattn_block_grads* grads, int accumulate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,29 +13,9 @@
 #include <mutex>
 #include <vector>
 
+#include "kattn_internal.h"
 #include "kattn_launch.h"
 #include "kerr_attn.h"
-
-constexpr unsigned long long kDefaultWaitNs = 1000000000ull;  // one second
-
-struct kattn_ctx {
-    int device = 0;
-    int num_sms = 0;
-    std::atomic<int> path{KATTN_PATH_AUTO};
-    int* d_status = nullptr;        // device word set by kernels whose bounded waits give up
-    cudaStream_t stream = nullptr;  // host-buffer entry points: kernels
-    cudaStream_t h2d = nullptr;     // host-buffer entry points: host-to-device copies
-    cudaStream_t d2h = nullptr;     // host-buffer entry points: device-to-host copies
-    std::vector<cudaEvent_t> events;  // chunk hand-offs between those three streams
-    std::mutex host_mu;             // serialises the host-buffer entry points
-    char* arena = nullptr;          // device staging for the host-buffer entry points
-    size_t arena_bytes = 0;
-    float* noalloc_ws = nullptr;    // device address of g_noalloc_ws on this device
-    cudaMemPool_t pool = nullptr;   // the context's own stream-ordered pool for per-call workspace
-    std::atomic<unsigned long long> wait_ns{kDefaultWaitNs};  // limit of the kernels' bounded waits
-    std::atomic<int> withhold_next_load{0};  // diagnostic hook (kattn_test_withhold_next_load)
-    std::atomic<int> deterministic{0};       // dQ by ordered slices (kattn_set_deterministic)
-};
 
 // Device-resident state of one forward (the reference's AttnCache):
 // q/k/v, o and lse, kept for the backward of the same sequences.
@@ -57,12 +37,11 @@ struct kattn_saved {
 // device address comes from cudaGetSymbolAddress (kattn_create, per device).
 static __device__ __align__(256) float g_noalloc_ws[KATTN_NOALLOC_MAX_ROWS];
 
-namespace {
+namespace kattn_abi {
 
 thread_local char g_last_error[512] = "";
 thread_local int g_last_launches = 0;
 
-int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int status, const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -76,20 +55,16 @@ int cuda_fail(cudaError_t e, const char* what) {
     return fail(status, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
-// Makes ctx->device current for the scope of one call and restores the
-// caller's device afterwards.
-struct DeviceScope {
-    int prev = -1;
-    int dev;
-    cudaError_t err = cudaSuccess;
-    explicit DeviceScope(int d) : dev(d) {
-        err = cudaGetDevice(&prev);
-        if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
-    }
-    ~DeviceScope() {
-        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
-    }
-};
+int ok_with_launches(int n) {
+    g_last_launches = n;
+    return KATTN_OK;
+}
+
+}  // namespace kattn_abi
+
+using namespace kattn_abi;
+
+namespace {
 
 constexpr int kTile = 64;  // query / key tile rows of the kernels
 
@@ -162,11 +137,6 @@ int bwd_checks(const kattn_ctx* ctx, const float* q, const float* k, const float
     KATTN_TRY(check_tensor("dq", dq, ld_d, C, device));
     KATTN_TRY(check_tensor("dk", dk, ld_d, C, device));
     KATTN_TRY(check_tensor("dv", dv, ld_d, C, device));
-    return KATTN_OK;
-}
-
-int ok_with_launches(int n) {
-    g_last_launches = n;
     return KATTN_OK;
 }
 

@@ -45,6 +45,7 @@ EXPORTED_SYMBOLS = (
     "kattn_saved_create", "kattn_saved_destroy", "kattn_fwd_host_save", "kattn_bwd_host_saved",
     "kattn_layernorm_fwd", "kattn_layernorm_bwd",
     "kattn_kerr_ode_fwd", "kattn_kerr_ode_bwd", "kattn_kerr_ode_fwd_host", "kattn_kerr_ode_bwd_host",
+    "kattn_block_create", "kattn_block_destroy", "kattn_block_fwd", "kattn_block_bwd",
 )
 
 # Widest row kattn_layernorm_fwd / _bwd accept (KATTN_LN_MAX_N).
@@ -116,6 +117,14 @@ def lib():
     L.kattn_bwd_host.restype = _i
     L.kattn_saved_create.argtypes = [_p, ctypes.POINTER(_p)]
     L.kattn_saved_create.restype = _i
+    L.kattn_block_create.argtypes = [_p, _i, _i, _i, _i, _i, ctypes.POINTER(_p)]
+    L.kattn_block_create.restype = _i
+    L.kattn_block_destroy.argtypes = [_p]
+    L.kattn_block_destroy.restype = _i
+    L.kattn_block_fwd.argtypes = [_p, _p, ctypes.POINTER(BlockParams), _p, _p, _p]
+    L.kattn_block_fwd.restype = _i
+    L.kattn_block_bwd.argtypes = [_p, _p, _p, _p, ctypes.POINTER(BlockGrads), _i, _p]
+    L.kattn_block_bwd.restype = _i
     L.kattn_saved_destroy.argtypes = [_p]
     L.kattn_saved_destroy.restype = _i
     L.kattn_fwd_host_save.argtypes = [_p, _p] + fwd_args[1:]
@@ -577,3 +586,101 @@ def kerr_ode_bwd_host(ctx: Context, dy, x, gamma_raw, omega, alpha: float, beta:
                                        _vec(d_alpha_beta, "d_alpha_beta"), M, nb, int(n_steps), int(accumulate))
     _check(st, "kattn_kerr_ode_bwd_host")
     return last_launch_count()
+
+
+# Parameter / gradient tables of kattn_block_fwd / _bwd (kattn_block_params /
+# kattn_block_grads in include/kerr_attn.h), in declaration order.
+BLOCK_FIELDS = ("ln1_w", "ln1_b", "w_attn", "b_attn", "w_proj", "b_proj", "ln2_w", "ln2_b", "gamma_raw", "omega",
+                "alpha_beta")
+
+
+class BlockParams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in BLOCK_FIELDS]
+
+
+class BlockGrads(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in BLOCK_FIELDS]
+
+
+def _table(cls, tensors: dict, ffn: bool):
+    t = cls()
+    for n in BLOCK_FIELDS:
+        x = tensors.get(n)
+        if x is None:
+            if ffn or n in BLOCK_FIELDS[:6]:
+                raise ValueError(f"{n} is required")
+            continue
+        if not (x.is_cuda and x.dtype == _f32() and x.is_contiguous()):
+            raise ValueError(f"{n} must be a contiguous float32 CUDA tensor")
+        setattr(t, n, x.data_ptr())
+    return t
+
+
+def _f32():
+    import torch
+    return torch.float32
+
+
+class Block:
+    """Device-resident transformer block (kattn_block_*): LN1, c_attn,
+    causal attention, c_proj and the residual, then, with rk4_n_steps > 0,
+    LN2 and the Kerr-ODE FFN core with its residual; every intermediate stays
+    on the device between :meth:`fwd` and :meth:`bwd` (the reference's
+    forward_backward_batch, src/pipeline.rs:764-1222, per block)."""
+
+    def __init__(self, ctx: Context, B: int, T: int, C: int, n_head: int, rk4_n_steps: int = 0):
+        h = ctypes.c_void_p()
+        _check(lib().kattn_block_create(ctx.handle, B, T, C, n_head, rk4_n_steps, ctypes.byref(h)),
+               "kattn_block_create")
+        self._h = h
+        self.ctx = ctx
+        self.shape = (B, T, C)
+        self.ffn = rk4_n_steps > 0
+        self._keep = None
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise RuntimeError("block is closed")
+        return self._h
+
+    def _rows(self, x, name):
+        B, T, C = self.shape
+        if not (x.is_cuda and x.dtype == _f32() and x.is_contiguous() and x.numel() == B * T * C):
+            raise ValueError(f"{name} must be a contiguous float32 CUDA tensor of {B * T * C} elements")
+        return x.data_ptr()
+
+    def fwd(self, params: dict, h, h_out, stream=None) -> int:
+        """h_out = block(h); h and params must stay unchanged until :meth:`bwd`."""
+        t = _table(BlockParams, params, self.ffn)
+        self._keep = (params, h)  # the backward reads them
+        st = lib().kattn_block_fwd(self.ctx.handle, self.handle, ctypes.byref(t), self._rows(h, "h"),
+                                   self._rows(h_out, "h_out"), _stream_ptr(stream, h.device))
+        _check(st, "kattn_block_fwd")
+        return last_launch_count()
+
+    def bwd(self, dh_out, dh, grads: dict, accumulate: bool = False, stream=None) -> int:
+        """dh = d(loss)/dh from dh_out (dh may be dh_out); parameter gradients into `grads`."""
+        t = _table(BlockGrads, grads, self.ffn)
+        st = lib().kattn_block_bwd(self.ctx.handle, self.handle, self._rows(dh_out, "dh_out"), self._rows(dh, "dh"),
+                                   ctypes.byref(t), int(accumulate), _stream_ptr(stream, dh.device))
+        _check(st, "kattn_block_bwd")
+        return last_launch_count()
+
+    def close(self):
+        if self._h is not None:
+            st = lib().kattn_block_destroy(self._h)
+            self._h = None
+            _check(st, "kattn_block_destroy")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

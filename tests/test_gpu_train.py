@@ -9,7 +9,9 @@ same runs on the oracle:
   64 tokens from a seeded Zipf(1.0) stream drawn as the reference samples;
 - a stack of the path's own layers (tests/train_stack.py): LN1, c_attn,
   causal attention, c_proj, LN2 and the Kerr-ODE per block, four blocks, SGD
-  on an MSE target, at the 128-dim shapes (head_dim 32) and at head_dim 64.
+  on an MSE target, at the 128-dim shapes (head_dim 32) and at head_dim 64,
+  once composed call by call and once through the device-resident block
+  pipeline (kattn_block_fwd / _bwd).
 
 Every forward and backward op of the path goes through the C ABI on the GPU
 side.
@@ -42,6 +44,18 @@ def test_loss_curve_matches_oracle(oracle_lib, B, T, C, H):
     ref, got = np.array(ref), np.array(got)
     assert np.isfinite(got).all()
     assert ref[-1] < 0.6 * ref[0]  # the run learns
+    rel = np.abs(got - ref) / ref
+    assert rel.max() < 1e-3, f"worst step {rel.argmax()}: {got[rel.argmax()]} vs {ref[rel.argmax()]}"
+
+
+def test_loss_curve_native_block_pipeline(oracle_lib):
+    """The same 50-step run with each block as one kattn_block_fwd /
+    kattn_block_bwd pair (the device-resident pipeline), head_dim 64."""
+    B, T, C, H = 2, 128, 256, 4
+    blocks, h0, target = train_stack.init(B, T, C, H, 4, seed=42)
+    ref = np.array(train_stack.train_oracle(blocks, h0, target, H, STEPS, LR))
+    got = np.array(train_stack.train_gpu_native(blocks, h0, target, H, STEPS, LR))
+    assert np.isfinite(got).all()
     rel = np.abs(got - ref) / ref
     assert rel.max() < 1e-3, f"worst step {rel.argmax()}: {got[rel.argmax()]} vs {ref[rel.argmax()]}"
 

@@ -174,3 +174,46 @@ def train_gpu(blocks, h0, target, H, n_steps, lr, rk4_steps=8, device=0):
         ctx.close()
     assert nb == P[0]["omega"].numel()
     return losses
+
+
+def train_gpu_native(blocks, h0, target, H, n_steps, lr, rk4_steps=8, device=0):
+    """train_gpu on the device-resident block pipeline: each block's forward
+    and backward are one kattn_block_fwd / kattn_block_bwd call (every
+    intermediate stays in the library's block object); the loss and the SGD
+    update are torch elementwise ops."""
+    import torch
+
+    import kerr_attn
+
+    dev = torch.device("cuda", device)
+    B, T, C = h0.shape
+    names = {"ln1_w": "ln1_w", "ln1_b": "ln1_b", "w_attn": "wa", "b_attn": "ba", "w_proj": "wp", "b_proj": "bp",
+             "ln2_w": "ln2_w", "ln2_b": "ln2_b", "gamma_raw": "gamma_raw", "omega": "omega",
+             "alpha_beta": "alpha_beta"}
+    P = [{n: torch.from_numpy(b[k].copy()).to(dev) for n, k in names.items()} for b in blocks]
+    G = [{n: torch.empty_like(v) for n, v in p.items()} for p in P]
+    tgt = torch.from_numpy(target).to(dev)
+    hs = [torch.from_numpy(h0).to(dev)] + [torch.empty(B, T, C, device=dev) for _ in blocks]
+    dh = torch.empty(B, T, C, device=dev)
+    ctx = kerr_attn.Context(device)
+    objs = [kerr_attn.Block(ctx, B, T, C, H, rk4_steps) for _ in blocks]
+    losses = []
+    try:
+        for _ in range(n_steps):
+            for i, o in enumerate(objs):
+                o.fwd(P[i], hs[i], hs[i + 1])
+            diff = hs[-1] - tgt
+            losses.append(float((diff.double() ** 2).mean().item() / 2))
+            dh.copy_(diff / diff.numel())
+            for i in reversed(range(len(objs))):
+                objs[i].bwd(dh, dh, G[i])
+            for p, g in zip(P, G):
+                for n in g:
+                    p[n] -= float(np.float32(lr * LR_SCALE.get(names[n], 1.0))) * g[n]
+        torch.cuda.synchronize(dev)
+        ctx.check_device()
+    finally:
+        for o in objs:
+            o.close()
+        ctx.close()
+    return losses
