@@ -101,6 +101,25 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int c0, 
         : "memory");
 }
 
+// Tiled 3-D store of one box from this CTA's shared memory to `map` at
+// coordinates (c0 innermost, c1, c2); elements outside the tensor are not
+// written.  Async proxy, tracked by bulk groups: the calling thread's later
+// memory operations and arrives do not wait for it.  The writers of the box
+// must have issued fence_async_smem before the store.
+__device__ __forceinline__ void tma_store_3d(const void* map, const void* src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+// Closes the bulk group of the stores issued so far.
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk group has finished reading shared memory
+// (the source may then be overwritten; the global writes may still be in flight).
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every committed bulk group has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Brings a tensor map (address of a __grid_constant__ parameter) into the
 // TMA unit's descriptor cache ahead of its first copy.
 __device__ __forceinline__ void prefetch_tensormap(const void* map) {
