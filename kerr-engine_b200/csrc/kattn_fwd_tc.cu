@@ -219,7 +219,11 @@ __device__ __forceinline__ void load_tile(const CUtensorMap& map, void* dst, uin
 }
 
 __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_constant__ Params p) {
-    pdl_enter();
+    // The next grid may launch at once (it waits for this one before it
+    // touches memory); this grid's setup below touches no global memory, so
+    // it runs while the grid before still drains, and every thread waits
+    // for that grid (griddepcontrol.wait) before its first global access.
+    pdl_launch();
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -250,6 +254,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_wait();
     const uint32_t tm = sm.tmem_slot;
     bool failed = false;
 

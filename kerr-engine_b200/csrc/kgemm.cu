@@ -196,7 +196,11 @@ __device__ __forceinline__ void load_a(const GParams& p, int m0, int q, int h, i
 
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constant__ GParams p) {
-    pdl_enter();
+    // The next grid may launch at once (it waits for this one before it
+    // touches memory); this grid's setup below touches no global memory, so
+    // it runs while the grid before still drains, and every thread waits
+    // for that grid (griddepcontrol.wait) before its first global access.
+    pdl_launch();
     extern __shared__ uint8_t smem_raw[];
     GSmem& sm = *reinterpret_cast<GSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x;
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_bf16x3(const __grid_constan
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_wait();
     const uint32_t tm = sm.tmem_slot;
     bool failed = false;
 
