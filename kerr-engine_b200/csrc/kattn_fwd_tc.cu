@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 // TMEM loads are warp-collective: every warp loads, the warps
-                // of the rows in this round stage.
+                // of the rows in this half stage.
                 {
                     float ov[32];
                     tmem_ld32(lane_base + tm + COL_O + 32 * hf, ov);
