@@ -15,8 +15,15 @@
 //   P = exp2(S^T * scale*log2e - lse*log2e),  dS = P * (dP^T - D)   (threads)
 //   dV  += P^T dO     M=128 N=64 K=64    TS: P from TMEM, dO MN-major
 //   dK  += dS^T Q     M=128 N=64 K=64    TS: dS from TMEM, Q MN-major
-//   dQ_i = dS K       M=64  N=64 K=128   SS: dS^T (shared) read MN-major, K MN-major;
+//   dQ_i = dS K       M=128 N=64 K=128   SS: stacked dS (below), K MN-major;
 //                     added into global dq with vector reductions.
+// The dQ product's A operand stacks dS hi and lo as 128 rows, so two MMAs
+// per 16 keys (times K hi, times K lo) form every term of the split product:
+// stacked row 32*qd + l (l < 16) is dS_hi of query 16*qd + l and row
+// 32*qd + 16 + l its dS_lo, so both parts of a query's dQ land in one warp's
+// TMEM lane quadrant and a shuffle adds them.  In shared memory the rows are
+// MN-major atoms: sh[b] holds stacked rows 0-63 (queries 0-31), sl[b] rows
+// 64-127 (queries 32-63), each [key][64 bf16], 128B-swizzled.
 // D = rowsum(dO * O) and the zeroed dq come from attn_bwd_rowdot.
 //
 // Warp roles (416 threads, one CTA per SM):
@@ -36,7 +43,7 @@
 //               its TMEM buffer is free; a tile's gradients as soon as its P
 //               and dS are written).
 // Everything a query tile touches is double-buffered (S^T / dP^T in TMEM,
-// dS^T in shared memory, the dQ accumulator in TMEM), so the tensor core runs
+// the stacked dS in shared memory, the dQ accumulator in TMEM), so the tensor core runs
 // tile i's gradient products while the elementwise warps work on tile i+1.
 // P and dS are packed over their own S^T / dP^T columns: for query columns
 // 16c..16c+15, bf16 hi goes to columns 16c..16c+7 and lo to 16c+8..16c+15,
@@ -82,8 +89,8 @@ struct alignas(1024) Smem {
     uint8_t ql[STAGES][BQ * 128];
     uint8_t gh[STAGES][BQ * 128];  // dO
     uint8_t gl[STAGES][BQ * 128];
-    uint8_t sh[2][BK * 128];  // dS^T [key][64 queries], per TMEM buffer
-    uint8_t sl[2][BK * 128];
+    uint8_t sh[2][BK * 128];  // stacked dS, rows 0-63, [key][64], per TMEM buffer
+    uint8_t sl[2][BK * 128];  // stacked dS, rows 64-127
     float lse2[STAGES][BQ];  // lse * log2(e), +inf beyond T
     float dsum[STAGES][BQ];  // D, 0 beyond T
     uint64_t kv_full;  // an item's K / V staged (phase r: the CTA's item r)
@@ -184,12 +191,15 @@ struct Descs {
     uint64_t kh, kl, vh, vl;      // K / V, K-major (S^T, dP^T A operands)
     uint64_t kh_mn, kl_mn;        // K, MN-major (dQ B operand)
     uint64_t qh, ql, gh, gl;      // Q / dO ring stage 0, K-major; stage s is STAGE_BYTES * s further
-    uint64_t s0h, s0l, s1h, s1l;  // dS^T buffer 0 / 1, MN-major (dQ A)
+    uint64_t s0, s1;              // stacked dS hi / lo of buffer 0 / 1, MN-major (dQ A, M=128)
 };
 
 constexpr uint32_t STAGE_BYTES = BQ * 128;  // one stage of one Q / dO tile
 constexpr uint32_t MN_LBO_Q = BQ * 128;     // leading-byte offset of a 64-row MN-major tile
 constexpr uint32_t MN_LBO_K = BK * 128;
+// The dQ product's A operand (M=128) is two 64-row MN-major atoms: sh[b]
+// (atom 0) and sl[b] (atom 1), this far apart.
+constexpr uint32_t DQ_A_LBO = 2 * BK * 128;
 
 __device__ __forceinline__ uint64_t as_mn(uint64_t kdesc, uint32_t lbo) {
     return (kdesc & ~(static_cast<uint64_t>(0x3FFFu) << 16)) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16);
@@ -206,10 +216,8 @@ __device__ __forceinline__ void make_descs(const Smem& sm, Descs& d) {
     d.ql = smem_desc(smem_u32(sm.ql[0]), 16, 1024);
     d.gh = smem_desc(smem_u32(sm.gh[0]), 16, 1024);
     d.gl = smem_desc(smem_u32(sm.gl[0]), 16, 1024);
-    d.s0h = smem_desc(smem_u32(sm.sh[0]), MN_LBO_K, 1024);
-    d.s0l = smem_desc(smem_u32(sm.sl[0]), MN_LBO_K, 1024);
-    d.s1h = smem_desc(smem_u32(sm.sh[1]), MN_LBO_K, 1024);
-    d.s1l = smem_desc(smem_u32(sm.sl[1]), MN_LBO_K, 1024);
+    d.s0 = smem_desc(smem_u32(sm.sh[0]), DQ_A_LBO, 1024);
+    d.s1 = smem_desc(smem_u32(sm.sh[1]), DQ_A_LBO, 1024);
 }
 
 // S^T and dP^T of the query tile in ring stage s into TMEM buffer b.
@@ -231,17 +239,20 @@ __device__ __forceinline__ void issue_sdp(const Descs& d, uint32_t tm, int s, in
     }
 }
 
-// dQ_b = dS K (dS^T of buffer b from shared memory, K MN-major).
+// dQ_b = dS K as one M=128 product per K half: A stacks dS hi and lo (128
+// rows, see the header), so [dS_hi; dS_lo] (K_hi + K_lo) accumulates
+// dS_hi K and dS_lo K in separate TMEM lanes, which the read-out adds.  Two
+// M=128 MMAs per 16 keys instead of three M=64 ones, at the same cost per
+// MMA; the extra lo*lo term only adds precision.
 __device__ __forceinline__ void issue_dq(const Descs& d, uint32_t tm, int b) {
-    constexpr uint32_t idesc_q = idesc_bf16(BQ, D, 1, 1);
+    constexpr uint32_t idesc_q = idesc_bf16(2 * BQ, D, 1, 1);
     const uint32_t cq = tm + col_dq(b);
-    const uint64_t sh = b ? d.s1h : d.s0h, sl = b ? d.s1l : d.s0l;
+    const uint64_t sa = b ? d.s1 : d.s0;
 #pragma unroll
     for (int ks = 0; ks < BK / 16; ++ks) {
         const uint32_t o = ks * 2048;
-        mma_ss(cq, desc_add(sh, o), desc_add(d.kh_mn, o), idesc_q, ks > 0);
-        mma_ss(cq, desc_add(sh, o), desc_add(d.kl_mn, o), idesc_q, 1);
-        mma_ss(cq, desc_add(sl, o), desc_add(d.kh_mn, o), idesc_q, 1);
+        mma_ss(cq, desc_add(sa, o), desc_add(d.kh_mn, o), idesc_q, ks > 0);
+        mma_ss(cq, desc_add(sa, o), desc_add(d.kl_mn, o), idesc_q, 1);
     }
 }
 
@@ -265,9 +276,12 @@ __device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, in
     }
 }
 
-// A dQ tile (M=64 accumulator: query row 16*qd + l sits in lane 32*qd + l,
+// A dQ tile (the stacked M=128 accumulator: query row 16*qd + l has its
+// dS_hi K part in lane 32*qd + l and its dS_lo K part in lane 32*qd + 16 + l,
 // l < 16), scaled and added into dq by the loader warp of lane quadrant qd,
-// 32 columns at a time.  The TMEM buffer is released on `dq_free` as soon as
+// 32 columns at a time.  Lanes l and l + 16 swap half of their columns, so
+// lane l sums columns 0-15 of the 32 and lane l + 16 columns 16-31.
+// The TMEM buffer is released on `dq_free` as soon as
 // both halves are in registers, with a relaxed arrive: a release arrive
 // would wait for this thread's outstanding global operations (the first
 // half's reductions, the next tile's prefetch loads), and the next gradient
@@ -276,9 +290,10 @@ template <bool DET>
 __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int lane, int q0,
                                             float* dqg, long ldq, uint64_t* dq_free) {
     const uint32_t ta = (static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b);
-    const int r = q0 + qd * 16 + lane;
-    float* dst = dqg + static_cast<long>(r) * ldq;
-    const bool on = lane < 16 && r < p.T;
+    const bool up = lane >= 16;  // sums columns 16-31 of each 32
+    const int r = q0 + qd * 16 + (lane & 15);
+    float* dst = dqg + static_cast<long>(r) * ldq + (up ? 16 : 0);
+    const bool on = r < p.T;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         float v[32];
@@ -288,15 +303,20 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
             tc_fence_before();
             mbar_arrive_relaxed(dq_free);
         }
-        if (on) {
 #pragma unroll
-            for (int c = 0; c < 32; c += 4) {
+        for (int c = 0; c < 16; c += 4) {
+            float x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float keep = up ? v[16 + c + u] : v[c + u];
+                const float send = up ? v[c + u] : v[16 + c + u];
+                x[u] = (keep + __shfl_xor_sync(0xffffffffu, send, 16)) * p.scale;
+            }
+            if (on) {
                 if (DET)  // deterministic mode: this key tile's slice, summed in order later
-                    *reinterpret_cast<float4*>(dst + 32 * h + c) =
-                        make_float4(v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale, v[c + 3] * p.scale);
+                    *reinterpret_cast<float4*>(dst + 32 * h + c) = make_float4(x[0], x[1], x[2], x[3]);
                 else
-                    red_add_v4(dst + 32 * h + c, v[c] * p.scale, v[c + 1] * p.scale, v[c + 2] * p.scale,
-                               v[c + 3] * p.scale);
+                    red_add_v4(dst + 32 * h + c, x[0], x[1], x[2], x[3]);
             }
         }
     }
@@ -304,10 +324,10 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
 
 // dK, dV of the CTA's item r -> global, by the elementwise warps.  Warp
 // (qd, hf) reads its 32 key rows x 32 columns of each accumulator (TMEM loads
-// are warp-collective and run on every lane) into the idle dS^T buffers, laid
+// are warp-collective and run on every lane) into the idle stacked-dS buffers, laid
 // out [row][16 float4] with the float4 index XOR-swizzled by row; then the 256
 // threads store whole 256-byte rows, two per warp instruction.  Rows past T
-// are not stored.  The dS^T buffers are free: the item's last dQ product has
+// are not stored.  Those buffers are free: the item's last dQ product has
 // completed and the next item's tiles are written by these same warps after
 // the second barrier.  The barriers are mbarriers with bounded waits, so a
 // warp that gave up earlier cannot leave the others blocked.
@@ -344,7 +364,7 @@ __device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm
             *reinterpret_cast<float4*>(dkg + r * p.ld_d + c4 * 4) = g;
         }
     }
-    mbar_arrive(&sm.stg_done);  // staging reads done before the next tile's dS^T writes
+    mbar_arrive(&sm.stg_done);  // staging reads done before the next tile's dS writes
     return mbar_wait_warp(&sm.stg_done, r & 1, p.wait_ns);
 }
 
@@ -515,6 +535,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         const int hf = warp >> 2;         // query columns 32*hf..+31 (two 16-column chunks)
         const int row = qd * 32 + lane;   // key row inside the tile
         const uint32_t lb = static_cast<uint32_t>(qd * 32) << 16;
+        // Offset from sh[0] of this thread's key row in the stacked-dS atom hf
+        // of buffer 0 (sl[0] is 2*BK*128 bytes after sh[0]; buffer 1 is BK*128
+        // bytes further).
+        const uint32_t ds_off = (hf ? 2 * BK * 128 : 0) + row * 128;
+        const uint32_t ds_sw = static_cast<uint32_t>(row & 7);
         int w = item_id(c, 0, G);
         Item it = make_item(p, w);
         {
@@ -539,7 +564,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                     break;
                 }
                 if (g >= 2 && !mbar_wait_warp(&sm.bar_d[buf], ((g - 2) >> 1) & 1, p.wait_ns)) {
-                    failed = true;  // dS^T buffer `buf` is read by tile g-2's dQ product
+                    failed = true;  // dS buffer `buf` is read by tile g-2's dQ product
                     break;
                 }
                 tc_fence_after();
@@ -590,13 +615,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                     tmem_st8(cs + 16 * cc + 8, pl);
                     tmem_st8(cp + 16 * cc, gh);
                     tmem_st8(cp + 16 * cc + 8, gl);
-                    // dS^T row for the dQ product: query chunks 4*hf + 2*cc, +1.
+                    // Key row of the stacked dS operand of the dQ product
+                    // (see the header): queries 32*hf + 16*cc.. go to
+                    // atom hf (sh[buf] or sl[buf]), hi in chunks 4*cc, +1 and
+                    // lo in chunks 4*cc + 2, +3.
+                    uint8_t* const dsr = sm.sh[0] + ds_off + buf * (BK * 128);
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
-                        const uint32_t off = sw128(row, 4 * hf + 2 * cc + u);
-                        *reinterpret_cast<uint4*>(sm.sh[buf] + off) =
+                        *reinterpret_cast<uint4*>(dsr + (((4 * cc + u) ^ ds_sw) << 4)) =
                             make_uint4(gh[4 * u], gh[4 * u + 1], gh[4 * u + 2], gh[4 * u + 3]);
-                        *reinterpret_cast<uint4*>(sm.sl[buf] + off) =
+                        *reinterpret_cast<uint4*>(dsr + (((4 * cc + 2 + u) ^ ds_sw) << 4)) =
                             make_uint4(gl[4 * u], gl[4 * u + 1], gl[4 * u + 2], gl[4 * u + 3]);
                     }
                 }
