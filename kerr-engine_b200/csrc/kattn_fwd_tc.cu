@@ -9,7 +9,8 @@
 // Work item = 128 query rows of one (batch, head) slab.  The kernel is
 // persistent: two CTAs per SM, CTA c taking items c, 2G-1-c, 2G+c, ... of the
 // list ordered longest first (a snake order: at the 768-dim shape 192 CTAs
-// run one long item, 88 run two short ones).  g numbers the CTA's 64-row key
+// run one long item, 88 run two short ones; block b acts as CTA G-1-b, so
+// the two-item CTAs launch first).  g numbers the CTA's 64-row key
 // tiles across its items; tile g uses K stage g&1, V stage g&1 and TMEM
 // buffers g&1.
 //
@@ -229,7 +230,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
-    const int cta = static_cast<int>(blockIdx.x);
+    // Block b walks the item list as CTA G-1-b, so the CTAs with two short
+    // items have the lowest block indices.  Of two CTAs sharing an SM, the
+    // warp scheduler favours the one launched first: with the two-item CTAs
+    // launched second, their first item ran at ~1.4 us per tile against
+    // ~0.8 us, and the kernel ended on their lone second item.
+    const int cta = static_cast<int>(gridDim.x - 1 - blockIdx.x);
     const int G = static_cast<int>(gridDim.x);
 
     if (warp == 0) {
