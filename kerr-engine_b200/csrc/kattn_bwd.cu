@@ -58,14 +58,16 @@ constexpr int ROWDOT_U = 1;
 
 template <int D>
 __global__ void __launch_bounds__(256) attn_bwd_rowdot(const BwdParams p) {
-    // The backward kernel behind this one may launch at once: it waits for
-    // this grid before it reads D or dq, and this grid finishes only after
-    // the grid before it (the one that wrote o) has.  D must be written only
-    // after this wait: kattn_bwd_noalloc hands every call the same workspace
-    // array, and the previous call's backward kernel, which reads it, is (or
-    // precedes) the grid waited for here.
-    pdl_launch();
+    // Wait for the grid before (the one that wrote o, dout or q, k, v), then
+    // let the backward kernel behind this one launch.  That order matters:
+    // attn_bwd_tc64 stages K and V before its own griddepcontrol.wait, which
+    // is safe only because no grid before this one is still running once
+    // this grid has passed its wait.  D must also be written only after this
+    // wait: kattn_bwd_noalloc hands every call the same workspace array, and
+    // the previous call's backward kernel, which reads it, is (or precedes)
+    // the grid waited for here.
     pdl_wait();
+    pdl_launch();
     constexpr int LPR = D / 4;
     constexpr int RPW = 32 / LPR;
     constexpr int U = ROWDOT_U;

@@ -373,7 +373,9 @@ template <bool DET>
 __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     // Launched behind attn_bwd_rowdot, whose outputs (D, the zeroed dq) only
     // the loader warps touch: they wait for it; the elementwise warps stage
-    // the first item's K / V meanwhile.
+    // the first item's K / V meanwhile.  Those reads need no wait: rowdot
+    // lets this grid launch only after its own griddepcontrol.wait, so every
+    // grid before rowdot has finished by now.
     pdl_launch();
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -47,10 +47,10 @@ __device__ __forceinline__ void pdl_enter() {
 // The two halves of pdl_enter, for a kernel whose threads do not all read
 // what the grid before it wrote: pdl_launch lets the next grid start
 // launching; pdl_wait blocks the calling thread until the grid before has
-// finished and its memory is visible.  The grid before that one has finished
-// as soon as this grid is running (that grid waited for it before letting
-// this one launch), so only the immediately preceding grid's outputs need
-// pdl_wait.
+// finished and its memory is visible.  A kernel that calls pdl_launch first
+// reads global memory only after its own pdl_wait: the grid before it may
+// itself still be waiting for its predecessor.  (attn_bwd_rowdot waits
+// before it launches the next grid, whose K / V staging relies on that.)
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
