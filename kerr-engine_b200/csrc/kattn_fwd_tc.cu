@@ -425,8 +425,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 const float4 x = *reinterpret_cast<const float4*>(box + ((c ^ (rl & 7)) << 4));
-                split2(x.x * p.scale_log2, x.y * p.scale_log2, qh[2 * c], ql[2 * c]);
-                split2(x.z * p.scale_log2, x.w * p.scale_log2, qh[2 * c + 1], ql[2 * c + 1]);
+                split2_x2(x.x * p.scale_log2, x.y * p.scale_log2, qh[2 * c], ql[2 * c]);
+                split2_x2(x.z * p.scale_log2, x.w * p.scale_log2, qh[2 * c + 1], ql[2 * c + 1]);
             }
             tmem_st16(lane_base + tm + Q_HI + 16 * hf, qh);
             tmem_st16(lane_base + tm + Q_LO + 16 * hf, ql);
@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 }
 
                 // (2) Softmax of this half of S_g: row max (masked columns to
-                // -inf, eight independent chains), combined with the other
+                // -inf, three-input maxima), combined with the other
                 // half's; then the probabilities, packed bf16 hi / lo over the
                 // 32 S columns just read (hi in the first 16, lo in the next).
                 bad |= !mbar_wait(&sm.bar_s[bf], (g >> 1) & 1, p.wait_ns);
@@ -507,13 +507,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 }
                 float mx[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) mx[u] = fmaxf(sv[u], sv[u + 8]);
+                for (int u = 0; u < 8; ++u) mx[u] = max3(sv[u], sv[u + 8], sv[u + 16]);
 #pragma unroll
-                for (int i = 16; i < 32; i += 8)
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], sv[i + u]);
-                sm.red[bf][hf][rl] = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                for (int u = 0; u < 4; ++u) mx[u] = max3(mx[u], mx[u + 4], sv[u + 24]);
+                mx[0] = max3(mx[0], sv[28], sv[29]);
+                mx[1] = max3(mx[1], sv[30], sv[31]);
+                sm.red[bf][hf][rl] = fmaxf(max3(mx[0], mx[1], mx[2]), mx[3]);
                 if (named_sync_or(1, NSM, bad)) {
                     failed = true;
                     break;
@@ -528,22 +527,28 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                     mu = mn;
                 }
                 const float ms = (mu == -INFINITY) ? 0.f : mu;
-                float acc8[8];
+                // Four packed partial sums (eight lanes); arguments and sums as
+                // packed f32x2 operations.
+                uint64_t acc2[4];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) acc8[u] = 0.f;
+                for (int u = 0; u < 4; ++u) acc2[u] = f2_pack(0.f, 0.f);
                 {
+                    const uint64_t ms2 = f2_pack(ms, ms);
                     uint32_t ph[16], pl[16];
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
-                        const float e0 = ex2(sv[i] - ms), e1 = ex2(sv[i + 1] - ms);
-                        acc8[(i >> 1) & 7] += e0 + e1;
-                        split2(e0, e1, ph[i / 2], pl[i / 2]);
+                        float d0, d1;
+                        f2_unpack(f2_sub(f2_pack(sv[i], sv[i + 1]), ms2), d0, d1);
+                        const float e0 = ex2(d0), e1 = ex2(d1);
+                        acc2[(i >> 1) & 3] = f2_add(acc2[(i >> 1) & 3], f2_pack(e0, e1));
+                        split2_x2(e0, e1, ph[i / 2], pl[i / 2]);
                     }
                     tmem_st16(cs, ph);
                     tmem_st16(cs + 16, pl);
                 }
-                const float rs =
-                    ((acc8[0] + acc8[1]) + (acc8[2] + acc8[3])) + ((acc8[4] + acc8[5]) + (acc8[6] + acc8[7]));
+                float r0, r1;
+                f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), r0, r1);
+                const float rs = r0 + r1;
                 l = (j == 0) ? rs : l * alpha + rs;
 
                 // (3) Rescale this half of O if a row of this warp raised mu

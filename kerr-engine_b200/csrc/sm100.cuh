@@ -330,10 +330,60 @@ __device__ __forceinline__ uint32_t pack_bf16(float even, float odd) {
 __device__ __forceinline__ float bf16_lo_f(uint32_t packed) { return __uint_as_float(packed << 16); }
 __device__ __forceinline__ float bf16_hi_f(uint32_t packed) { return __uint_as_float(packed & 0xFFFF0000u); }
 
+// ---------------------------------------------------------------- f32x2
+// Two f32 lanes in one 64-bit register pair for the packed sm_100
+// instructions (add / sub / mul / fma .rn.f32x2): each lane is rounded
+// exactly as the scalar instruction would round it, at half the issue slots.
+__device__ __forceinline__ uint64_t f2_pack(float x, float y) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& x, float& y) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // Splits two floats into packed hi and lo bf16x2 words.
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
     hi = pack_bf16(a, b);
     lo = pack_bf16(a - bf16_lo_f(hi), b - bf16_hi_f(hi));
+}
+
+// The same split with the two residuals x - hi in one packed subtraction
+// (identical results).  The packed operands want register pairs, so it pays
+// where registers are free (the forward kernel) and spills where a kernel
+// sits at its register limit (the backward kernel keeps split2).
+__device__ __forceinline__ void split2_x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    hi = pack_bf16(a, b);
+    float ra, rb;
+    f2_unpack(f2_sub(f2_pack(a, b), f2_pack(bf16_lo_f(hi), bf16_hi_f(hi))), ra, rb);
+    lo = pack_bf16(ra, rb);
 }
 
 // Byte offset of (row, 16-byte chunk) inside a 128B-swizzled tile of 128-byte rows.

@@ -135,8 +135,8 @@ struct RawTile {
             const int f = t + it * NTH;
             const int r = f >> 4, c4 = f & 15;
             uint2 h, l;
-            sm100::split2(a[it].x * mul, a[it].y * mul, h.x, l.x);
-            sm100::split2(a[it].z * mul, a[it].w * mul, h.y, l.y);
+            sm100::split2_x2(a[it].x * mul, a[it].y * mul, h.x, l.x);
+            sm100::split2_x2(a[it].z * mul, a[it].w * mul, h.y, l.y);
             const uint32_t off = sm100::sw128(r, c4 >> 1) + (c4 & 1) * 8;
             *reinterpret_cast<uint2*>(tile + off) = h;
             *reinterpret_cast<uint2*>(tile + R * 128 + off) = l;
