@@ -356,9 +356,12 @@ def run_ours(args):
     if tensor_path:
         kernels = ("attn_bwd_rowdot", "attn_bwd_tc64")
         bf16_peak = peaks.get("bf16_tflops")
-        pipe = {"name": "tcgen05 kind::f16 (bf16x3: 3 MMAs per product)",
-                "achieved_tflops": bwd_tflops, "executed_tflops": 3 * bwd_tflops,
-                "peak_tflops": bf16_peak, "frac": (3 * bwd_tflops / bf16_peak) if bf16_peak else None,
+        # Executed on the tensor pipe per query tile: S^T recomputed, dP^T, dV and
+        # dK at 3 MMAs each (bf16 hi/lo split), dQ as two stacked M=128 MMAs
+        # (the work of 4): 16 products' worth against the 4 algorithmic ones.
+        pipe = {"name": "tcgen05 kind::f16 (bf16 hi/lo split; S^T recomputed)",
+                "achieved_tflops": bwd_tflops, "executed_tflops": 4 * bwd_tflops,
+                "peak_tflops": bf16_peak, "frac": (4 * bwd_tflops / bf16_peak) if bf16_peak else None,
                 "peak_source": f"{peak_src} dense bf16 (burst)",
                 "algorithmic_flops_per_launch": work["bwd_flops"]}
     else:
@@ -1067,9 +1070,10 @@ def run_sweep(args):
         sm_mhz = ck["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
         tensor = d == 64
         # Roofline time: HBM bytes at the measured copy rate, or the pipe's
-        # executed flops (3 MMAs per product on the tensor path) at its peak.
+        # executed flops at its peak (tensor path: 3 MMAs per forward product;
+        # 4x the backward's algorithmic flops, S^T recomputed and dQ stacked).
         pipe_tflops = bf16 if tensor else props.multi_processor_count * 256 * sm_mhz * 1e-6
-        executed = (3 if tensor else 1) * flops
+        executed = (3 * w["fwd_flops"] + 4 * w["bwd_flops"]) if tensor else flops
         t_roof = max(byts / (hbm * 1e9), executed / (pipe_tflops * 1e12))
         line = {"metric": SWEEP_METRIC, "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
                 "steps": reps, "ms_per_step": ms, "higher_is_better": True, "dtype": "f32",
