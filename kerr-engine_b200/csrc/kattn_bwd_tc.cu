@@ -369,7 +369,8 @@ __device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm
 }
 
 // DET: the deterministic dQ mode (slices in p.dq_part instead of reductions into dq).
-template <bool DET>
+// V8: q, k, v, dout rows start on 32-byte boundaries (256-bit row loads).
+template <bool DET, bool V8>
 __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     // Launched behind attn_bwd_rowdot, whose outputs (D, the zeroed dq) only
     // the loader warps touch: they wait for it; the elementwise warps stage
@@ -430,8 +431,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
             const Item it = make_item(p, cl.w);
             const long base = static_cast<long>(it.b) * p.T;
             const int q0 = (cl.it0 + cl.n) * BQ;
-            x.load(p.q + base * p.ld_qkv + it.h * D, p.ld_qkv, p.dout + base * p.ld_o + it.h * D, p.ld_o, q0, p.T,
-                   t);
+            x.template load<V8>(p.q + base * p.ld_qkv + it.h * D, p.ld_qkv, p.dout + base * p.ld_o + it.h * D,
+                                p.ld_o, q0, p.T, t);
             if (t < BQ) {
                 const long bh = (static_cast<long>(it.b) * p.H + it.h) * p.T;
                 const bool ok = q0 + t < p.T;
@@ -546,7 +547,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         Item it = make_item(p, w);
         {
             const long base = static_cast<long>(it.b) * p.T;
-            tc::stage_rows2<BK, NELEM>(sm.kh, sm.kl, p.k + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.vh, sm.vl,
+            tc::stage_rows2<BK, NELEM, V8>(sm.kh, sm.kl, p.k + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.vh, sm.vl,
                                        p.v + base * p.ld_qkv + it.h * D, p.ld_qkv, it.k0, p.T, tid);
         }
         fence_async_smem();
@@ -646,8 +647,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 nx = make_item(p, wn);
                 const long base = static_cast<long>(nx.b) * p.T;
                 tc::Rows2<BK, NELEM> kv;
-                kv.load(p.k + base * p.ld_qkv + nx.h * D, p.ld_qkv, p.v + base * p.ld_qkv + nx.h * D, p.ld_qkv,
-                        nx.k0, p.T, tid);
+                kv.template load<V8>(p.k + base * p.ld_qkv + nx.h * D, p.ld_qkv, p.v + base * p.ld_qkv + nx.h * D,
+                                     p.ld_qkv, nx.k0, p.T, tid);
                 if (!mbar_wait_warp(&sm.kv_free, r & 1, p.wait_ns)) {
                     failed = true;
                     break;
@@ -715,9 +716,14 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    // 256-bit row loads when every row of q, k, v and dout starts on a
+    // 32-byte boundary (the per-head column offsets, 256 bytes, keep it).
+    auto a32 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 31) == 0; };
+    const bool v8 = a32(a.q) && a32(a.k) && a32(a.v) && a32(a.dout) && a.ld_qkv % 8 == 0 && a.ld_o % 8 == 0;
     static std::atomic<uint64_t> attr_done{0};  // one bit per device and variant: the attribute is per device
-    const uint64_t bit = 1ull << ((2 * dev + (p.dq_part ? 1 : 0)) & 63);
-    auto kernel = p.dq_part ? attn_bwd_tc64<true> : attn_bwd_tc64<false>;
+    const uint64_t bit = 1ull << ((4 * dev + (p.dq_part ? 2 : 0) + (v8 ? 1 : 0)) & 63);
+    auto kernel = p.dq_part ? (v8 ? attn_bwd_tc64<true, true> : attn_bwd_tc64<true, false>)
+                            : (v8 ? attn_bwd_tc64<false, true> : attn_bwd_tc64<false, false>);
     if (!(attr_done.load(std::memory_order_relaxed) & bit)) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;

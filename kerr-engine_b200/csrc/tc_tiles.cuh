@@ -46,6 +46,14 @@ __device__ __forceinline__ void stage_rows(uint8_t* hi, uint8_t* lo, const float
     }
 }
 
+// 32 bytes of read-only global memory in one 256-bit load (sm_100); p must
+// be 32-byte aligned.
+__device__ __forceinline__ void ldg_v8(const float* p, float4& a, float4& b) {
+    asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(a.x), "=f"(a.y), "=f"(a.z), "=f"(a.w), "=f"(b.x), "=f"(b.y), "=f"(b.z), "=f"(b.w)
+                 : "l"(p));
+}
+
 // Two tiles of the same shape (e.g. Q and dO, or K and V) held in registers
 // between their loads and their conversion, so the loads can be issued early
 // and the shared-memory stores made once the destination is free.
@@ -55,6 +63,9 @@ struct Rows2 {
     static constexpr int ITEMS = R * 8 / NTH;
     float4 a[2][ITEMS], b[2][ITEMS];
 
+    // V8: every row start is 32-byte aligned (base pointers and row strides),
+    // so each 8-float chunk is one 256-bit load instead of two 128-bit ones.
+    template <bool V8 = false>
     __device__ __forceinline__ void load(const float* g0, long ld0, const float* g1, long ld1, int row0, int T,
                                          int t) {
 #pragma unroll
@@ -67,12 +78,19 @@ struct Rows2 {
             a[1][it] = a[0][it];
             b[1][it] = a[0][it];
             if (row0 + r < T) {
-                const float4* s0 = reinterpret_cast<const float4*>(g0 + static_cast<long>(row0 + r) * ld0 + ch * 8);
-                const float4* s1 = reinterpret_cast<const float4*>(g1 + static_cast<long>(row0 + r) * ld1 + ch * 8);
-                a[0][it] = __ldg(s0);
-                b[0][it] = __ldg(s0 + 1);
-                a[1][it] = __ldg(s1);
-                b[1][it] = __ldg(s1 + 1);
+                const float* f0 = g0 + static_cast<long>(row0 + r) * ld0 + ch * 8;
+                const float* f1 = g1 + static_cast<long>(row0 + r) * ld1 + ch * 8;
+                if constexpr (V8) {
+                    ldg_v8(f0, a[0][it], b[0][it]);
+                    ldg_v8(f1, a[1][it], b[1][it]);
+                } else {
+                    const float4* s0 = reinterpret_cast<const float4*>(f0);
+                    const float4* s1 = reinterpret_cast<const float4*>(f1);
+                    a[0][it] = __ldg(s0);
+                    b[0][it] = __ldg(s0 + 1);
+                    a[1][it] = __ldg(s1);
+                    b[1][it] = __ldg(s1 + 1);
+                }
             }
         }
     }
@@ -102,11 +120,11 @@ struct Rows2 {
 
 // Two tiles of the same shape in one pass: all loads of both are in flight
 // before the first conversion.
-template <int R, int NTH>
+template <int R, int NTH, bool V8 = false>
 __device__ __forceinline__ void stage_rows2(uint8_t* hi0, uint8_t* lo0, const float* g0, long ld0, uint8_t* hi1,
                                             uint8_t* lo1, const float* g1, long ld1, int row0, int T, int t) {
     Rows2<R, NTH> x;
-    x.load(g0, ld0, g1, ld1, row0, T, t);
+    x.template load<V8>(g0, ld0, g1, ld1, row0, T, t);
     x.store(hi0, lo0, hi1, lo1, t);
 }
 

@@ -8,7 +8,9 @@ slice of a workspace, and one more kernel adds the slices in key-tile order
 Checked here, on both kernel families and with and without the causal mask:
 repeated calls give bitwise-identical dq (and dk, dv); dq matches the oracle
 (causal) at the parity tolerance and the reduction path closely; the
-allocation-free entry point refuses the mode.
+allocation-free entry point refuses the mode.  The mode's bitwise
+reproducibility also checks that the tensor-core backward's two row-load
+paths (rows on 32-byte boundaries or not) agree.
 """
 import numpy as np
 import pytest
@@ -95,3 +97,46 @@ def test_noalloc_refuses_deterministic_mode():
 
 def test_set_deterministic_argument_checks():
     assert kerr_attn.lib().kattn_set_deterministic(None, 1) == kerr_attn.KATTN_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_row_alignment_paths_agree(causal):
+    """The tensor-core backward loads rows with 256-bit loads when q, k, v
+    and dout rows all start on 32-byte boundaries, and with 128-bit loads
+    otherwise.  The same inputs placed 16 bytes off a 32-byte boundary (one
+    spare float before each buffer's first row) take the second path; in the
+    deterministic mode both give bitwise-identical results."""
+    B, T, H, d = 2, 200, 2, 64
+    qkv, dout = make_inputs(B, T, H, d, seed=17)
+    C = H * d
+    dev = torch.device("cuda", 0)
+
+    def place(a, shift):
+        """a (contiguous [B, T, W]) as a view `shift` floats into a larger buffer."""
+        flat = torch.empty(a.size + 8, device=dev)
+        v = flat[shift:shift + a.size].view(a.shape)
+        v.copy_(torch.from_numpy(a))
+        return v
+
+    def run_at(ctx, shift):
+        x = place(qkv, shift)
+        g = place(dout, shift)
+        assert (x.data_ptr() % 32 == 0) == (shift == 0)
+        q, k, v = kerr_attn.split_qkv(x, C)
+        o = torch.empty(B, T, C, device=dev)
+        lse = torch.empty(B, H, T, device=dev)
+        kerr_attn.fwd(ctx, q, k, v, o, lse, H, causal=causal)
+        dqkv = torch.full((B, T, 3 * C), float("nan"), device=dev)
+        dq, dk, dv = kerr_attn.split_qkv(dqkv, C)
+        kerr_attn.bwd(ctx, q, k, v, o, g, lse, dq, dk, dv, H, causal=causal)
+        torch.cuda.synchronize()
+        ctx.check_device()
+        return dqkv.cpu()
+
+    with kerr_attn.Context(0) as ctx:
+        ctx.set_path(kerr_attn.PATH_TENSOR)
+        ctx.set_deterministic(True)
+        a = run_at(ctx, 0)
+        b = run_at(ctx, 4)
+    assert torch.isfinite(a).all()
+    assert torch.equal(a, b)
