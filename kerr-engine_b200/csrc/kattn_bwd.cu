@@ -18,6 +18,7 @@
 
 #include "kattn_common.cuh"
 #include "kattn_launch.h"
+#include "sm100.cuh"
 
 namespace kattn {
 
@@ -49,14 +50,15 @@ struct BwdParams {
 };
 
 // D[b,h,t] = dout[b,t,h,:] . o[b,t,h,:];  dq[b,t,h,:] = 0.
-// D/4 lanes per (b, t, h) row, one float4 each; a warp takes RPW*U
-// consecutive rows (consecutive heads of a token are contiguous in memory)
-// and issues all U rounds of loads before it reduces any.  U = 1 (one row
-// per lane group, more warps) measured faster than U = 4 at the 768-dim
-// shape.
+// D/W lanes per (b, t, h) row, W floats each (W = 8: one 256-bit load of
+// dout and of o per lane, when their rows and dq's start on 32-byte
+// boundaries; W = 4: 128-bit loads); a warp takes RPW*U consecutive rows
+// (consecutive heads of a token are contiguous in memory) and issues all U
+// rounds of loads before it reduces any.  U = 1 (one row per lane group,
+// more warps) measured faster than U = 4 at the 768-dim shape.
 constexpr int ROWDOT_U = 1;
 
-template <int D>
+template <int D, bool V8>
 __global__ void __launch_bounds__(256) attn_bwd_rowdot(const BwdParams p) {
     // Wait for the grid before (the one that wrote o, dout or q, k, v), then
     // let the backward kernel behind this one launch.  That order matters:
@@ -68,17 +70,19 @@ __global__ void __launch_bounds__(256) attn_bwd_rowdot(const BwdParams p) {
     // the grid waited for here.
     pdl_wait();
     pdl_launch();
-    constexpr int LPR = D / 4;
+    constexpr int W = V8 ? 8 : 4;
+    constexpr int LPR = D / W;
     constexpr int RPW = 32 / LPR;
     constexpr int U = ROWDOT_U;
     const long nrows = static_cast<long>(p.B) * p.T * p.H;
     const int lane = threadIdx.x & 31;
     const int sub = lane / LPR;
-    const int c = (lane % LPR) * 4;
+    const int c = (lane % LPR) * W;
     const long warp = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long nwarps = (static_cast<long>(gridDim.x) * blockDim.x) >> 5;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
     for (long base = warp * RPW * U; base < nrows; base += nwarps * RPW * U) {
-        float4 g[U], o[U];
+        float4 g[U][2], o[U][2];
         long bt[U];
         int h[U];
 #pragma unroll
@@ -86,22 +90,42 @@ __global__ void __launch_bounds__(256) attn_bwd_rowdot(const BwdParams p) {
             const long row = base + u * RPW + sub;
             bt[u] = row / p.H;
             h[u] = static_cast<int>(row - bt[u] * p.H);
+            g[u][0] = g[u][1] = o[u][0] = o[u][1] = z;
             if (row < nrows) {
-                g[u] = *reinterpret_cast<const float4*>(p.dout + bt[u] * p.ld_o + h[u] * D + c);
-                o[u] = *reinterpret_cast<const float4*>(p.o + bt[u] * p.ld_o + h[u] * D + c);
-            } else {
-                g[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                o[u] = g[u];
+                const float* gp = p.dout + bt[u] * p.ld_o + h[u] * D + c;
+                const float* op = p.o + bt[u] * p.ld_o + h[u] * D + c;
+                if constexpr (V8) {
+                    sm100::ldg_v8(gp, g[u][0], g[u][1]);
+                    sm100::ldg_v8(op, o[u][0], o[u][1]);
+                } else {
+                    g[u][0] = *reinterpret_cast<const float4*>(gp);
+                    o[u][0] = *reinterpret_cast<const float4*>(op);
+                }
             }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const long row = base + u * RPW + sub;
-            float acc = g[u].x * o[u].x + g[u].y * o[u].y + g[u].z * o[u].z + g[u].w * o[u].w;
+            // Both paths add in one order, so D is bitwise the same: a sum of
+            // four products per 4-column group, then a butterfly over the
+            // groups.  A 256-bit lane holds groups 2l and 2l+1, which pair
+            // up in the butterfly's last step.
+            float acc = g[u][0].x * o[u][0].x + g[u][0].y * o[u][0].y + g[u][0].z * o[u][0].z + g[u][0].w * o[u][0].w;
+            float acc1 = 0.f;
+            if constexpr (V8)
+                acc1 = g[u][1].x * o[u][1].x + g[u][1].y * o[u][1].y + g[u][1].z * o[u][1].z + g[u][1].w * o[u][1].w;
 #pragma unroll
-            for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            for (int off = LPR / 2; off > 0; off >>= 1) {
+                acc += __shfl_xor_sync(0xffffffffu, acc, off);
+                if constexpr (V8) acc1 += __shfl_xor_sync(0xffffffffu, acc1, off);
+            }
+            if constexpr (V8) acc += acc1;
             if (row < nrows) {
-                *reinterpret_cast<float4*>(p.dq + bt[u] * p.ld_d + h[u] * D + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                float* dqp = p.dq + bt[u] * p.ld_d + h[u] * D + c;
+                if constexpr (V8)
+                    sm100::stg_v8(dqp, z, z);
+                else
+                    *reinterpret_cast<float4*>(dqp) = z;
                 if ((lane % LPR) == 0) {
                     const long b = bt[u] / p.T;
                     const long t = bt[u] - b * p.T;
@@ -378,12 +402,17 @@ template <int D>
 static cudaError_t launch_prep_d(const BwdParams& p, int num_sms, cudaStream_t stream, int* launches) {
     // One wave when it fits (8 blocks of 256 threads per SM), every load
     // issued at once; larger problems take grid-stride rounds.
+    // 256-bit accesses when every row of o, dout and dq starts on a 32-byte
+    // boundary (the per-head offsets, D * 4 bytes, keep it).
+    auto a32 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 31) == 0; };
+    const bool v8 = a32(p.o) && a32(p.dout) && a32(p.dq) && p.ld_o % 8 == 0 && p.ld_d % 8 == 0;
     const long nrows = static_cast<long>(p.B) * p.T * p.H;
-    const long rows_per_block = (256 / 32) * (32 / (D / 4)) * ROWDOT_U;
+    const long rows_per_block = (256 / 32) * (32 / (D / (v8 ? 8 : 4))) * ROWDOT_U;
     long blocks = (nrows + rows_per_block - 1) / rows_per_block;
     const long cap = 8L * (num_sms > 0 ? num_sms : 148);
     if (blocks > cap) blocks = cap;
-    cudaError_t e = launch_pdl(attn_bwd_rowdot<D>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
+    cudaError_t e = launch_pdl(v8 ? attn_bwd_rowdot<D, true> : attn_bwd_rowdot<D, false>,
+                               dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

@@ -330,6 +330,21 @@ __device__ __forceinline__ uint32_t pack_bf16(float even, float odd) {
 __device__ __forceinline__ float bf16_lo_f(uint32_t packed) { return __uint_as_float(packed << 16); }
 __device__ __forceinline__ float bf16_hi_f(uint32_t packed) { return __uint_as_float(packed & 0xFFFF0000u); }
 
+// ---------------------------------------------------------------- 256-bit global access
+// 32 bytes of read-only global memory in one 256-bit load (sm_100); p must
+// be 32-byte aligned.
+__device__ __forceinline__ void ldg_v8(const float* p, float4& a, float4& b) {
+    asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(a.x), "=f"(a.y), "=f"(a.z), "=f"(a.w), "=f"(b.x), "=f"(b.y), "=f"(b.z), "=f"(b.w)
+                 : "l"(p));
+}
+// 32 bytes to global memory in one 256-bit store; p must be 32-byte aligned.
+__device__ __forceinline__ void stg_v8(float* p, float4 a, float4 b) {
+    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(a.x), "f"(a.y), "f"(a.z),
+                 "f"(a.w), "f"(b.x), "f"(b.y), "f"(b.z), "f"(b.w)
+                 : "memory");
+}
+
 // ---------------------------------------------------------------- f32x2
 // Two f32 lanes in one 64-bit register pair for the packed sm_100
 // instructions (add / sub / mul / fma .rn.f32x2): each lane is rounded

@@ -46,14 +46,6 @@ __device__ __forceinline__ void stage_rows(uint8_t* hi, uint8_t* lo, const float
     }
 }
 
-// 32 bytes of read-only global memory in one 256-bit load (sm_100); p must
-// be 32-byte aligned.
-__device__ __forceinline__ void ldg_v8(const float* p, float4& a, float4& b) {
-    asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=f"(a.x), "=f"(a.y), "=f"(a.z), "=f"(a.w), "=f"(b.x), "=f"(b.y), "=f"(b.z), "=f"(b.w)
-                 : "l"(p));
-}
-
 // Two tiles of the same shape (e.g. Q and dO, or K and V) held in registers
 // between their loads and their conversion, so the loads can be issued early
 // and the shared-memory stores made once the destination is free.
@@ -81,8 +73,8 @@ struct Rows2 {
                 const float* f0 = g0 + static_cast<long>(row0 + r) * ld0 + ch * 8;
                 const float* f1 = g1 + static_cast<long>(row0 + r) * ld1 + ch * 8;
                 if constexpr (V8) {
-                    ldg_v8(f0, a[0][it], b[0][it]);
-                    ldg_v8(f1, a[1][it], b[1][it]);
+                    sm100::ldg_v8(f0, a[0][it], b[0][it]);
+                    sm100::ldg_v8(f1, a[1][it], b[1][it]);
                 } else {
                     const float4* s0 = reinterpret_cast<const float4*>(f0);
                     const float4* s1 = reinterpret_cast<const float4*>(f1);
