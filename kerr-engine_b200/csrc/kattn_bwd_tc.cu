@@ -72,7 +72,7 @@ constexpr int STAGES = 3;  // query-tile ring depth (Q, dO, lse, D)
 static_assert(BK == kBwdTcKeyRows, "dQ slices of the deterministic mode");
 
 // TMEM columns (512 allocated).  Buffer b: S^T (then P packed) at col_s(b),
-// dP^T (then dS packed) at col_dp(b), dQ tile (M=64 layout) at col_dq(b).
+// dP^T (then dS packed) at col_dp(b), dQ tile (the stacked M=128 accumulator) at col_dq(b).
 __device__ __forceinline__ uint32_t col_s(int b) { return b ? 128u : 0u; }
 __device__ __forceinline__ uint32_t col_dp(int b) { return b ? 192u : 64u; }
 __device__ __forceinline__ uint32_t col_dq(int b) { return b ? 320u : 256u; }
