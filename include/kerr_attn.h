@@ -67,11 +67,13 @@ enum {
 };
 
 /* Kernel families (kattn_set_path).  AUTO uses the tensor-core kernels where
- * they exist (head_dim 64) and the FFMA kernels elsewhere. */
+ * they exist (forward at head_dim 32 and 64, backward at 64) and the FFMA
+ * kernels elsewhere. */
 enum {
     KATTN_PATH_AUTO = 0,
     KATTN_PATH_FFMA = 1,   /* f32 CUDA-core kernels, every supported head_dim */
-    KATTN_PATH_TENSOR = 2  /* tcgen05 bf16x3 kernels; head_dim 64 only */
+    KATTN_PATH_TENSOR = 2  /* tcgen05 bf16x3 kernels: head_dim 64, and 32 (whose
+                              backward runs on the FFMA kernels); others refused */
 };
 
 /* Library version, major*10000 + minor*100 + patch. */

@@ -182,8 +182,8 @@ cudaError_t dispatch_bwd(kattn_ctx* ctx, const kattn::BwdArgs& a, cudaStream_t s
 }
 
 int path_check(const kattn_ctx* ctx, int d) {
-    if (ctx->path.load(std::memory_order_relaxed) == KATTN_PATH_TENSOR && d != 64)
-        return fail(KATTN_ERR_UNSUPPORTED, "the tensor-core path supports head_dim 64 only (got %d)", d);
+    if (ctx->path.load(std::memory_order_relaxed) == KATTN_PATH_TENSOR && d != 64 && d != 32)
+        return fail(KATTN_ERR_UNSUPPORTED, "the tensor-core path supports head_dim 64 and 32 (got %d)", d);
     return KATTN_OK;
 }
 

@@ -43,6 +43,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "kattn_common.cuh"
 #include "kattn_launch.h"
@@ -62,33 +63,42 @@ constexpr int MMA_WARP = NSM / 32;
 constexpr int TMA_WARP = MMA_WARP + 1;
 constexpr int NTHREADS = NSM + 64;
 constexpr unsigned IDLE_NS = 64;  // back-off of an idle issuer loop
-constexpr int D = 64;
 
 // TMEM columns.  Buffer b: S at col_s(b) (64 f32 columns; P packed over it:
 // for key columns 32c..32c+31, bf16 hi in columns 32c..32c+15 and lo in
 // 32c+16..32c+31); the O accumulator of the current item at COL_O.
 __device__ __forceinline__ uint32_t col_s(int b) { return b ? 64u : 0u; }
 constexpr uint32_t COL_O = 128;
-// Q of the current item as the A operand of S = Q K^T: d pair (2i, 2i+1) of a
-// row packed in column i, hi at Q_HI, lo at Q_LO (32 columns each).
+// O takes D columns.  Q of the current item as the A operand of S = Q K^T:
+// d pair (2i, 2i+1) of a row packed in column i, hi at Q_HI, lo at Q_LO (D/2
+// columns each).
 constexpr uint32_t Q_HI = 192;
 constexpr uint32_t Q_LO = 224;
 // mu may trail the true row maximum by up to this much (log2 units).
 constexpr float RESCALE_LOG2 = 8.f;
 constexpr uint32_t TMEM_COLS = 256;
 
-// A K / V buffer holds a raw f32 tile (rows x 256 bytes) as TMA lands it,
-// then the converted bf16 hi half (rows x 128 bytes) followed by the lo half.
-// The Q buffer holds the raw tile only, as two 128B-swizzled boxes of 32
-// columns (each thread then reads its own row without bank conflicts).
-constexpr uint32_t Q_BYTES = BM * 256;
-constexpr uint32_t Q_BOX_BYTES = BM * 128;
-constexpr uint32_t KV_BYTES = BN * 256;
+// Head dimension D = 64 or 32.  A K / V buffer holds a raw f32 tile (rows x
+// 4D bytes) as TMA lands it, then the converted bf16 hi half (rows x 2D
+// bytes) followed by the lo half, 128B-swizzled at D = 64 and 64B-swizzled at
+// D = 32.  The Q buffer holds the raw tile only, as D/32 128B-swizzled boxes
+// of 32 columns (each thread then reads its own row without bank conflicts).
+template <int D>
+struct Cfg {
+    static_assert(D == 64 || D == 32, "head_dim 64 or 32");
+    static constexpr uint32_t Q_BYTES = BM * D * 4;
+    static constexpr uint32_t Q_BOX_BYTES = BM * 128;
+    static constexpr uint32_t KV_BYTES = BN * D * 4;
+    static constexpr uint32_t HALF = BN * D * 2;      // one converted bf16 half of a K / V tile
+    static constexpr uint32_t ROW = D * 2;            // bytes of a converted row
+    static constexpr uint32_t SBO = 8 * ROW;          // 8-row swizzle atom
+};
 
+template <int D>
 struct alignas(1024) Smem {
-    uint8_t q[Q_BYTES];
-    uint8_t k[2][KV_BYTES];
-    uint8_t v[2][KV_BYTES];
+    uint8_t q[Cfg<D>::Q_BYTES];
+    uint8_t k[2][Cfg<D>::KV_BYTES];
+    uint8_t v[2][Cfg<D>::KV_BYTES];
     uint64_t q_full;       // raw Q of the CTA's item r landed (phase r&1)
     uint64_t q_ready;      // Q of item r in TMEM; its shared-memory buffer is free (phase r&1)
     uint64_t k_full[2];    // raw K tile g landed in stage g&1 (phase (g>>1)&1)
@@ -104,7 +114,7 @@ struct alignas(1024) Smem {
 };
 
 struct alignas(64) Params {
-    CUtensorMap tq, tk, tv;  // {H*64 columns, T rows, B} f32; boxes {32, BM, 1} (128B swizzle) for q, {64, BN, 1} for k, v
+    CUtensorMap tq, tk, tv;  // {H*D columns, T rows, B} f32; boxes {32, BM, 1} (128B swizzle) for q, {D, BN, 1} for k, v
     float* o;
     long ld_o;
     float* lse;
@@ -165,27 +175,42 @@ struct Ahead {
     __device__ __forceinline__ int slab(const Params& p) const { return w % (p.B * p.H); }
 };
 
-// Shared-memory descriptors of the Q tile and of K / V stage 0 (stage 1 is
-// KV_BYTES further), rebuilt by the issuing thread at each issue (a few
-// integer operations) rather than held in registers by every thread.
+// Shared-memory descriptors of K / V stage 0 (stage 1 is KV_BYTES further),
+// rebuilt by the issuing thread at each issue (a few integer operations)
+// rather than held in registers by every thread.  K is the K-major B operand
+// of S; V the MN-major B operand of P V (one N atom, so the leading-byte
+// offset is unused).  D = 32 rows are 64 bytes, in the 64B-swizzled layout.
 struct Descs {
     uint64_t kh, kl, vh, vl;
 };
 
-__device__ __forceinline__ Descs make_descs(const Smem& sm) {
+template <int D>
+__device__ __forceinline__ uint64_t k_desc(uint32_t addr) {
+    if constexpr (D == 64) return smem_desc(addr, 16, Cfg<D>::SBO);
+    else return smem_desc_sw64(addr, Cfg<D>::SBO);
+}
+template <int D>
+__device__ __forceinline__ uint64_t v_desc(uint32_t addr) {
+    if constexpr (D == 64) return smem_desc(addr, BN * 128, Cfg<D>::SBO);
+    else return smem_desc_sw64(addr, Cfg<D>::SBO);
+}
+
+template <int D>
+__device__ __forceinline__ Descs make_descs(const Smem<D>& sm) {
     Descs d;
-    d.kh = smem_desc(smem_u32(sm.k[0]), 16, 1024);
-    d.kl = smem_desc(smem_u32(sm.k[0] + BN * 128), 16, 1024);
-    d.vh = smem_desc(smem_u32(sm.v[0]), BN * 128, 1024);  // MN-major (P V B operand)
-    d.vl = smem_desc(smem_u32(sm.v[0] + BN * 128), BN * 128, 1024);
+    d.kh = k_desc<D>(smem_u32(sm.k[0]));
+    d.kl = k_desc<D>(smem_u32(sm.k[0] + Cfg<D>::HALF));
+    d.vh = v_desc<D>(smem_u32(sm.v[0]));
+    d.vl = v_desc<D>(smem_u32(sm.v[0] + Cfg<D>::HALF));
     return d;
 }
 
 // S = Q K^T of the key tile in stage `stage` into TMEM buffer b (TS: Q from
 // TMEM, so only K is read from shared memory).
+template <int D>
 __device__ __forceinline__ void issue_s(const Descs& d, uint32_t tm, int stage, int b) {
     constexpr uint32_t idesc = idesc_bf16(BM, BN, 0, 0);
-    const uint32_t so = stage * KV_BYTES;
+    const uint32_t so = stage * Cfg<D>::KV_BYTES;
     const uint64_t kh = desc_add(d.kh, so), kl = desc_add(d.kl, so);
 #pragma unroll
     for (int s = 0; s < D / 16; ++s) {
@@ -198,13 +223,14 @@ __device__ __forceinline__ void issue_s(const Descs& d, uint32_t tm, int stage, 
 
 // O (+)= P V of the key tile in stage `stage`, P packed over S buffer b;
 // `first`: the item's first tile (O is overwritten).
+template <int D>
 __device__ __forceinline__ void issue_pv(const Descs& d, uint32_t tm, int stage, int b, bool first) {
     constexpr uint32_t idesc = idesc_bf16(BM, D, 0, 1);
-    const uint32_t so = stage * KV_BYTES;
+    const uint32_t so = stage * Cfg<D>::KV_BYTES;
     const uint64_t vh = desc_add(d.vh, so), vl = desc_add(d.vl, so);
 #pragma unroll
     for (int s = 0; s < BN / 16; ++s) {
-        const uint32_t o = s * 2048;
+        const uint32_t o = s * 16 * Cfg<D>::ROW;  // 16 keys
         const uint32_t ph = tm + col_s(b) + 32 * (s >> 1) + 8 * (s & 1);
         mma_ts(tm + COL_O, ph, desc_add(vh, o), idesc, (first && s == 0) ? 0u : 1u);
         mma_ts(tm + COL_O, ph, desc_add(vl, o), idesc, 1);
@@ -213,20 +239,26 @@ __device__ __forceinline__ void issue_pv(const Descs& d, uint32_t tm, int stage,
 }
 
 // TMA of one raw tile: `rows` rows of slab (b, h) from row `row0`.
+template <int D>
 __device__ __forceinline__ void load_tile(const CUtensorMap& map, void* dst, uint64_t* bar, uint32_t bytes, int h,
                                           int row0, int b) {
     mbar_arrive_expect_tx(bar, bytes);
     tma_load_3d(dst, &map, h * D, row0, b, bar);
 }
 
-__global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_constant__ Params p) {
+template <int D>
+__device__ __forceinline__ void fwd_body(const Params& p) {
     // The next grid may launch at once (it waits for this one before it
     // touches memory); this grid's setup below touches no global memory, so
     // it runs while the grid before still drains, and every thread waits
     // for that grid (griddepcontrol.wait) before its first global access.
     pdl_launch();
     extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    using C = Cfg<D>;
+    // A raw K / V tile, converted in place: 128B-swizzled rows at D = 64,
+    // 64B-swizzled at D = 32.
+    using Tile = std::conditional_t<D == 64, tc::RawTile<BN, NSM>, tc::RawTile32<BN, NSM>>;
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -285,7 +317,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 bool progressed = false;
                 if (np < ns && mbar_test_wait(&sm.pv_ready[np & 1], (np >> 1) & 1)) {
                     tc_fence_after();
-                    issue_pv(make_descs(sm), tm, np & 1, np & 1, pq.j == 0);
+                    issue_pv<D>(make_descs<D>(sm), tm, np & 1, np & 1, pq.j == 0);
                     mma_commit(&sm.bar_o[np & 1]);
                     ++np;
                     pq.next(p, cta, G);
@@ -294,7 +326,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 if (sq.valid() && np >= ns - 1 && mbar_test_wait(&sm.k_ready[ns & 1], (ns >> 1) & 1) &&
                     (sq.j != 0 || mbar_test_wait(&sm.q_ready, sq.r & 1))) {
                     tc_fence_after();
-                    issue_s(make_descs(sm), tm, ns & 1, ns & 1);
+                    issue_s<D>(make_descs<D>(sm), tm, ns & 1, ns & 1);
                     mma_commit(&sm.bar_s[ns & 1]);
                     ++ns;
                     sq.next(p, cta, G);
@@ -349,9 +381,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 if (qq.valid() && (qq.r == 0 || mbar_test_wait(&sm.q_ready, (qq.r - 1) & 1))) {
                     const int sl = qq.slab(p);
                     const int q0 = (p.n_qtiles - 1 - qq.w / (p.B * p.H)) * BM;
-                    mbar_arrive_expect_tx(&sm.q_full, Q_BYTES);
-                    tma_load_3d(sm.q, &p.tq, (sl % p.H) * D, q0, sl / p.H, &sm.q_full);
-                    tma_load_3d(sm.q + Q_BOX_BYTES, &p.tq, (sl % p.H) * D + 32, q0, sl / p.H, &sm.q_full);
+                    mbar_arrive_expect_tx(&sm.q_full, C::Q_BYTES);
+#pragma unroll
+                    for (int bx = 0; bx < D / 32; ++bx)
+                        tma_load_3d(sm.q + bx * C::Q_BOX_BYTES, &p.tq, (sl % p.H) * D + 32 * bx, q0, sl / p.H,
+                                    &sm.q_full);
                     ++qq.r;
                     qq.set(p, cta, G);
                     progressed = true;
@@ -359,7 +393,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 if (kq.valid() && (gk < 2 || mbar_test_wait(&sm.bar_s[gk & 1], ((gk - 2) >> 1) & 1))) {
                     const int sl = kq.slab(p);
                     if (gk != 0 || !p.withhold_first_key_load)
-                        load_tile(p.tk, sm.k[gk & 1], &sm.k_full[gk & 1], KV_BYTES, sl % p.H, kq.j * BN, sl / p.H);
+                        load_tile<D>(p.tk, sm.k[gk & 1], &sm.k_full[gk & 1], C::KV_BYTES, sl % p.H, kq.j * BN, sl / p.H);
                     ++gk;
                     kq.next(p, cta, G);
                     progressed = true;
@@ -370,7 +404,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                     stg_item[gv & 1] = -1;
                     if (vq.j + 1 == vq.n_kv) stg_item[gv & 1] = vq.r;
                     const int sl = vq.slab(p);
-                    load_tile(p.tv, sm.v[gv & 1], &sm.v_full[gv & 1], KV_BYTES, sl % p.H, vq.j * BN, sl / p.H);
+                    load_tile<D>(p.tv, sm.v[gv & 1], &sm.v_full[gv & 1], C::KV_BYTES, sl % p.H, vq.j * BN, sl / p.H);
                     ++gv;
                     vq.next(p, cta, G);
                     progressed = true;
@@ -415,21 +449,29 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
         const int rl = (warp & 3) * 32 + (tid & 31);  // row in the item's tile, TMEM lane
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
         bool bad = false;
-        // Columns 32*hf.. of row rl of item rq's Q (scaled by scale*log2(e)),
-        // from swizzled box hf into TMEM lane rl.  Every S of the item before
-        // has completed (the caller waited for the last one).
+        // Columns (D/2)*hf.. of row rl of item rq's Q (scaled by
+        // scale*log2(e)), from swizzled box hf (D = 64) or half hf of the one
+        // box (D = 32), into TMEM lane rl.  Every S of the item before has
+        // completed (the caller waited for the last one).
         auto load_q = [&](int rq) {
             bad |= !mbar_wait(&sm.q_full, rq & 1, p.wait_ns);
-            const uint8_t* box = sm.q + hf * Q_BOX_BYTES + rl * 128;
-            uint32_t qh[16], ql[16];
+            constexpr int NC = D / 8;  // float4 chunks of this thread's half row
+            const uint8_t* box = sm.q + (D == 64 ? hf * C::Q_BOX_BYTES : 0) + rl * 128;
+            const int c0 = D == 64 ? 0 : 4 * hf;
+            uint32_t qh[2 * NC], ql[2 * NC];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float4 x = *reinterpret_cast<const float4*>(box + ((c ^ (rl & 7)) << 4));
+            for (int c = 0; c < NC; ++c) {
+                const float4 x = *reinterpret_cast<const float4*>(box + (((c0 + c) ^ (rl & 7)) << 4));
                 split2_x2(x.x * p.scale_log2, x.y * p.scale_log2, qh[2 * c], ql[2 * c]);
                 split2_x2(x.z * p.scale_log2, x.w * p.scale_log2, qh[2 * c + 1], ql[2 * c + 1]);
             }
-            tmem_st16(lane_base + tm + Q_HI + 16 * hf, qh);
-            tmem_st16(lane_base + tm + Q_LO + 16 * hf, ql);
+            if constexpr (D == 64) {
+                tmem_st16(lane_base + tm + Q_HI + 16 * hf, qh);
+                tmem_st16(lane_base + tm + Q_LO + 16 * hf, ql);
+            } else {
+                tmem_st8(lane_base + tm + Q_HI + 8 * hf, qh);
+                tmem_st8(lane_base + tm + Q_LO + 8 * hf, ql);
+            }
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&sm.q_ready);
@@ -450,7 +492,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
             // Q into TMEM.  Later items' K_0 and Q are converted during the
             // previous item's last tile, so their first S runs meanwhile.
             if (g == 0) {
-                tc::RawTile<BN, NSM> kr;
+                Tile kr;
                 bad |= !mbar_wait(&sm.k_full[0], 0, p.wait_ns);
                 kr.read(sm.k[0], tid);
                 if (named_sync_or(1, NSM, bad)) {
@@ -472,7 +514,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                 // item's first), so S_{g+1} can run during this softmax.
                 if (j + 1 < n_kv || has_next) {
                     const int gn = g + 1;
-                    tc::RawTile<BN, NSM> kr;
+                    Tile kr;
                     bad |= !mbar_wait(&sm.k_full[gn & 1], (gn >> 1) & 1, p.wait_ns);
                     kr.read(sm.k[gn & 1], tid);
                     if (named_sync_or(1, NSM, bad)) {
@@ -559,19 +601,19 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
                     bad |= !mbar_wait(&sm.bar_o[gp & 1], (gp >> 1) & 1, p.wait_ns);
                     tc_fence_after();
 #pragma unroll
-                    for (int c = 0; c < 32; c += 16) {
+                    for (int c = 0; c < D / 2; c += 16) {
                         float ov[16];
                         uint32_t ow[16];
-                        tmem_ld16(lane_base + tm + COL_O + 32 * hf + c, ov);
+                        tmem_ld16(lane_base + tm + COL_O + (D / 2) * hf + c, ov);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 16; ++i) ow[i] = __float_as_uint(ov[i] * alpha);
-                        tmem_st16(lane_base + tm + COL_O + 32 * hf + c, ow);
+                        tmem_st16(lane_base + tm + COL_O + (D / 2) * hf + c, ow);
                     }
                 }
                 tmem_wait_st();
                 {
-                    tc::RawTile<BN, NSM> vr;
+                    Tile vr;
                     bad |= !mbar_wait(&sm.v_full[bf], (g >> 1) & 1, p.wait_ns);
                     vr.read(sm.v[bf], tid);
                     if (named_sync_or(1, NSM, bad)) {
@@ -602,36 +644,38 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
             const float lt = sm.red[0][0][rl] + sm.red[0][1][rl];
             const float inv = 1.f / lt;
             if (hf == 0 && row < p.T) p.lse[(static_cast<long>(it.b) * p.H + it.h) * p.T + row] = (mu + log2f(lt)) * kLn2;
-            float4* stg = reinterpret_cast<float4*>(sm.v[gl & 1]);  // 64 rows x 16 float4 = 16 KB
+            constexpr int NCH = D / 4;  // float4 chunks of an O row
+            float4* stg = reinterpret_cast<float4*>(sm.v[gl & 1]);  // 64 rows x NCH float4 (the stage)
             float* og = p.o + static_cast<long>(it.b) * p.T * p.ld_o + it.h * D;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 // TMEM loads are warp-collective: every warp loads, the warps
                 // of the rows in this half stage.
                 {
-                    float ov[32];
-                    tmem_ld32(lane_base + tm + COL_O + 32 * hf, ov);
+                    float ov[D / 2];
+                    if constexpr (D == 64) tmem_ld32(lane_base + tm + COL_O + 32 * hf, ov);
+                    else tmem_ld16(lane_base + tm + COL_O + 16 * hf, ov);
                     tmem_wait_ld();
                     if ((rl >> 6) == half) {
                         const int rr = rl & 63;
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int c4 = 8 * hf + i;
-                            stg[rr * 16 + (c4 ^ (rr & 15))] =
+                        for (int i = 0; i < D / 8; ++i) {
+                            const int c4 = (D / 8) * hf + i;
+                            stg[rr * NCH + (c4 ^ (rr & (NCH - 1)))] =
                                 make_float4(ov[4 * i] * inv, ov[4 * i + 1] * inv, ov[4 * i + 2] * inv, ov[4 * i + 3] * inv);
                         }
                     }
                 }
                 named_sync(1, NSM);
 #pragma unroll
-                for (int k = 0; k < 64 * 16 / NSM; ++k) {
+                for (int k = 0; k < 64 * NCH / NSM; ++k) {
                     const int i = tid + k * NSM;
-                    const int rr = i >> 4;
-                    const int c4 = i & 15;
+                    const int rr = i / NCH;
+                    const int c4 = i % NCH;
                     const int qrow = it.q0 + 64 * half + rr;
                     if (qrow < p.T)
                         *reinterpret_cast<float4*>(og + static_cast<long>(qrow) * p.ld_o + c4 * 4) =
-                            stg[rr * 16 + (c4 ^ (rr & 15))];
+                            stg[rr * NCH + (c4 ^ (rr & (NCH - 1)))];
                 }
                 named_sync(1, NSM);
             }
@@ -647,6 +691,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_consta
     __syncthreads();
     if (warp == 0) tmem_dealloc(tm, TMEM_COLS);
 }
+
+__global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc64(const __grid_constant__ Params p) { fwd_body<64>(p); }
+__global__ void __launch_bounds__(NTHREADS, 2) attn_fwd_tc32(const __grid_constant__ Params p) { fwd_body<32>(p); }
 
 }  // namespace
 
@@ -670,11 +717,11 @@ EncodeTiled encode_tiled() {
 
 }  // namespace
 
-bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int H, int box_cols, int box_rows,
+bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int H, int d, int box_cols, int box_rows,
                  CUtensorMapSwizzle swizzle) {
     const EncodeTiled fn = encode_tiled();
     if (fn == nullptr) return false;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(H) * D, static_cast<cuuint64_t>(T),
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(H) * d, static_cast<cuuint64_t>(T),
                                 static_cast<cuuint64_t>(B)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(ld) * 4 * T};
     const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
@@ -709,13 +756,15 @@ bool encode_2d_bf16(CUtensorMap* map, const uint16_t* base, long cols, long rows
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool fwd_tc_supported(const FwdArgs& a) { return a.d == 64; }
+bool fwd_tc_supported(const FwdArgs& a) { return a.d == 64 || a.d == 32; }
 
 cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches) {
+    if (!fwd_tc_supported(a)) return cudaErrorInvalidValue;
+    const int D = a.d;
     Params p;
-    if (!encode_rows(&p.tq, a.q, a.ld_qkv, a.B, a.T, a.H, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_rows(&p.tk, a.k, a.ld_qkv, a.B, a.T, a.H, D, BN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&p.tv, a.v, a.ld_qkv, a.B, a.T, a.H, D, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (!encode_rows(&p.tq, a.q, a.ld_qkv, a.B, a.T, a.H, D, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_rows(&p.tk, a.k, a.ld_qkv, a.B, a.T, a.H, D, D, BN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_rows(&p.tv, a.v, a.ld_qkv, a.B, a.T, a.H, D, D, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     p.o = a.o;
     p.ld_o = a.ld_o;
@@ -733,14 +782,15 @@ cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream
     const long n_work = static_cast<long>(p.n_qtiles) * a.B * a.H;
     if (n_work <= 0 || n_work > INT32_MAX) return cudaErrorInvalidValue;
     p.n_work = static_cast<int>(n_work);
-    const size_t smem = sizeof(Smem) + 1024;
+    const size_t smem = (D == 64 ? sizeof(Smem<64>) : sizeof(Smem<32>)) + 1024;
+    auto kernel = D == 64 ? attn_fwd_tc64 : attn_fwd_tc32;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static std::atomic<uint64_t> attr_done{0};  // one bit per device: the attribute is per device
-    const uint64_t bit = 1ull << (dev & 63);
+    static std::atomic<uint64_t> attr_done{0};  // one bit per device and head_dim: the attribute is per device
+    const uint64_t bit = 1ull << ((2 * dev + (D == 32 ? 1 : 0)) & 63);
     if (!(attr_done.load(std::memory_order_relaxed) & bit)) {
-        e = cudaFuncSetAttribute(attn_fwd_tc64, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         attr_done.fetch_or(bit);
     }
@@ -748,7 +798,7 @@ cudaError_t launch_fwd_tc(const FwdArgs& a, int num_sms, int* status, cudaStream
     // walking its items in the snake order.
     const long slots = 2L * (num_sms > 0 ? num_sms : 148);
     const int grid = static_cast<int>(n_work < slots ? n_work : slots);
-    e = launch_pdl(attn_fwd_tc64, dim3(static_cast<unsigned>(grid)), dim3(NTHREADS), smem, stream, p);
+    e = launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(NTHREADS), smem, stream, p);
     if (e == cudaSuccess) *launches += 1;
     return e;
 }

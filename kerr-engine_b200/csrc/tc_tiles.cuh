@@ -156,9 +156,10 @@ struct RawTile {
 
 // A raw f32 tile of R rows x 32 floats (128 bytes per row, as a TMA box
 // lands it) -> the same bytes rewritten as bf16 hi (first R*64 bytes) and lo
-// (next R*64 bytes) in the 64B-swizzled K-major UMMA layout.  Same read /
-// barrier / write protocol as RawTile; thread t handles float4 f = t,
-// t + NTH, ... (row f/8, columns 4(f%8)..+3).
+// (next R*64 bytes) in the 64B-swizzled UMMA layout (the forward at head_dim
+// 32: K-major K, MN-major V), scaled by `mul`.  Same read / barrier / write
+// protocol as RawTile; thread t handles float4 f = t, t + NTH, ... (row f/8,
+// columns 4(f%8)..+3).
 template <int R, int NTH>
 struct RawTile32 {
     static_assert((R * 8) % NTH == 0, "tile items must divide evenly");
@@ -170,14 +171,14 @@ struct RawTile32 {
         for (int it = 0; it < ITEMS; ++it) a[it] = reinterpret_cast<const float4*>(tile)[t + it * NTH];
     }
 
-    __device__ __forceinline__ void write(uint8_t* tile, int t) const {
+    __device__ __forceinline__ void write(uint8_t* tile, float mul, int t) const {
 #pragma unroll
         for (int it = 0; it < ITEMS; ++it) {
             const int f = t + it * NTH;
             const int r = f >> 3, c4 = f & 7;
             uint2 h, l;
-            sm100::split2(a[it].x, a[it].y, h.x, l.x);
-            sm100::split2(a[it].z, a[it].w, h.y, l.y);
+            sm100::split2_x2(a[it].x * mul, a[it].y * mul, h.x, l.x);
+            sm100::split2_x2(a[it].z * mul, a[it].w * mul, h.y, l.y);
             const uint32_t off = sm100::sw64(r, c4 >> 1) + (c4 & 1) * 8;
             *reinterpret_cast<uint2*>(tile + off) = h;
             *reinterpret_cast<uint2*>(tile + R * 64 + off) = l;

@@ -8,12 +8,12 @@
 
 namespace kattn {
 
-// The first H*64 columns of a [B*T][ld] f32 buffer as a 3-D tensor
-// {H*64 columns, T rows, B}, boxes of `box_cols` columns x `box_rows` rows of
+// The first H*d columns of a [B*T][ld] f32 buffer as a 3-D tensor
+// {H*d columns, T rows, B}, boxes of `box_cols` columns x `box_rows` rows of
 // one batch entry; rows past T are out of bounds and read as zeros.  `base`
 // is 16-byte aligned and ld a multiple of 4 (checked at the C ABI).  False
 // when the driver entry point is missing or the encoding is refused.
-bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int H, int box_cols, int box_rows,
+bool encode_rows(CUtensorMap* map, const float* base, long ld, int B, int T, int H, int d, int box_cols, int box_rows,
                  CUtensorMapSwizzle swizzle);
 
 // A row-major f32 matrix of `rows` rows x `cols` columns (row stride ld
