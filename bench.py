@@ -1069,38 +1069,29 @@ def run_sweep(args):
         gbs = byts / (ms / 1e3) / 1e9
         ck = clocks.summary()
         sm_mhz = ck["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
-        tensor = d == 64 and args.path != "ffma"  # both kernels on the tensor cores
-        fwd_tc = d == 32 and args.path != "ffma"  # tensor-core forward, FFMA backward
-        ffma_tflops = props.multi_processor_count * 256 * sm_mhz * 1e-6
+        # The kernel family the library picks: tensor cores at d=64, and at d=32
+        # from 16384 (batch, head, position) rows up (AUTO), or as asked.
+        tensor = args.path != "ffma" and (d == 64 or (d == 32 and (args.path == "tensor" or B * H * T >= 16384)))
         # Roofline time: HBM bytes at the measured copy rate, or the pipe's
         # executed flops at its peak (tensor path: 3 MMAs per forward product;
         # 4x the backward's algorithmic flops, S^T recomputed and dQ stacked).
-        # At d=32 the forward runs on the tensor cores and the backward on
-        # FFMA, one after the other: the two kernels' roofline times add.
-        pipe_tflops = bf16 if tensor else ffma_tflops
+        pipe_tflops = bf16 if tensor else props.multi_processor_count * 256 * sm_mhz * 1e-6
         executed = (3 * w["fwd_flops"] + 4 * w["bwd_flops"]) if tensor else flops
-        if fwd_tc:
-            t_roof = (max(w["fwd_bytes"] / (hbm * 1e9), 3 * w["fwd_flops"] / (bf16 * 1e12)) +
-                      max(w["bwd_bytes"] / (hbm * 1e9), w["bwd_flops"] / (ffma_tflops * 1e12)))
-        else:
-            t_roof = max(byts / (hbm * 1e9), executed / (pipe_tflops * 1e12))
+        t_roof = max(byts / (hbm * 1e9), executed / (pipe_tflops * 1e12))
         line = {"metric": SWEEP_METRIC, "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
                 "steps": reps, "ms_per_step": ms, "higher_is_better": True, "dtype": "f32",
                 "data": f"synthetic (seeded q,k,v ~ N(0,1) x {sig:.4f}, dout ~ N(0,1))",
                 "config": {"workload": name, "batch": B, "n_head": H, "seq_len": T, "head_dim": d, "causal": True,
                            "l2": f"{nbuf} distinct buffer sets rotated" if nbuf > 1 else "inputs exceed L2"},
-                "kernel_path": ("tcgen05 bf16x3" if tensor else
-                                "forward tcgen05 bf16x3, backward fp32 FFMA" if fwd_tc else "fp32 FFMA"),
+                "kernel_path": "tcgen05 bf16x3" if tensor else "fp32 FFMA",
                 "gpu_launches": launches,
                 "roofline": {"achieved_gbs": gbs, "hbm_peak_gbs": hbm, "hbm_frac": gbs / hbm,
                              "achieved_tflops": tf, "frac_of_roofline": (t_roof * 1e3) / ms,
                              "roofline_ms": t_roof * 1e3,
                              "pipe": ("tcgen05 kind::f16, 3 MMAs per product, measured dense bf16 "
                                       f"{bf16} TF/s ({peak_src})") if tensor else
-                                     (f"forward: tcgen05 kind::f16 at the measured dense bf16 {bf16} TF/s; "
-                                      f"backward: FP32 FFMA nominal at {sm_mhz:.0f} MHz") if fwd_tc else
                                      f"FP32 FFMA nominal at {sm_mhz:.0f} MHz",
-                             "pipe_frac": None if fwd_tc else executed / (ms / 1e3) / 1e12 / pipe_tflops},
+                             "pipe_frac": executed / (ms / 1e3) / 1e12 / pipe_tflops},
                 "clocks": ck}
         print(json.dumps(line), flush=True)
         del bufs

@@ -66,14 +66,13 @@ enum {
     KATTN_ERR_DEVICE_TIMEOUT = 7    /* a kernel gave up a bounded wait on the tensor core */
 };
 
-/* Kernel families (kattn_set_path).  AUTO uses the tensor-core kernels where
- * they exist (forward at head_dim 32 and 64, backward at 64) and the FFMA
- * kernels elsewhere. */
+/* Kernel families (kattn_set_path).  AUTO uses the tensor-core kernels at
+ * head_dim 64, and at head_dim 32 for problems of at least 16384 (batch,
+ * head, position) rows, where they are faster; the FFMA kernels elsewhere. */
 enum {
     KATTN_PATH_AUTO = 0,
     KATTN_PATH_FFMA = 1,   /* f32 CUDA-core kernels, every supported head_dim */
-    KATTN_PATH_TENSOR = 2  /* tcgen05 bf16x3 kernels: head_dim 64, and 32 (whose
-                              backward runs on the FFMA kernels); others refused */
+    KATTN_PATH_TENSOR = 2  /* tcgen05 bf16x3 kernels: head_dim 64 and 32; others refused */
 };
 
 /* Library version, major*10000 + minor*100 + patch. */

@@ -140,11 +140,20 @@ int bwd_checks(const kattn_ctx* ctx, const float* q, const float* k, const float
     return KATTN_OK;
 }
 
+// AUTO's kernel family: the tensor-core kernels at head_dim 64, and at head_dim
+// 32 from 16384 (batch, head, position) rows up.  Below that the FFMA kernels'
+// shorter set-up wins: at 4 x 4 heads x 64 positions a forward + backward took
+// 60 us on FFMA against 76 us on the tensor cores; at 64 x 4 x 256, 170 us
+// against 65 us.
+bool auto_tensor(int d, long rows) { return d == 64 || (d == 32 && rows >= 16384); }
+
 // Forward launch on the kernel family the context selects, with the
 // context's wait limit (and, once, its diagnostic hook) on the tensor path.
 cudaError_t dispatch_fwd(kattn_ctx* ctx, const kattn::FwdArgs& a, cudaStream_t s, int* launches) {
     const int path = ctx->path.load(std::memory_order_relaxed);
-    if (path != KATTN_PATH_FFMA && kattn::fwd_tc_supported(a)) {
+    const long rows = static_cast<long>(a.B) * a.H * a.T;
+    if (kattn::fwd_tc_supported(a) &&
+        (path == KATTN_PATH_TENSOR || (path == KATTN_PATH_AUTO && auto_tensor(a.d, rows)))) {
         kattn::FwdArgs b = a;
         b.wait_ns = ctx->wait_ns.load(std::memory_order_relaxed);
         b.withhold_first_key_load = ctx->withhold_next_load.exchange(0);
@@ -156,7 +165,9 @@ cudaError_t dispatch_fwd(kattn_ctx* ctx, const kattn::FwdArgs& a, cudaStream_t s
 // Backward launch on the kernel family the context selects.
 cudaError_t dispatch_bwd(kattn_ctx* ctx, const kattn::BwdArgs& a, cudaStream_t s, int* launches) {
     const int path = ctx->path.load(std::memory_order_relaxed);
-    const bool tensor = path != KATTN_PATH_FFMA && kattn::bwd_tc_supported(a);
+    const long rows = static_cast<long>(a.B) * a.H * a.T;
+    const bool tensor = kattn::bwd_tc_supported(a) &&
+                        (path == KATTN_PATH_TENSOR || (path == KATTN_PATH_AUTO && auto_tensor(a.d, rows)));
     kattn::BwdArgs b = a;
     b.wait_ns = ctx->wait_ns.load(std::memory_order_relaxed);
     // Deterministic dQ: every key tile stores its contribution into its own

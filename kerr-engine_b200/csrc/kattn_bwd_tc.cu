@@ -63,7 +63,6 @@ namespace {
 
 constexpr int BK = 128;  // key rows per CTA
 constexpr int BQ = 64;   // query rows per tile
-constexpr int D = 64;
 constexpr int NELEM = 256;  // elementwise threads (warps 0-7)
 constexpr int NLOAD = 128;  // loader threads (warps 8-11)
 constexpr int NTHREADS = NELEM + NLOAD + 32;
@@ -80,15 +79,25 @@ constexpr uint32_t COL_DV = 384;
 constexpr uint32_t COL_DK = 448;
 constexpr uint32_t TMEM_COLS = 512;
 
+// Head dimension D = 64 or 32: K, V, Q and dO rows are D bf16 (2D bytes),
+// 128B-swizzled at D = 64 and 64B-swizzled at D = 32.
+template <int D>
+struct BCfg {
+    static_assert(D == 64 || D == 32, "head_dim 64 or 32");
+    static constexpr uint32_t ROW = 2 * D;              // bytes of a bf16 row
+    static constexpr uint32_t STAGE_BYTES = BQ * ROW;   // one stage of one Q / dO tile
+};
+
+template <int D>
 struct alignas(1024) Smem {
-    uint8_t kh[BK * 128];  // [key][64 bf16], 128B swizzle
-    uint8_t kl[BK * 128];
-    uint8_t vh[BK * 128];
-    uint8_t vl[BK * 128];
-    uint8_t qh[STAGES][BQ * 128];  // [query][64 bf16]
-    uint8_t ql[STAGES][BQ * 128];
-    uint8_t gh[STAGES][BQ * 128];  // dO
-    uint8_t gl[STAGES][BQ * 128];
+    uint8_t kh[BK * 2 * D];  // [key][D bf16]
+    uint8_t kl[BK * 2 * D];
+    uint8_t vh[BK * 2 * D];
+    uint8_t vl[BK * 2 * D];
+    uint8_t qh[STAGES][BQ * 2 * D];  // [query][D bf16]
+    uint8_t ql[STAGES][BQ * 2 * D];
+    uint8_t gh[STAGES][BQ * 2 * D];  // dO
+    uint8_t gl[STAGES][BQ * 2 * D];
     uint8_t sh[2][BK * 128];  // stacked dS, rows 0-63, [key][64], per TMEM buffer
     uint8_t sl[2][BK * 128];  // stacked dS, rows 64-127
     float lse2[STAGES][BQ];  // lse * log2(e), +inf beyond T
@@ -105,7 +114,7 @@ struct alignas(1024) Smem {
     uint32_t tmem_slot;
 };
 
-static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory (plus alignment slack) exceeds 227 KB");
+static_assert(sizeof(Smem<64>) + 1024 <= 232448, "shared memory (plus alignment slack) exceeds 227 KB");
 
 struct Params {
     const float* q;
@@ -194,8 +203,7 @@ struct Descs {
     uint64_t s0, s1;              // stacked dS hi / lo of buffer 0 / 1, MN-major (dQ A, M=128)
 };
 
-constexpr uint32_t STAGE_BYTES = BQ * 128;  // one stage of one Q / dO tile
-constexpr uint32_t MN_LBO_Q = BQ * 128;     // leading-byte offset of a 64-row MN-major tile
+constexpr uint32_t MN_LBO_Q = BQ * 128;     // leading-byte offset of a 64-row MN-major tile (one N atom: unused)
 constexpr uint32_t MN_LBO_K = BK * 128;
 // The dQ product's A operand (M=128) is two 64-row MN-major atoms: sh[b]
 // (atom 0) and sl[b] (atom 1), this far apart.
@@ -205,26 +213,37 @@ __device__ __forceinline__ uint64_t as_mn(uint64_t kdesc, uint32_t lbo) {
     return (kdesc & ~(static_cast<uint64_t>(0x3FFFu) << 16)) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16);
 }
 
-__device__ __forceinline__ void make_descs(const Smem& sm, Descs& d) {
-    d.kh = smem_desc(smem_u32(sm.kh), 16, 1024);
-    d.kl = smem_desc(smem_u32(sm.kl), 16, 1024);
-    d.vh = smem_desc(smem_u32(sm.vh), 16, 1024);
-    d.vl = smem_desc(smem_u32(sm.vl), 16, 1024);
+// A K-major descriptor of rows of D bf16: 128B-swizzled at D = 64, 64B-swizzled
+// (8-row atoms of 512 bytes) at D = 32.  The MN-major uses of these tiles
+// have N = D, one swizzle atom, so their leading-byte offset is unused.
+template <int D>
+__device__ __forceinline__ uint64_t row_desc(uint32_t addr) {
+    if constexpr (D == 64) return smem_desc(addr, 16, 1024);
+    else return smem_desc_sw64(addr, 512);
+}
+
+template <int D>
+__device__ __forceinline__ void make_descs(const Smem<D>& sm, Descs& d) {
+    d.kh = row_desc<D>(smem_u32(sm.kh));
+    d.kl = row_desc<D>(smem_u32(sm.kl));
+    d.vh = row_desc<D>(smem_u32(sm.vh));
+    d.vl = row_desc<D>(smem_u32(sm.vl));
     d.kh_mn = as_mn(d.kh, MN_LBO_K);
     d.kl_mn = as_mn(d.kl, MN_LBO_K);
-    d.qh = smem_desc(smem_u32(sm.qh[0]), 16, 1024);
-    d.ql = smem_desc(smem_u32(sm.ql[0]), 16, 1024);
-    d.gh = smem_desc(smem_u32(sm.gh[0]), 16, 1024);
-    d.gl = smem_desc(smem_u32(sm.gl[0]), 16, 1024);
+    d.qh = row_desc<D>(smem_u32(sm.qh[0]));
+    d.ql = row_desc<D>(smem_u32(sm.ql[0]));
+    d.gh = row_desc<D>(smem_u32(sm.gh[0]));
+    d.gl = row_desc<D>(smem_u32(sm.gl[0]));
     d.s0 = smem_desc(smem_u32(sm.sh[0]), DQ_A_LBO, 1024);
     d.s1 = smem_desc(smem_u32(sm.sh[1]), DQ_A_LBO, 1024);
 }
 
 // S^T and dP^T of the query tile in ring stage s into TMEM buffer b.
+template <int D>
 __device__ __forceinline__ void issue_sdp(const Descs& d, uint32_t tm, int s, int b) {
     constexpr uint32_t idesc = idesc_bf16(BK, BQ, 0, 0);
     const uint32_t cs = tm + col_s(b), cp = tm + col_dp(b);
-    const uint32_t so = s * STAGE_BYTES;
+    const uint32_t so = s * BCfg<D>::STAGE_BYTES;
     const uint64_t qh = desc_add(d.qh, so), ql = desc_add(d.ql, so);
     const uint64_t gh = desc_add(d.gh, so), gl = desc_add(d.gl, so);
 #pragma unroll
@@ -244,28 +263,31 @@ __device__ __forceinline__ void issue_sdp(const Descs& d, uint32_t tm, int s, in
 // dS_hi K and dS_lo K in separate TMEM lanes, which the read-out adds.  Two
 // M=128 MMAs per 16 keys instead of three M=64 ones, at the same cost per
 // MMA; the extra lo*lo term only adds precision.
+template <int D>
 __device__ __forceinline__ void issue_dq(const Descs& d, uint32_t tm, int b) {
     constexpr uint32_t idesc_q = idesc_bf16(2 * BQ, D, 1, 1);
     const uint32_t cq = tm + col_dq(b);
     const uint64_t sa = b ? d.s1 : d.s0;
 #pragma unroll
     for (int ks = 0; ks < BK / 16; ++ks) {
-        const uint32_t o = ks * 2048;
-        mma_ss(cq, desc_add(sa, o), desc_add(d.kh_mn, o), idesc_q, ks > 0);
-        mma_ss(cq, desc_add(sa, o), desc_add(d.kl_mn, o), idesc_q, 1);
+        const uint32_t os = ks * 2048;                   // 16 keys of the stacked dS (128-byte rows)
+        const uint32_t ok = ks * 16 * BCfg<D>::ROW;      // 16 keys of K
+        mma_ss(cq, desc_add(sa, os), desc_add(d.kh_mn, ok), idesc_q, ks > 0);
+        mma_ss(cq, desc_add(sa, os), desc_add(d.kl_mn, ok), idesc_q, 1);
     }
 }
 
 // dV += P^T dO, dK += dS^T Q (P, dS from TMEM buffer b; dO, Q of ring stage s).
+template <int D>
 __device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, int b, bool first) {
     constexpr uint32_t idesc_kv = idesc_bf16(BK, D, 0, 1);
-    const uint32_t so = s * STAGE_BYTES;
+    const uint32_t so = s * BCfg<D>::STAGE_BYTES;
     const uint64_t qh = as_mn(desc_add(d.qh, so), MN_LBO_Q), ql = as_mn(desc_add(d.ql, so), MN_LBO_Q);
     const uint64_t gh = as_mn(desc_add(d.gh, so), MN_LBO_Q), gl = as_mn(desc_add(d.gl, so), MN_LBO_Q);
 #pragma unroll
     for (int ks = 0; ks < BQ / 16; ++ks) {
         const uint32_t acc = (first && ks == 0) ? 0u : 1u;
-        const uint32_t o = ks * 2048;
+        const uint32_t o = ks * 16 * BCfg<D>::ROW;  // 16 queries
         const uint32_t ph = tm + col_s(b) + 16 * ks, gph = tm + col_dp(b) + 16 * ks;  // hi; lo is 8 further
         mma_ts(tm + COL_DV, ph, desc_add(gh, o), idesc_kv, acc);
         mma_ts(tm + COL_DV, ph, desc_add(gl, o), idesc_kv, 1);
@@ -286,7 +308,7 @@ __device__ __forceinline__ void issue_dkv(const Descs& d, uint32_t tm, int s, in
 // would wait for this thread's outstanding global operations (the first
 // half's reductions, the next tile's prefetch loads), and the next gradient
 // products wait for this buffer.
-template <bool DET>
+template <bool DET, int D>
 __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b, int qd, int lane, int q0,
                                             float* dqg, long ldq, uint64_t* dq_free) {
     const uint32_t ta = (static_cast<uint32_t>(qd * 32) << 16) + tm + col_dq(b);
@@ -295,11 +317,11 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
     float* dst = dqg + static_cast<long>(r) * ldq + (up ? 16 : 0);
     const bool on = r < p.T;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < D / 32; ++h) {
         float v[32];
         tmem_ld32(ta + 32 * h, v);
         tmem_wait_ld();
-        if (h == 1) {
+        if (h == D / 32 - 1) {
             tc_fence_before();
             mbar_arrive_relaxed(dq_free);
         }
@@ -331,35 +353,48 @@ __device__ __forceinline__ void dq_epilogue(const Params& p, uint32_t tm, int b,
 // completed and the next item's tiles are written by these same warps after
 // the second barrier.  The barriers are mbarriers with bounded waits, so a
 // warp that gave up earlier cannot leave the others blocked.
-__device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm, const Item& it, uint32_t lb,
+template <int D>
+__device__ __forceinline__ bool store_dkv(const Params& p, Smem<D>& sm, uint32_t tm, const Item& it, uint32_t lb,
                                           int row, int hf, int tid, int r) {
-    float4* stg_v = reinterpret_cast<float4*>(sm.sh[0]);  // 128 rows x 256 B = 32 KB (sh[0], sh[1])
+    constexpr int NCH = D / 4;  // float4 chunks of a row
+    float4* stg_v = reinterpret_cast<float4*>(sm.sh[0]);  // BK rows x D floats (16 or 32 KB)
     float4* stg_k = reinterpret_cast<float4*>(sm.sl[0]);
     float a[32];
-    tmem_ld32(lb + tm + COL_DV + 32 * hf, a);
-    tmem_wait_ld();
+    if constexpr (D == 64) {
+        tmem_ld32(lb + tm + COL_DV + 32 * hf, a);
+        tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-        stg_v[row * 16 + ((8 * hf + i) ^ (row & 15))] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
-    tmem_ld32(lb + tm + COL_DK + 32 * hf, a);
-    tmem_wait_ld();
+        for (int i = 0; i < 8; ++i)
+            stg_v[row * 16 + ((8 * hf + i) ^ (row & 15))] = make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
+        tmem_ld32(lb + tm + COL_DK + 32 * hf, a);
+        tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-        stg_k[row * 16 + ((8 * hf + i) ^ (row & 15))] =
-            make_float4(a[4 * i] * p.scale, a[4 * i + 1] * p.scale, a[4 * i + 2] * p.scale, a[4 * i + 3] * p.scale);
+        for (int i = 0; i < 8; ++i)
+            stg_k[row * 16 + ((8 * hf + i) ^ (row & 15))] =
+                make_float4(a[4 * i] * p.scale, a[4 * i + 1] * p.scale, a[4 * i + 2] * p.scale, a[4 * i + 3] * p.scale);
+    } else {
+        // 32 columns per accumulator: the warps with hf = 0 take dV, hf = 1 dK.
+        const float sc = hf ? p.scale : 1.f;
+        float4* stg = hf ? stg_k : stg_v;
+        tmem_ld32(lb + tm + (hf ? COL_DK : COL_DV), a);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            stg[row * 8 + (i ^ (row & 7))] = make_float4(a[4 * i] * sc, a[4 * i + 1] * sc, a[4 * i + 2] * sc, a[4 * i + 3] * sc);
+    }
     mbar_arrive(&sm.stg_full);
     if (!mbar_wait_warp(&sm.stg_full, r & 1, p.wait_ns)) return false;
     const long row0 = static_cast<long>(it.b) * p.T + it.k0;
     float* dvg = p.dv + row0 * p.ld_d + it.h * D;
     float* dkg = p.dk + row0 * p.ld_d + it.h * D;
 #pragma unroll
-    for (int k = 0; k < BK * 16 / NELEM; ++k) {
+    for (int k = 0; k < BK * NCH / NELEM; ++k) {
         const int i = tid + k * NELEM;
-        const int r = i >> 4;
-        const int c4 = i & 15;
+        const int r = i / NCH;
+        const int c4 = i % NCH;
         if (it.k0 + r < p.T) {
-            const float4 v = stg_v[r * 16 + (c4 ^ (r & 15))];
-            const float4 g = stg_k[r * 16 + (c4 ^ (r & 15))];
+            const float4 v = stg_v[r * NCH + (c4 ^ (r & (NCH - 1)))];
+            const float4 g = stg_k[r * NCH + (c4 ^ (r & (NCH - 1)))];
             *reinterpret_cast<float4*>(dvg + r * p.ld_d + c4 * 4) = v;
             *reinterpret_cast<float4*>(dkg + r * p.ld_d + c4 * 4) = g;
         }
@@ -370,8 +405,8 @@ __device__ __forceinline__ bool store_dkv(const Params& p, Smem& sm, uint32_t tm
 
 // DET: the deterministic dQ mode (slices in p.dq_part instead of reductions into dq).
 // V8: q, k, v, dout rows start on 32-byte boundaries (256-bit row loads).
-template <bool DET, bool V8>
-__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
+template <bool DET, bool V8, int D>
+__device__ __forceinline__ void bwd_body(const Params& p) {
     // Launched behind attn_bwd_rowdot, whose outputs (D, the zeroed dq) only
     // the loader warps touch: they wait for it; the elementwise warps stage
     // the first item's K / V meanwhile.  Those reads need no wait: rowdot
@@ -379,7 +414,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     // grid before rowdot has finished by now.
     pdl_launch();
     extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
     const int c = static_cast<int>(blockIdx.x);
     const int G = static_cast<int>(gridDim.x);
@@ -425,7 +460,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         Cursor cl, cq;  // tile to load, tile whose dQ is added
         cl.start(p, c, G);
         cq.start(p, c, G);
-        tc::Rows2<BQ, NLOAD> x;
+        tc::Rows2<BQ, NLOAD, D> x;
         float lse_t = 0.f, ds_t = 0.f;
         auto prefetch = [&]() {
             const Item it = make_item(p, cl.w);
@@ -473,7 +508,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 const long hd = static_cast<long>(p.H) * D;
                 float* dqg = DET ? p.dq_part + (static_cast<long>(it.k0 / BK) * p.B + it.b) * p.T * hd + it.h * D
                                  : p.dq + static_cast<long>(it.b) * p.T * p.ld_d + it.h * D;
-                dq_epilogue<DET>(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg, DET ? hd : p.ld_d,
+                dq_epilogue<DET, D>(p, tm, m & 1, qd, lane, (cq.it0 + cq.n) * BQ, dqg, DET ? hd : p.ld_d,
                             &sm.dq_free[m & 1]);
                 cq.next(p, c, G);
             }
@@ -503,7 +538,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                     }
                     if (kv_ok && mbar_test_wait(&sm.full[ns % STAGES], (ns / STAGES) & 1)) {
                         tc_fence_after();
-                        issue_sdp(d, tm, ns % STAGES, ns & 1);
+                        issue_sdp<D>(d, tm, ns % STAGES, ns & 1);
                         mma_commit(&sm.bar_s[ns & 1]);
                         ++ns;
                         cs.next(p, c, G);
@@ -513,9 +548,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
                 if (ng < ns && mbar_test_wait(&sm.pds[ng & 1], (ng >> 1) & 1) &&
                     (ng < 2 || mbar_test_wait(&sm.dq_free[ng & 1], ((ng - 2) >> 1) & 1))) {
                     tc_fence_after();
-                    issue_dq(d, tm, ng & 1);
+                    issue_dq<D>(d, tm, ng & 1);
                     if (cg.n == cg.n_it - 1) mma_commit(&sm.kv_free);
-                    issue_dkv(d, tm, ng % STAGES, ng & 1, cg.n == 0);
+                    issue_dkv<D>(d, tm, ng % STAGES, ng & 1, cg.n == 0);
                     mma_commit(&sm.bar_d[ng & 1]);  // one commit: back-to-back commits stall the MMA pipe
                     ++ng;
                     cg.next(p, c, G);
@@ -547,7 +582,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
         Item it = make_item(p, w);
         {
             const long base = static_cast<long>(it.b) * p.T;
-            tc::stage_rows2<BK, NELEM, V8>(sm.kh, sm.kl, p.k + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.vh, sm.vl,
+            tc::stage_rows2<BK, NELEM, V8, D>(sm.kh, sm.kl, p.k + base * p.ld_qkv + it.h * D, p.ld_qkv, sm.vh, sm.vl,
                                        p.v + base * p.ld_qkv + it.h * D, p.ld_qkv, it.k0, p.T, tid);
         }
         fence_async_smem();
@@ -646,7 +681,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
             if (has_next) {
                 nx = make_item(p, wn);
                 const long base = static_cast<long>(nx.b) * p.T;
-                tc::Rows2<BK, NELEM> kv;
+                tc::Rows2<BK, NELEM, D> kv;
                 kv.template load<V8>(p.k + base * p.ld_qkv + nx.h * D, p.ld_qkv, p.v + base * p.ld_qkv + nx.h * D,
                                      p.ld_qkv, nx.k0, p.T, tid);
                 if (!mbar_wait_warp(&sm.kv_free, r & 1, p.wait_ns)) {
@@ -678,9 +713,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
     if (warp == 0) tmem_dealloc(tm, TMEM_COLS);
 }
 
+template <bool DET, bool V8>
+__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc64(const Params p) {
+    bwd_body<DET, V8, 64>(p);
+}
+template <bool DET, bool V8>
+__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_tc32(const Params p) {
+    bwd_body<DET, V8, 32>(p);
+}
+
 }  // namespace
 
-bool bwd_tc_supported(const BwdArgs& a) { return a.d == 64; }
+bool bwd_tc_supported(const BwdArgs& a) { return a.d == 64 || a.d == 32; }
 
 cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream_t stream, int* launches) {
     cudaError_t e = launch_bwd_prep(a, num_sms, stream, launches);
@@ -712,7 +756,8 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     const long n_work = static_cast<long>(p.n_ktiles) * a.B * a.H;
     if (n_work <= 0 || n_work > INT32_MAX) return cudaErrorInvalidValue;
     p.n_work = static_cast<int>(n_work);
-    const size_t smem = sizeof(Smem) + 1024;
+    const bool d32 = a.d == 32;
+    const size_t smem = (d32 ? sizeof(Smem<32>) : sizeof(Smem<64>)) + 1024;
     int dev = 0;
     e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -721,9 +766,11 @@ cudaError_t launch_bwd_tc(const BwdArgs& a, int num_sms, int* status, cudaStream
     auto a32 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 31) == 0; };
     const bool v8 = a32(a.q) && a32(a.k) && a32(a.v) && a32(a.dout) && a.ld_qkv % 8 == 0 && a.ld_o % 8 == 0;
     static std::atomic<uint64_t> attr_done{0};  // one bit per device and variant: the attribute is per device
-    const uint64_t bit = 1ull << ((4 * dev + (p.dq_part ? 2 : 0) + (v8 ? 1 : 0)) & 63);
-    auto kernel = p.dq_part ? (v8 ? attn_bwd_tc64<true, true> : attn_bwd_tc64<true, false>)
-                            : (v8 ? attn_bwd_tc64<false, true> : attn_bwd_tc64<false, false>);
+    const uint64_t bit = 1ull << ((8 * dev + (d32 ? 4 : 0) + (p.dq_part ? 2 : 0) + (v8 ? 1 : 0)) & 63);
+    auto kernel = d32 ? (p.dq_part ? (v8 ? attn_bwd_tc32<true, true> : attn_bwd_tc32<true, false>)
+                                   : (v8 ? attn_bwd_tc32<false, true> : attn_bwd_tc32<false, false>))
+                      : (p.dq_part ? (v8 ? attn_bwd_tc64<true, true> : attn_bwd_tc64<true, false>)
+                                   : (v8 ? attn_bwd_tc64<false, true> : attn_bwd_tc64<false, false>));
     if (!(attr_done.load(std::memory_order_relaxed) & bit)) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;

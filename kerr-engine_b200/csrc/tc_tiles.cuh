@@ -48,12 +48,21 @@ __device__ __forceinline__ void stage_rows(uint8_t* hi, uint8_t* lo, const float
 
 // Two tiles of the same shape (e.g. Q and dO, or K and V) held in registers
 // between their loads and their conversion, so the loads can be issued early
-// and the shared-memory stores made once the destination is free.
-template <int R, int NTH>
+// and the shared-memory stores made once the destination is free.  Rows of
+// W floats (64: bf16 rows of 128 bytes, 128B-swizzled; 32: rows of 64 bytes,
+// 64B-swizzled); thread t handles (row, 8-float chunk) items t, t + NTH, ...
+template <int R, int NTH, int W = 64>
 struct Rows2 {
-    static_assert((R * 8) % NTH == 0, "tile items must divide evenly");
-    static constexpr int ITEMS = R * 8 / NTH;
+    static_assert(W == 64 || W == 32, "rows of 64 or 32 floats");
+    static constexpr int CH = W / 8;  // 8-float chunks per row
+    static_assert((R * CH) % NTH == 0, "tile items must divide evenly");
+    static constexpr int ITEMS = R * CH / NTH;
     float4 a[2][ITEMS], b[2][ITEMS];
+
+    __device__ __forceinline__ static uint32_t offset(int r, int ch) {
+        if constexpr (W == 64) return sm100::sw128(r, ch);
+        else return sm100::sw64(r, ch);
+    }
 
     // V8: every row start is 32-byte aligned (base pointers and row strides),
     // so each 8-float chunk is one 256-bit load instead of two 128-bit ones.
@@ -63,8 +72,8 @@ struct Rows2 {
 #pragma unroll
         for (int it = 0; it < ITEMS; ++it) {
             const int i = t + it * NTH;
-            const int r = i >> 3;
-            const int ch = i & 7;
+            const int r = i / CH;
+            const int ch = i % CH;
             a[0][it] = make_float4(0.f, 0.f, 0.f, 0.f);
             b[0][it] = a[0][it];
             a[1][it] = a[0][it];
@@ -95,14 +104,14 @@ struct Rows2 {
 #pragma unroll
             for (int it = 0; it < ITEMS; ++it) {
                 const int i = t + it * NTH;
-                const int r = i >> 3;
-                const int ch = i & 7;
+                const int r = i / CH;
+                const int ch = i % CH;
                 uint4 h, l;
                 sm100::split2(a[u][it].x, a[u][it].y, h.x, l.x);
                 sm100::split2(a[u][it].z, a[u][it].w, h.y, l.y);
                 sm100::split2(b[u][it].x, b[u][it].y, h.z, l.z);
                 sm100::split2(b[u][it].z, b[u][it].w, h.w, l.w);
-                const uint32_t off = sm100::sw128(r, ch);
+                const uint32_t off = offset(r, ch);
                 *reinterpret_cast<uint4*>(hi + off) = h;
                 *reinterpret_cast<uint4*>(lo + off) = l;
             }
@@ -112,10 +121,10 @@ struct Rows2 {
 
 // Two tiles of the same shape in one pass: all loads of both are in flight
 // before the first conversion.
-template <int R, int NTH, bool V8 = false>
+template <int R, int NTH, bool V8 = false, int W = 64>
 __device__ __forceinline__ void stage_rows2(uint8_t* hi0, uint8_t* lo0, const float* g0, long ld0, uint8_t* hi1,
                                             uint8_t* lo1, const float* g1, long ld1, int row0, int T, int t) {
-    Rows2<R, NTH> x;
+    Rows2<R, NTH, W> x;
     x.template load<V8>(g0, ld0, g1, ld1, row0, T, t);
     x.store(hi0, lo0, hi1, lo1, t);
 }

@@ -10,8 +10,8 @@ run as two C-ABI calls with every intermediate on the device, and on the
 oracle's CPU restatements of each operation (the same composition as the
 loss-curve harness, tests/train_stack.py).  Tolerances: h_out within 1e-4
 and every gradient within 1e-3 norm-wise relative error (the attention
-parity tolerances), at head_dim 64 (tensor-core kernels) and head_dim 32
-(tensor-core forward, FFMA backward), with and without the FFN.
+parity tolerances), on the tensor-core path (head_dim 64) and the FFMA path
+(head_dim 32 at these sizes), with and without the FFN.
 """
 import numpy as np
 import pytest
@@ -67,8 +67,8 @@ NAMES = {"ln1_w": "ln1_w", "ln1_b": "ln1_b", "w_attn": "wa", "b_attn": "ba", "w_
          "ln2_w": "ln2_w", "ln2_b": "ln2_b", "gamma_raw": "gamma_raw", "omega": "omega", "alpha_beta": "alpha_beta"}
 
 
-# (B, T, C, H): head_dim 64 (tensor cores, ragged T) and head_dim 32 (tensor-core
-# forward, FFMA backward).
+# (B, T, C, H): head_dim 64 (tensor cores, ragged T) and head_dim 32 (FFMA at
+# this size).
 @pytest.mark.parametrize("B,T,C,H", [(2, 130, 128, 2), (2, 64, 128, 4)])
 @pytest.mark.parametrize("ffn", [False, True])
 def test_block_matches_oracle(oracle_lib, B, T, C, H, ffn):

@@ -44,9 +44,10 @@ def run(ctx, qkv, dout, H, causal):
 
 
 # (B, T, H, d, path): the 768-dim headline's head shape on the tensor cores
-# (ragged T: the last key tile partly past T), two key tiles and more, and the
-# FFMA kernels at head_dim 32 and 64.
-CASES = [(2, 300, 2, 64, "tensor"), (1, 513, 3, 64, "tensor"), (2, 200, 2, 32, "ffma"), (1, 130, 2, 64, "ffma")]
+# (ragged T: the last key tile partly past T), two key tiles and more, head_dim
+# 32 on the tensor cores, and the FFMA kernels at head_dim 32 and 64.
+CASES = [(2, 300, 2, 64, "tensor"), (1, 513, 3, 64, "tensor"), (2, 200, 2, 32, "tensor"), (2, 200, 2, 32, "ffma"),
+         (1, 130, 2, 64, "ffma")]
 
 
 @pytest.mark.parametrize("B,T,H,d,path", CASES)

@@ -34,8 +34,8 @@ STEPS = 50
 LR = 0.03
 
 
-# (B, T, C, H): the 128-dim model's shapes (B=4, T=64, head_dim 32: tensor-core
-# forward, FFMA backward) and a head_dim 64 stack (the tensor-core kernels).
+# (B, T, C, H): the 128-dim model's shapes (B=4, T=64, head_dim 32: the FFMA
+# kernels at this size) and a head_dim 64 stack (the tensor-core kernels).
 @pytest.mark.parametrize("B,T,C,H", [(4, 64, 128, 4), (2, 128, 256, 4)])
 def test_loss_curve_matches_oracle(oracle_lib, B, T, C, H):
     blocks, h0, target = train_stack.init(B, T, C, H, 4, seed=42)
