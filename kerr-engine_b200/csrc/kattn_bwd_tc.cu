@@ -1,5 +1,7 @@
 // Causal self-attention backward on the 5th-generation tensor cores
-// (sm_100a), head_dim 64.  Replaces ComputeBackend::attention_backward
+// (sm_100a), head_dim 64 and 32 (one kernel body, templated on the head
+// dimension D; the notes below give the D = 64 sizes).  Replaces
+// ComputeBackend::attention_backward
 // (src/backend.rs:223-231; CPU src/backward.rs:464-514; WGSL
 // attn_backward_scores / attn_backward_dkv), recomputing the probabilities
 // from the forward's log-sum-exp instead of reading a cached [H][T][T] P.

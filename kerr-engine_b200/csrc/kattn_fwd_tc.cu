@@ -1,5 +1,7 @@
 // Causal self-attention forward on the 5th-generation tensor cores (sm_100a),
-// head_dim 64.  Replaces the scalar head loop of src/pipeline.rs:305-347.
+// head_dim 64 and 32 (one kernel body, templated on the head dimension D; the
+// notes below give the D = 64 sizes).  Replaces the scalar head loop of
+// src/pipeline.rs:305-347.
 //
 // Numerics: every f32 operand x is split into bf16 hi = bf16(x) and
 // lo = bf16(x - hi); each product A*B is formed as hi*hi + hi*lo + lo*hi with

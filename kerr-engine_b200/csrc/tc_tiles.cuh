@@ -6,46 +6,6 @@
 namespace kattn {
 namespace tc {
 
-// Rows [row0, row0 + R) of one 64-column head slice (row stride ld floats)
-// -> bf16 hi / lo tiles of R rows x 128 bytes in the 128B-swizzled layout,
-// multiplied by `mul`, zero beyond row T.  NTH threads cooperate; thread `t`
-// handles (row, 8-float chunk) items t, t + NTH, ...  All loads are issued
-// before the first conversion so they are in flight together.
-template <int R, int NTH>
-__device__ __forceinline__ void stage_rows(uint8_t* hi, uint8_t* lo, const float* g, long ld, int row0, int T,
-                                           float mul, int t) {
-    static_assert((R * 8) % NTH == 0, "tile items must divide evenly");
-    constexpr int ITEMS = R * 8 / NTH;
-    float4 a[ITEMS], b[ITEMS];
-#pragma unroll
-    for (int it = 0; it < ITEMS; ++it) {
-        const int i = t + it * NTH;
-        const int r = i >> 3;
-        const int ch = i & 7;
-        a[it] = make_float4(0.f, 0.f, 0.f, 0.f);
-        b[it] = a[it];
-        if (row0 + r < T) {
-            const float4* s = reinterpret_cast<const float4*>(g + static_cast<long>(row0 + r) * ld + ch * 8);
-            a[it] = __ldg(s);
-            b[it] = __ldg(s + 1);
-        }
-    }
-#pragma unroll
-    for (int it = 0; it < ITEMS; ++it) {
-        const int i = t + it * NTH;
-        const int r = i >> 3;
-        const int ch = i & 7;
-        uint4 h, l;
-        sm100::split2(a[it].x * mul, a[it].y * mul, h.x, l.x);
-        sm100::split2(a[it].z * mul, a[it].w * mul, h.y, l.y);
-        sm100::split2(b[it].x * mul, b[it].y * mul, h.z, l.z);
-        sm100::split2(b[it].z * mul, b[it].w * mul, h.w, l.w);
-        const uint32_t off = sm100::sw128(r, ch);
-        *reinterpret_cast<uint4*>(hi + off) = h;
-        *reinterpret_cast<uint4*>(lo + off) = l;
-    }
-}
-
 // Two tiles of the same shape (e.g. Q and dO, or K and V) held in registers
 // between their loads and their conversion, so the loads can be issued early
 // and the shared-memory stores made once the destination is free.  Rows of
@@ -191,41 +151,6 @@ struct RawTile32 {
             const uint32_t off = sm100::sw64(r, c4 >> 1) + (c4 & 1) * 8;
             *reinterpret_cast<uint2*>(tile + off) = h;
             *reinterpret_cast<uint2*>(tile + R * 64 + off) = l;
-        }
-    }
-};
-
-// A raw f32 tile of R rows x C floats (row-major, C*4 bytes per row, as a
-// TMA box lands it) whose columns run along an operand's M or N dimension and
-// whose rows run along K -> the same bytes rewritten as bf16 hi (first
-// R*C*2 bytes) and lo halves in the MN-major 128B-swizzled UMMA layout: C/64
-// atoms of R rows x 128 bytes, atom a holding columns 64a..64a+63, atoms
-// R*128 bytes apart (the descriptor's leading-byte offset).  Same read /
-// barrier / write protocol as RawTile.
-template <int R, int C, int NTH>
-struct RawTileMN {
-    static_assert(C % 64 == 0 && (R * C / 4) % NTH == 0, "tile items must divide evenly");
-    static constexpr int F4_PER_ROW = C / 4;
-    static constexpr int ITEMS = R * C / 4 / NTH;
-    float4 a[ITEMS];
-
-    __device__ __forceinline__ void read(const uint8_t* tile, int t) {
-#pragma unroll
-        for (int it = 0; it < ITEMS; ++it) a[it] = reinterpret_cast<const float4*>(tile)[t + it * NTH];
-    }
-
-    __device__ __forceinline__ void write(uint8_t* tile, int t) const {
-#pragma unroll
-        for (int it = 0; it < ITEMS; ++it) {
-            const int f = t + it * NTH;
-            const int r = f / F4_PER_ROW;
-            const int col = 4 * (f - r * F4_PER_ROW);
-            uint2 h, l;
-            sm100::split2(a[it].x, a[it].y, h.x, l.x);
-            sm100::split2(a[it].z, a[it].w, h.y, l.y);
-            const uint32_t off = (col >> 6) * (R * 128) + sm100::sw128(r, (col & 63) >> 3) + ((col >> 2) & 1) * 8;
-            *reinterpret_cast<uint2*>(tile + off) = h;
-            *reinterpret_cast<uint2*>(tile + (C / 64) * R * 128 + off) = l;
         }
     }
 };
